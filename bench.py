@@ -1,0 +1,422 @@
+"""Throughput of the fused score -> 2:4 mask -> pack pass on B200.
+
+Workload (default): a 7B-class decoder - 32 layers of
+q/k/v/o (4096x4096, 1024x4096 x2, 4096x4096), gate/up (14336x4096) and down
+(4096x14336) BF16 matrices, 6,979,321,856 prunable parameters - each matrix
+with 64 BF16 gradient samples ~ N(0, 1e-3^2), weights ~ N(0, 0.02^2); Fisher EMA
+(alpha 0.01, beta 0.99), OBD scoring (lambda 0.01), optimal C(4,2) 2:4 mask,
+proportional redistribution, FP32 weights + packed mask bytes written.
+
+One step = the whole 32-layer pass (224 fused launches).  Gradients for all 32
+layers do not fit in HBM (~0.9 TB), so two resident random-init layer sets (A,
+B; 29 GB each) alternate layer by layer; every launch streams 0.5-7.6 GB, far
+above the 126 MB L2, so no L2 flush is needed between launches.  Each rank runs
+the same per-rank job (weak scaling): the path has no cross-rank data
+dependency, only the timing barrier and max-over-ranks reduction.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tensorbit-core_b200"))
+
+LAYER = [("q_proj", 4096, 4096), ("k_proj", 1024, 4096), ("v_proj", 1024, 4096),
+         ("o_proj", 4096, 4096), ("gate_proj", 14336, 4096), ("up_proj", 14336, 4096),
+         ("down_proj", 4096, 14336)]
+LAYERS = 32
+S = 64
+PARAMS_PER_LAYER = sum(r * c for _, r, c in LAYER)          # 218,103,808
+PARAMS_PER_STEP = PARAMS_PER_LAYER * LAYERS                   # 6,979,321,856
+BYTES_PER_PARAM = 2 + 2 * S + 4 + 0.25                        # W bf16 + 64 grads bf16 + W' f32 + mask
+METRIC = "2:4 score+mask+pack Gparams/s at 1/2/4/8 B200; % HBM roofline; OBS TFLOP/s"
+WORKLOAD = "7B-class decoder (32 layers, hidden 4096, inter 14336, 32q/8kv heads x128), 64 BF16 grads/tensor, OBD, optimal 2:4 + proportional redistribution"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi samples (200 ms) of this rank's GPU while the timed region runs."""
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, uuid: str, index: str):
+        self.uuid, self.index = uuid.lower(), str(index)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            return None
+        rows = [[x.strip() for x in line.split(",")] for line in out.strip().splitlines()]
+        rows = [r for r in rows if len(r) >= 9]
+        mine = [r for r in rows if self.uuid and r[1].lower().endswith(self.uuid)]
+        if not mine:
+            mine = [r for r in rows if r[0] == self.index]
+        sm, mx, power, reasons = [], [], [], set()
+        for r in mine:
+            try:
+                sm.append(float(r[2]))
+                mx.append(float(r[3]))
+                power.append(float(r[4]))
+            except ValueError:
+                continue
+            for nm, v in zip(self.NAMES, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "power_w_max": max(power),
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# roofline denominators and ncu traffic
+# ---------------------------------------------------------------------------
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic_per_param():
+    """dram bytes read+written per parameter of the fused BF16 2:4 kernel from the
+    committed ncu summary (profiles/), or None when no capture is committed."""
+    p = os.path.join(ROOT, "profiles", "fused_vec_bf16_2of4_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"dram_bytes_per_param\s*=\s*([0-9.]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def make_layer_set(torch, gen, dev):
+    tensors = []
+    for name, r, c in LAYER:
+        n = r * c
+        w = (torch.randn(n, device=dev, generator=gen, dtype=torch.bfloat16) * 0.02)
+        g = (torch.randn(S, n, device=dev, generator=gen, dtype=torch.bfloat16) * 1e-3)
+        w_out = torch.empty(n, device=dev, dtype=torch.float32)
+        mask = torch.empty(n // 4, device=dev, dtype=torch.uint8)
+        tensors.append((name, n, w, g, w_out, mask))
+    return tensors
+
+
+def prune_args_for(tb, n, w_ptr, g_ptr, w_out_ptr, mask_ptr, g_stride=0):
+    return tb.prune_args(weights=w_ptr, w_dtype=tb.BF16, grads=g_ptr, g_dtype=tb.BF16, S=S, N=n,
+                         g_stride=g_stride, alpha=0.01, beta=0.99, damping=0.01, mode="obd",
+                         use_fisher=True, n=2, m=4, strategy="optimal", redist="proportional",
+                         w_out=w_out_ptr, mask_out=mask_ptr)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import tbabi as tb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    tb.lib()
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sets = [make_layer_set(torch, gen, dev), make_layer_set(torch, gen, dev)]
+    plan = []
+    for layer in range(LAYERS):
+        for (name, n, w, g, w_out, mask) in sets[layer % 2]:
+            plan.append((n, prune_args_for(tb, n, w.data_ptr(), g.data_ptr(), w_out.data_ptr(), mask.data_ptr())))
+    torch.cuda.synchronize()
+
+    def step(events=None):
+        for i, (n, a) in enumerate(plan):
+            if events is not None:
+                events[i][0].record(stream)
+            rc = tb.lib().tb_score_mask_pack(C.byref(a), sptr)
+            if rc:
+                tb.check(rc)
+            if events is not None:
+                events[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in plan]
+              for _ in range(args.steps)]
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = vis.split(",")[local] if vis and len(vis.split(",")) > local else str(local)
+    clocks = Clocks(str(getattr(torch.cuda.get_device_properties(dev), "uuid", "")), phys)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for k in range(args.steps):
+        step(events[k])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+    kernel_ms = sum(a.elapsed_time(b) for ev in events for a, b in ev)
+    launches = args.steps * len(plan)
+    t = torch.tensor([elapsed_ms, kernel_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, kernel_ms = t.tolist()
+
+    params_total = PARAMS_PER_STEP * args.steps * world
+    value = params_total / (elapsed_ms / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+    per_launch_bytes = PARAMS_PER_STEP * BYTES_PER_PARAM / len(plan)
+    achieved = per_launch_bytes / (kernel_ms / launches / 1e3) / 1e9
+    traffic_pp = ncu_traffic_per_param()
+
+    # ---- end to end through the host-buffer entry point --------------------
+    e2e = None
+    del sets
+    torch.cuda.empty_cache()
+    if not args.no_e2e:
+        e2e = run_e2e(torch, tb, dev, gen, args, world, rank, local)
+
+    # ---- CPU baseline (rank 0, single GPU only) ----------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(torch, dev, threads=os.cpu_count() or 1, seconds=4.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "Gparams/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(elapsed_ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded torch Philox; random-init weights and gradients of the 7B shapes)",
+            "config": {"workload": WORKLOAD, "params_per_rank_step": PARAMS_PER_STEP, "grad_samples": S,
+                       "weights": "bf16", "grads": "bf16", "outputs": "fp32 weights + u8 mask",
+                       "layer_sets_resident": 2,
+                       "l2": "no flush: every launch streams 0.5-7.6 GB >> 126 MB L2",
+                       "parallelism": f"weak: {world} rank(s), each its own 32-layer pass, no data-path collective"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_param": BYTES_PER_PARAM,
+                         "traffic": (round(traffic_pp * PARAMS_PER_STEP / len(plan)) if traffic_pp else None),
+                         "traffic_per_param": traffic_pp,
+                         "kernel": "fused_vec_kernel<BF16,BF16,M=4>",
+                         "kernel_ms_total": round(kernel_ms, 3)},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def run_e2e(torch, tb, dev, gen, args, world, rank, local):
+    """Same metric through tb_score_mask_pack_host with pinned host buffers: every
+    step copies that step's inputs host->device and the results back inside the
+    timed region.  One step = one decoder layer (7 matrices, 218,103,808 params);
+    the 7B pass is 32 identical layers."""
+    import torch.distributed as dist
+    nmax = max(r * c for _, r, c in LAYER)
+    hw = torch.empty(nmax, dtype=torch.bfloat16, pin_memory=True)
+    hg = torch.empty(S, nmax, dtype=torch.bfloat16, pin_memory=True)
+    hwo = torch.empty(nmax, dtype=torch.float32, pin_memory=True)
+    hm = torch.empty(nmax // 4, dtype=torch.uint8, pin_memory=True)
+    hw.copy_((torch.randn(nmax, device=dev, generator=gen) * 0.02).to(torch.bfloat16))
+    for s0 in range(0, S, 8):
+        hg[s0:s0 + 8].copy_((torch.randn(8, nmax, device=dev, generator=gen) * 1e-3).to(torch.bfloat16))
+    torch.cuda.synchronize()
+    calls = []
+    h2d = d2h = 0
+    for name, r, c in LAYER:
+        n = r * c
+        # All matrices read the leading n columns of the shared pinned buffers.
+        calls.append(prune_args_for(tb, n, hw.data_ptr(), hg.data_ptr(), hwo.data_ptr(), hm.data_ptr(), g_stride=nmax))
+        h2d += n * 2 + S * n * 2
+        d2h += n * 4 + n // 4
+
+    def layer():
+        for a in calls:
+            tb.check(tb.lib().tb_score_mask_pack_host(C.byref(a)))
+
+    layer()  # warm-up: staging buffers, streams
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        layer()
+    el = time.perf_counter() - t0
+    t = torch.tensor([el], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    el = t.item()
+    value = PARAMS_PER_LAYER * args.e2e_steps * world / el / 1e9
+    return {"value": round(value, 4), "unit": "Gparams/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": args.e2e_steps, "step": "one decoder layer (7 matrices) via tb_score_mask_pack_host, pinned host memory",
+            "s_per_step": round(el / args.e2e_steps, 4)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own CPU code (oracle/_ref) or the port
+# ---------------------------------------------------------------------------
+def cpu_sample(torch, dev):
+    import numpy as np
+    n = 4096 * 4096
+    gen = torch.Generator(device=dev).manual_seed(99)
+    w = (torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16).float().cpu().numpy()
+    g = (torch.randn(S, n, device=dev, generator=gen) * 1e-3).to(torch.bfloat16).float().cpu().numpy()
+    return np.ascontiguousarray(w), np.ascontiguousarray(g), n
+
+
+def cpu_baseline(torch, dev, threads, seconds):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle, ref_available
+    kind = "reference" if ref_available() else "port"
+    w, g, n = cpu_sample(torch, dev)
+    if kind == "reference":
+        o = Oracle("ref")
+        run = lambda: o.parallel_pass(w.copy(), g, mode="obd", n=2, m=4, strategy="optimal",
+                                      redist="proportional", threads=threads)
+    else:
+        o = Oracle("port")
+        run = lambda: (o.pipeline(w, g, mode="obd", strategy="optimal", redist="proportional")[0], None)
+        threads = 1
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        rc, _ = run()
+        assert rc == 0, rc
+        done += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    el = time.perf_counter() - t0
+    return {"value": round(n * done / el / 1e9, 5), "unit": "Gparams/s", "cores": threads, "kind": kind,
+            "sample": f"one 4096x4096 matrix (16,777,216 params) with 64 FP32-widened BF16 gradient samples, "
+                      f"OBD + optimal 2:4 + proportional, {threads} contiguous shards on {threads} threads, "
+                      f"{done} pass(es) in {el:.1f} s"}
+
+
+def run_reference(args):
+    """Reference arm: the reference's CPU implementation of this path on the
+    host cores (rank 0 only), same metric and unit."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle, ref_available
+    kind = "reference" if ref_available() else "port"
+    threads = os.cpu_count() or 1
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    if dev.type == "cuda":
+        w, g, n = cpu_sample(torch, dev)
+    else:
+        import numpy as np
+        n = 4096 * 4096
+        rng = np.random.default_rng(99)
+        w = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.02))
+        g = (rng.standard_normal((S, n), dtype=np.float32) * np.float32(1e-3))
+    o = Oracle("ref" if kind == "reference" else "port")
+
+    def one():
+        if kind == "reference":
+            rc, _ = o.parallel_pass(w.copy(), g, mode="obd", n=2, m=4, strategy="optimal",
+                                    redist="proportional", threads=threads)
+        else:
+            rc = o.pipeline(w, g, mode="obd", strategy="optimal", redist="proportional")[0]
+        assert rc == 0
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    el = time.perf_counter() - t0
+    value = n * args.steps / el / 1e9
+    cores = threads if kind == "reference" else 1
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "Gparams/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_per_step": "one 4096x4096 matrix, 64 FP32-widened BF16 gradient samples"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "Gparams/s", "cores": cores, "kind": kind,
+                         "sample": f"per step one 4096x4096 matrix (16,777,216 params) x 64 samples, {cores} shard(s) on {cores} thread(s)"},
+        "e2e": {"value": round(value, 5), "unit": "Gparams/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,165 @@
+/* tb_kernels.h - C ABI of the B200 (sm_100a) pruning kernels.
+ *
+ * Drop-in replacement for the reference's kernel boundary:
+ *   include/tensorbit/core/kernels.hpp:24-124   (7 C++ launch_* declarations)
+ *   src/kernels.cu:338-435                      (their CUDA launchers)
+ *   src/kernels_stubs.cpp:13-63                 (their CPU-build no-op stubs)
+ * plus the host-side loops of the pruners that the reference never moved to a
+ * device (include/tensorbit/core/ehap.hpp, coring.hpp), so that one call can do
+ * the whole per-tensor score -> N:M mask -> pack pass.
+ *
+ * Conventions (all entry points):
+ *   - extern "C", plain pointers and sizes; no C++ or torch types.
+ *   - Every function returns an int status: TB_OK (0) or a negative TB_ERR_*.
+ *     Nothing aborts the process (the reference aborts via CUDA_CHECK,
+ *     common.hpp:38-49); the text of the last error is in tb_last_error().
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy default
+ *     stream.  Launches are asynchronous; results are ready after the stream
+ *     synchronises.  Size/argument checks happen on the host before launch.
+ *   - Device pointers are owned by the caller unless stated otherwise.
+ *   - Floating-point results reproduce the reference's CPU expression trees
+ *     bit for bit (IEEE round-to-nearest, no fused multiply-add); masks
+ *     reproduce the reference CPU path's selection, ties included.
+ *   - Without a CUDA device every compute call returns TB_ERR_NO_DEVICE; there
+ *     is no CPU fallback.
+ */
+#ifndef TB_KERNELS_H
+#define TB_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TB_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+    TB_OK              = 0,
+    TB_ERR_SHAPE       = -1, /* sizes disagree or numel % M != 0 (EHAPError/CORINGError::kShapeMismatch) */
+    TB_ERR_ZERO_SIZE   = -2, /* empty tensor (kZeroSizeTensor)                                        */
+    TB_ERR_CONFIG      = -3, /* bad N:M (CORINGError::kInvalidNMConfig) or sparsity (EHAPError::kInvalidConfig) */
+    TB_ERR_CUDA        = -4, /* CUDA runtime error; see tb_last_error()                               */
+    TB_ERR_TIMEOUT     = -5, /* a bounded device-side wait gave up                                    */
+    TB_ERR_UNSUPPORTED = -6, /* combination not implemented (e.g. M > 8: masks are one byte per group) */
+    TB_ERR_ARG         = -7, /* null pointer, bad enum value, misaligned pointer                      */
+    TB_ERR_NO_DEVICE   = -8, /* no CUDA device visible                                                */
+    TB_ERR_CAPACITY    = -9  /* request exceeds a fixed capacity of the entry point                   */
+};
+
+/* ---- enumerations (values equal the reference's enum values) ----------- */
+enum { TB_F32 = 0, TB_F16 = 1, TB_BF16 = 2 };                 /* TBHeader::precision codes, serialization.hpp:48 */
+enum { TB_IMP_OBD = 0, TB_IMP_OBS = 1, TB_IMP_NORMALIZED = 2 }; /* ImportanceMode, ehap.hpp:49-53 */
+enum { TB_MASK_TOPN = 0, TB_MASK_OPTIMAL = 1, TB_MASK_ITERATIVE = 2 }; /* MaskStrategy, coring.hpp:37-41 */
+enum { TB_REDIST_NONE = 0, TB_REDIST_PROPORTIONAL = 1, TB_REDIST_UNIFORM = 2 }; /* RedistMode, coring.hpp:43-47 */
+
+/* ---- library / device plumbing ----------------------------------------- */
+int         tb_abi_version(void);
+const char* tb_last_error(void);               /* thread-local text of the last failure */
+int         tb_device_count(int* count);
+int         tb_set_device(int device);
+int         tb_malloc(void** ptr, size_t bytes);  /* device memory for TensorDense (tensor.hpp:97-104) */
+int         tb_free(void* ptr);
+int         tb_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int         tb_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int         tb_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+int         tb_memset(void* dst, int value, size_t bytes, void* stream);
+int         tb_stream_sync(void* stream);
+/* Builds the per-device tie tables needed by TB_MASK_TOPN / TB_MASK_ITERATIVE
+ * for this (n, m) on the current device.  Calls that need them build them on
+ * first use; call this first if the stream will later be captured. */
+int         tb_prepare_nm(int n, int m);
+
+/* ---- legacy launchers: kernels.hpp:24-124, same arguments -------------- */
+/* F[i] = sum_b g[b*N+i]^2 (kernels.hpp:24-28; not called by the reference pruners). */
+int tb_fisher_diagonal(const float* gradients, float* fisher_diag, size_t B, size_t N, void* stream);
+/* F[i] = F[i] + (alpha*g[i])*g[i] (kernels.hpp:38-42).  Composed with
+ * tb_fisher_beta_decay this is bit-identical to the reference's host EMA step
+ * F = beta*F + (alpha*(1-beta))*g*g (ehap.hpp:194-197). */
+int tb_fisher_accumulate(float* fisher_diag, const float* gradients, size_t N, float alpha, void* stream);
+/* F[i] = beta*F[i] (kernels.hpp:51-54). */
+int tb_fisher_beta_decay(float* fisher_diag, float beta, size_t N, void* stream);
+/* OBD importance s = w*w*(F+damping), or w*w when F is NULL (kernels.hpp:65-70). */
+int tb_ehap_importance(const float* weights, const float* fisher_diag, float* importance, size_t N,
+                       float damping, void* stream);
+/* 2:4 top-N mask, one byte per group (kernels.hpp:85-88). */
+int tb_nm_mask_2_4(const float* importance, uint8_t* mask_out, size_t N, void* stream);
+/* n:m top-N mask, one byte per group (kernels.hpp:101-106); m <= 8. */
+int tb_nm_mask_generic(const float* importance, uint8_t* mask_out, size_t N_elements, int group_n,
+                       int group_m, void* stream);
+/* Zero w[i] where bit (i % m) of mask[i / m] is clear (kernels.hpp:120-124). */
+int tb_apply_mask(float* weights, const uint8_t* mask, size_t N, int group_m, void* stream);
+
+/* ---- stage entry points (the pruners' loops, on the device) ------------ */
+/* One EHAPPruner::accumulate_fisher call (ehap.hpp:148-201) over N gradients of
+ * dtype g_dtype: first_step != 0 gives F = (alpha*g)*g, otherwise
+ * F = beta*F + ((alpha*(1-beta))*g)*g with the reference's float rounding. */
+int tb_fisher_ema_step(float* fisher, const void* gradients, int g_dtype, size_t N, float alpha,
+                       float beta, int first_step, void* stream);
+/* EHAPPruner::compute_importance (ehap.hpp:206-285) for all three modes; F may be
+ * NULL (no Fisher state: s = w*w).  Weights of dtype w_dtype are widened as the
+ * reference's safetensors loader does (src/main.cpp:213-245). */
+int tb_importance(const void* weights, int w_dtype, const float* fisher, float* importance,
+                  size_t N, float damping, int mode, void* stream);
+/* CORINGPruner::generate_nm_mask (coring.hpp:90-165): strategy TB_MASK_*,
+ * `rounds` swap-refine rounds, optional per-group |score| sort (permute_weights).
+ * Writes N/m bytes. */
+int tb_nm_mask(const float* importance, uint8_t* mask_out, size_t N, int n, int m, int strategy,
+               int rounds, int permute, void* stream);
+/* CORINGPruner::redistribute (coring.hpp:228-294) of the weights as they are now. */
+int tb_redistribute(float* weights, const uint8_t* mask, const float* importance, size_t N, int m,
+                    int mode, void* stream);
+
+/* ---- fused score -> mask -> pack pass ------------------------------------ */
+/* One pass over a tensor: Fisher EMA over S gradient samples, importance,
+ * CORING N:M mask, apply, redistribution, and emission of the .tb weight and
+ * mask sections.  Equivalent to the reference sequence
+ *   accumulate_fisher x S -> compute_importance -> CORINGPruner::prune
+ *   -> generate_nm_mask                       (src/main.cpp:375,397-409)
+ * without the EHAP global pre-prune. */
+typedef struct tb_prune_args {
+    uint32_t struct_size;      /* sizeof(tb_prune_args) */
+    /* inputs (device pointers) */
+    const void*  weights;      /* [N] of w_dtype                                         */
+    int32_t      w_dtype;
+    int32_t      g_dtype;
+    const void*  grads;        /* [S, g_stride] of g_dtype, sample-major; NULL iff S == 0 */
+    uint64_t     S;            /* gradient samples                                       */
+    uint64_t     N;            /* elements                                               */
+    uint64_t     g_stride;     /* elements between samples; 0 means N                    */
+    const float* fisher_in;    /* [N] Fisher state after fisher_steps_in steps, or NULL   */
+    uint64_t     fisher_steps_in;
+    /* EHAPConfig subset (ehap.hpp:70-93) */
+    float        alpha;        /* accumulate_fisher's alpha (tb-prune passes 0.01)        */
+    float        beta;         /* ema_decay                                              */
+    float        damping;      /* lambda                                                 */
+    int32_t      importance_mode;
+    int32_t      use_fisher;   /* use_diagonal_fisher                                    */
+    /* CORINGConfig subset (coring.hpp:49-69) */
+    int32_t      nm_n, nm_m;
+    int32_t      mask_strategy;
+    int32_t      iterative_rounds;
+    int32_t      redist_mode;
+    int32_t      permute;
+    /* outputs (device pointers) */
+    float*       w_out;        /* [N] FP32 pruned weights = .tb weight section           */
+    uint8_t*     mask_out;     /* [N/m] packed groups     = .tb mask section             */
+    float*       fisher_out;   /* [N] or NULL                                            */
+    float*       scores_out;   /* [N] or NULL                                            */
+    unsigned long long* near_ties; /* device counter incremented per near-tie group, or NULL */
+} tb_prune_args;
+
+int tb_score_mask_pack(const tb_prune_args* args, void* stream);
+
+/* Same pass with every pointer in args a HOST pointer (pinned memory is
+ * fastest).  The library stages chunks through device buffers it allocates,
+ * overlapping host->device copies, the kernel and device->host copies on
+ * several streams, and returns when the outputs are in host memory. */
+int tb_score_mask_pack_host(const tb_prune_args* args);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TB_KERNELS_H */

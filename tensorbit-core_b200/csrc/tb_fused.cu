@@ -1,0 +1,530 @@
+// Fused score -> N:M mask -> pack pass (stages 1 and 2 of the pruning path).
+//
+// One read of W, the S gradient samples and (optionally) the prior Fisher
+// state; one write of the FP32 pruned weights and the packed mask bytes - the
+// .tb weight and mask sections (serialization.hpp:101-151).  Per element it
+// runs the reference's EMA recurrence over the samples in registers
+// (ehap.hpp:186-200), scores it (ehap.hpp:256-284), and per group selects,
+// applies and redistributes exactly as CORINGPruner::prune (coring.hpp:299-313).
+//
+// Layout in HBM: W [N] (FP32/BF16/F16), G [S][g_stride] sample-major, outputs
+// W' [N] FP32 and mask [N/M] u8.  Each thread owns 16 consecutive elements:
+// per sample a warp reads 32 x 32 B (BF16) contiguous with 16-byte
+// non-L1-allocating loads, so a CTA streams all samples of its 4096-element
+// column slab with every load independent of the FP chain.  The pass is
+// HBM-bound (about 2S+6 bytes per parameter against ~3 FP ops per
+// parameter-sample).
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "tb_device.cuh"
+#include "tb_runtime.h"
+
+namespace tb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kEpt = 16;  // elements per thread in the vector kernel
+
+struct FusedParams {
+    const void* w;
+    const void* g;
+    const float* fin;
+    float* wout;
+    uint8_t* mout;
+    float* fout;
+    float* sout;
+    unsigned long long* ties;
+    const uint8_t* lut;
+    size_t N;        // elements in this launch
+    size_t S;        // samples actually read (0 when the Fisher is off)
+    size_t gstride;  // elements between samples
+    float alpha, beta, contrib, damp;
+    int mode;
+    int have_f;      // a Fisher state exists after this pass
+    int first;       // sample 0 initialises F (no prior state)
+    int use_fin;     // F starts from fin
+    int n, strategy, rounds, redist, permute;
+    int wdt, gdt;    // dtypes (generic kernel)
+};
+
+// --- 16-element vector loads --------------------------------------------------
+template <int DT> struct Vec16;
+template <> struct Vec16<TB_F32> {
+    static constexpr int kWords = 4;  // uint4 per 16 elements
+    __device__ static void decode(const uint4 (&b)[kWords], float (&x)[kEpt]) {
+#pragma unroll
+        for (int k = 0; k < kWords; ++k) {
+            x[4 * k + 0] = __uint_as_float(b[k].x);
+            x[4 * k + 1] = __uint_as_float(b[k].y);
+            x[4 * k + 2] = __uint_as_float(b[k].z);
+            x[4 * k + 3] = __uint_as_float(b[k].w);
+        }
+    }
+};
+template <> struct Vec16<TB_BF16> {
+    static constexpr int kWords = 2;
+    __device__ static void decode(const uint4 (&b)[kWords], float (&x)[kEpt]) {
+#pragma unroll
+        for (int k = 0; k < kWords; ++k) {
+            const uint32_t u[4] = {b[k].x, b[k].y, b[k].z, b[k].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                x[8 * k + 2 * j + 0] = __uint_as_float(u[j] << 16);
+                x[8 * k + 2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+            }
+        }
+    }
+};
+template <> struct Vec16<TB_F16> {
+    static constexpr int kWords = 2;
+    __device__ static void decode(const uint4 (&b)[kWords], float (&x)[kEpt]) {
+#pragma unroll
+        for (int k = 0; k < kWords; ++k) {
+            const uint32_t u[4] = {b[k].x, b[k].y, b[k].z, b[k].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                x[8 * k + 2 * j + 0] = f16ref_to_f32(u[j] & 0xFFFFu);
+                x[8 * k + 2 * j + 1] = f16ref_to_f32(u[j] >> 16);
+            }
+        }
+    }
+};
+
+template <int DT>
+__device__ __forceinline__ void load16(const void* base, size_t e0, float (&x)[kEpt]) {
+    constexpr int W = Vec16<DT>::kWords;
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const char*>(base) + e0 * Dtype<DT>::kBytes);
+    uint4 b[W];
+#pragma unroll
+    for (int k = 0; k < W; ++k) b[k] = ldg_stream(p + k);
+    Vec16<DT>::decode(b, x);
+}
+
+__device__ __forceinline__ void store16(float* base, size_t e0, const float (&x)[kEpt]) {
+    float4* p = reinterpret_cast<float4*>(base + e0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) stg_stream(p + k, make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]));
+}
+
+__device__ __forceinline__ void count_ties(unsigned long long* ties, int local) {
+    const unsigned active = __activemask();
+    const int total = __reduce_add_sync(active, local);
+    if (total && (threadIdx.x & 31) == (__ffs(active) - 1)) atomicAdd(ties, static_cast<unsigned long long>(total));
+}
+
+// Stage 2 on one thread's 16 scores: select, apply, redistribute; returns the
+// packed mask bytes (group k in byte k).
+template <int M>
+__device__ __forceinline__ uint64_t groups16(const FusedParams& p, const float (&s)[kEpt], float (&w)[kEpt],
+                                             int& ties) {
+    uint64_t packed = 0;
+#pragma unroll
+    for (int q = 0; q < kEpt / M; ++q) {
+        float v[M], sg[M], wg[M];
+#pragma unroll
+        for (int k = 0; k < M; ++k) { v[k] = s[q * M + k]; sg[k] = v[k]; }
+        if (p.ties) ties += near_tie<M>(v, p.n) ? 1 : 0;
+        const uint32_t byte = select_group<M>(v, p.n, p.strategy, p.rounds, p.permute != 0, p.lut);
+#pragma unroll
+        for (int k = 0; k < M; ++k) wg[k] = ((byte >> k) & 1u) ? w[q * M + k] : 0.0f;
+        redistribute_group<M>(wg, sg, byte, p.redist);
+#pragma unroll
+        for (int k = 0; k < M; ++k) w[q * M + k] = wg[k];
+        packed |= static_cast<uint64_t>(byte & 0xFFu) << (8 * q);
+    }
+    return packed;
+}
+
+// Vector kernel: 16 elements per thread, all pointers 16-byte aligned and
+// g_stride * sizeof(G) a multiple of 16 (checked on the host).
+template <int WDT, int GDT, int M>
+__global__ void __launch_bounds__(kThreads) fused_vec_kernel(const FusedParams p) {
+    constexpr int GW = Vec16<GDT>::kWords;
+    constexpr int U = (GW == 2) ? 4 : 2;  // samples in flight per thread
+    const size_t nchunks = p.N / kEpt;
+    const size_t gstride_b = p.gstride * Dtype<GDT>::kBytes;
+    int ties = 0;
+    for (size_t c = blockIdx.x * (size_t)kThreads + threadIdx.x; c < nchunks; c += (size_t)gridDim.x * kThreads) {
+        const size_t e0 = c * kEpt;
+        float F[kEpt];
+        // ---- stage 1: Fisher EMA over the samples, in registers ----
+        const char* gb = static_cast<const char*>(p.g) + e0 * Dtype<GDT>::kBytes;
+        size_t s = 0;
+        if (p.first && p.S > 0) {
+            uint4 b[GW];
+#pragma unroll
+            for (int k = 0; k < GW; ++k) b[k] = ldg_stream(reinterpret_cast<const uint4*>(gb) + k);
+            float x[kEpt];
+            Vec16<GDT>::decode(b, x);
+#pragma unroll
+            for (int i = 0; i < kEpt; ++i) F[i] = ema_first(p.alpha, x[i]);
+            s = 1;
+        } else if (p.use_fin) {
+            load16<TB_F32>(p.fin, e0, F);
+        } else {
+#pragma unroll
+            for (int i = 0; i < kEpt; ++i) F[i] = 0.0f;
+        }
+        for (; s + U <= p.S; s += U) {
+            uint4 b[U][GW];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int k = 0; k < GW; ++k)
+                    b[u][k] = ldg_stream(reinterpret_cast<const uint4*>(gb + (s + u) * gstride_b) + k);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float x[kEpt];
+                Vec16<GDT>::decode(b[u], x);
+#pragma unroll
+                for (int i = 0; i < kEpt; ++i) F[i] = ema_next(F[i], p.beta, p.contrib, x[i]);
+            }
+        }
+        for (; s < p.S; ++s) {
+            uint4 b[GW];
+#pragma unroll
+            for (int k = 0; k < GW; ++k) b[k] = ldg_stream(reinterpret_cast<const uint4*>(gb + s * gstride_b) + k);
+            float x[kEpt];
+            Vec16<GDT>::decode(b, x);
+#pragma unroll
+            for (int i = 0; i < kEpt; ++i) F[i] = ema_next(F[i], p.beta, p.contrib, x[i]);
+        }
+        // ---- importance ----
+        float w[kEpt], sc[kEpt];
+        load16<WDT>(p.w, e0, w);
+        const bool have_f = p.have_f != 0;
+#pragma unroll
+        for (int i = 0; i < kEpt; ++i) sc[i] = importance(w[i], F[i], p.damp, p.mode, have_f);
+        // ---- stage 2: select, apply, redistribute, pack ----
+        const uint64_t packed = groups16<M>(p, sc, w, ties);
+        store16(p.wout, e0, w);
+        constexpr int kMaskBytes = kEpt / M;
+        if (kMaskBytes == 8) *reinterpret_cast<uint64_t*>(p.mout + c * 8) = packed;
+        else if (kMaskBytes == 4) *reinterpret_cast<uint32_t*>(p.mout + c * 4) = static_cast<uint32_t>(packed);
+        else *reinterpret_cast<uint16_t*>(p.mout + c * 2) = static_cast<uint16_t>(packed);
+        if (p.fout && have_f) store16(p.fout, e0, F);
+        if (p.sout) store16(p.sout, e0, sc);
+    }
+    if (p.ties) count_ties(p.ties, ties);
+}
+
+// Generic kernel: one group of M elements per thread, scalar loads; covers any
+// alignment, M in [2, 8], and the tail of the vector kernel.
+template <int M>
+__global__ void __launch_bounds__(kThreads) fused_group_kernel(const FusedParams p) {
+    const size_t G = p.N / M;
+    int ties = 0;
+    for (size_t g = blockIdx.x * (size_t)kThreads + threadIdx.x; g < G; g += (size_t)gridDim.x * kThreads) {
+        const size_t e0 = g * M;
+        float F[M], w[M], sc[M], v[M];
+#pragma unroll
+        for (int k = 0; k < M; ++k) {
+            const size_t e = e0 + k;
+            float f = 0.0f;
+            size_t s = 0;
+            if (p.first && p.S > 0) { f = ema_first(p.alpha, load_any(p.g, p.gdt, e)); s = 1; }
+            else if (p.use_fin) f = p.fin[e];
+            for (; s < p.S; ++s) f = ema_next(f, p.beta, p.contrib, load_any(p.g, p.gdt, s * p.gstride + e));
+            F[k] = f;
+            w[k] = load_any(p.w, p.wdt, e);
+            sc[k] = importance(w[k], f, p.damp, p.mode, p.have_f != 0);
+            v[k] = sc[k];
+        }
+        if (p.ties) ties += near_tie<M>(v, p.n) ? 1 : 0;
+        const uint32_t byte = select_group<M>(v, p.n, p.strategy, p.rounds, p.permute != 0, p.lut);
+#pragma unroll
+        for (int k = 0; k < M; ++k) w[k] = ((byte >> k) & 1u) ? w[k] : 0.0f;
+        redistribute_group<M>(w, sc, byte, p.redist);
+#pragma unroll
+        for (int k = 0; k < M; ++k) {
+            p.wout[e0 + k] = w[k];
+            if (p.fout && p.have_f) p.fout[e0 + k] = F[k];
+            if (p.sout) p.sout[e0 + k] = sc[k];
+        }
+        p.mout[g] = static_cast<uint8_t>(byte);
+    }
+    if (p.ties) count_ties(p.ties, ties);
+}
+
+unsigned grid_for(size_t items) {
+    size_t b = (items + kThreads - 1) / kThreads;
+    return static_cast<unsigned>(std::max<size_t>(1, std::min<size_t>(b, (size_t)1 << 30)));
+}
+
+template <int WDT, int GDT>
+void launch_vec_m(int m, unsigned grid, cudaStream_t st, const FusedParams& p) {
+    if (m == 2) fused_vec_kernel<WDT, GDT, 2><<<grid, kThreads, 0, st>>>(p);
+    else if (m == 4) fused_vec_kernel<WDT, GDT, 4><<<grid, kThreads, 0, st>>>(p);
+    else fused_vec_kernel<WDT, GDT, 8><<<grid, kThreads, 0, st>>>(p);
+}
+
+template <int WDT>
+void launch_vec_g(int gdt, int m, unsigned grid, cudaStream_t st, const FusedParams& p) {
+    if (gdt == TB_F32) launch_vec_m<WDT, TB_F32>(m, grid, st, p);
+    else if (gdt == TB_BF16) launch_vec_m<WDT, TB_BF16>(m, grid, st, p);
+    else launch_vec_m<WDT, TB_F16>(m, grid, st, p);
+}
+
+void launch_vec(const FusedParams& p, int m, cudaStream_t st) {
+    const unsigned grid = grid_for(p.N / kEpt);
+    if (p.wdt == TB_F32) launch_vec_g<TB_F32>(p.gdt, m, grid, st, p);
+    else if (p.wdt == TB_BF16) launch_vec_g<TB_BF16>(p.gdt, m, grid, st, p);
+    else launch_vec_g<TB_F16>(p.gdt, m, grid, st, p);
+}
+
+void launch_group(const FusedParams& p, int m, cudaStream_t st) {
+    const unsigned grid = grid_for(p.N / m);
+    switch (m) {
+    case 2: fused_group_kernel<2><<<grid, kThreads, 0, st>>>(p); break;
+    case 3: fused_group_kernel<3><<<grid, kThreads, 0, st>>>(p); break;
+    case 4: fused_group_kernel<4><<<grid, kThreads, 0, st>>>(p); break;
+    case 5: fused_group_kernel<5><<<grid, kThreads, 0, st>>>(p); break;
+    case 6: fused_group_kernel<6><<<grid, kThreads, 0, st>>>(p); break;
+    case 7: fused_group_kernel<7><<<grid, kThreads, 0, st>>>(p); break;
+    default: fused_group_kernel<8><<<grid, kThreads, 0, st>>>(p); break;
+    }
+}
+
+int dtype_bytes(int dt) { return dt == TB_F32 ? 4 : 2; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Validates args in the order the reference sequence would fail
+// (accumulate_fisher, compute_importance, generate_nm_mask) and fills the
+// kernel parameters.
+int prepare(const tb_prune_args* a, FusedParams& p) {
+    if (!a) return fail(TB_ERR_ARG, "null args");
+    if (a->struct_size < sizeof(tb_prune_args)) return fail(TB_ERR_ARG, "tb_prune_args.struct_size too small");
+    const int n = a->nm_n, m = a->nm_m;
+    if (a->N == 0) return fail(TB_ERR_ZERO_SIZE, "empty tensor");
+    if (n <= 0 || m <= 0 || n >= m) return fail(TB_ERR_CONFIG, "invalid N:M %d:%d", n, m);
+    if (a->N % static_cast<uint64_t>(m) != 0) return fail(TB_ERR_SHAPE, "numel %llu not divisible by M=%d",
+                                                           (unsigned long long)a->N, m);
+    if (m > 8) return fail(TB_ERR_UNSUPPORTED, "M=%d > 8: masks hold one byte per group", m);
+    if (a->w_dtype < TB_F32 || a->w_dtype > TB_BF16 || a->g_dtype < TB_F32 || a->g_dtype > TB_BF16)
+        return fail(TB_ERR_ARG, "bad dtype");
+    if (a->importance_mode < TB_IMP_OBD || a->importance_mode > TB_IMP_NORMALIZED)
+        return fail(TB_ERR_ARG, "bad importance mode %d", a->importance_mode);
+    if (a->mask_strategy < TB_MASK_TOPN || a->mask_strategy > TB_MASK_ITERATIVE)
+        return fail(TB_ERR_ARG, "bad mask strategy %d", a->mask_strategy);
+    if (a->redist_mode < TB_REDIST_NONE || a->redist_mode > TB_REDIST_UNIFORM)
+        return fail(TB_ERR_ARG, "bad redistribution mode %d", a->redist_mode);
+    if (!a->weights || !a->w_out || !a->mask_out) return fail(TB_ERR_ARG, "null weights/outputs");
+    const bool use_f = a->use_fisher != 0;
+    if (use_f && a->S > 0 && !a->grads) return fail(TB_ERR_ARG, "null gradients with S > 0");
+    if (use_f && a->fisher_steps_in > 0 && !a->fisher_in) return fail(TB_ERR_ARG, "fisher_steps_in > 0 without fisher_in");
+    const uint64_t gstride = a->g_stride ? a->g_stride : a->N;
+    if (gstride < a->N) return fail(TB_ERR_ARG, "g_stride < N");
+
+    p = FusedParams{};
+    p.w = a->weights;
+    p.g = a->grads;
+    p.fin = a->fisher_in;
+    p.wout = a->w_out;
+    p.mout = a->mask_out;
+    p.fout = a->fisher_out;
+    p.sout = a->scores_out;
+    p.ties = a->near_ties;
+    p.N = a->N;
+    p.S = use_f ? a->S : 0;
+    p.gstride = gstride;
+    p.alpha = a->alpha;
+    p.beta = a->beta;
+    const float one_m_beta = 1.0f - a->beta;  // ehap.hpp:165
+    p.contrib = a->alpha * one_m_beta;        // ehap.hpp:195
+    p.damp = a->damping;
+    p.mode = a->importance_mode;
+    p.use_fin = use_f && a->fisher_steps_in > 0;
+    p.first = use_f && a->fisher_steps_in == 0 && a->S > 0;
+    p.have_f = use_f && (a->S > 0 || a->fisher_steps_in > 0);
+    p.n = n;
+    p.strategy = a->mask_strategy;
+    p.rounds = a->iterative_rounds;
+    p.redist = a->redist_mode;
+    p.permute = a->permute;
+    p.wdt = a->w_dtype;
+    p.gdt = a->g_dtype;
+    return TB_OK;
+}
+
+int launch_fused(FusedParams p, int m, cudaStream_t st) {
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    if (p.strategy != TB_MASK_OPTIMAL && (rc = topn_table(p.n, m, &p.lut))) return rc;
+    const bool vec_m = (m == 2 || m == 4 || m == 8);
+    const bool vec_ok = vec_m && aligned16(p.w) && aligned16(p.wout) && (!p.S || aligned16(p.g)) &&
+                        (!p.use_fin || aligned16(p.fin)) && (!p.fout || aligned16(p.fout)) &&
+                        (!p.sout || aligned16(p.sout)) &&
+                        (reinterpret_cast<uintptr_t>(p.mout) % (kEpt / m) == 0) &&
+                        ((p.gstride * dtype_bytes(p.gdt)) % 16 == 0);
+    const size_t nvec = vec_ok ? (p.N / kEpt) * kEpt : 0;
+    if (nvec) {
+        FusedParams q = p;
+        q.N = nvec;
+        launch_vec(q, m, st);
+        if ((rc = check_launch("fused_vec_kernel"))) return rc;
+    }
+    if (nvec < p.N) {
+        // Remaining elements (a multiple of M): offset every pointer.
+        FusedParams t = p;
+        t.N = p.N - nvec;
+        t.w = static_cast<const char*>(p.w) + nvec * dtype_bytes(p.wdt);
+        if (p.S) t.g = static_cast<const char*>(p.g) + nvec * dtype_bytes(p.gdt);
+        if (p.fin) t.fin = p.fin + nvec;
+        t.wout = p.wout + nvec;
+        t.mout = p.mout + nvec / m;
+        if (p.fout) t.fout = p.fout + nvec;
+        if (p.sout) t.sout = p.sout + nvec;
+        launch_group(t, m, st);
+        if ((rc = check_launch("fused_group_kernel"))) return rc;
+    }
+    return TB_OK;
+}
+
+// ---- host-buffer pipeline ----------------------------------------------------
+// Per-device staging for tb_score_mask_pack_host: kSlots independent
+// (stream, buffers) slots; chunk k goes to slot k % kSlots, so the H2D copy of
+// one chunk, the kernel of another and the D2H copy of a third overlap.
+constexpr int kSlots = 3;
+
+struct Slot {
+    cudaStream_t st = nullptr;
+    char* dbuf = nullptr;
+    size_t cap = 0;
+};
+
+struct HostPipe {
+    int dev = -1;
+    Slot slot[kSlots];
+    unsigned long long* ties = nullptr;
+};
+
+std::mutex g_pipe_mu;
+std::vector<HostPipe*> g_pipes;
+
+int get_pipe(int dev, size_t need, HostPipe** out) {
+    std::lock_guard<std::mutex> lk(g_pipe_mu);
+    HostPipe* hp = nullptr;
+    for (auto* x : g_pipes)
+        if (x->dev == dev) hp = x;
+    if (!hp) {
+        hp = new HostPipe;
+        hp->dev = dev;
+        for (auto& s : hp->slot) {
+            cudaError_t e = cudaStreamCreateWithFlags(&s.st, cudaStreamNonBlocking);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+        }
+        cudaError_t e = cudaMalloc(&hp->ties, sizeof(unsigned long long));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(tie counter)");
+        g_pipes.push_back(hp);
+    }
+    for (auto& s : hp->slot) {
+        if (s.cap >= need) continue;
+        if (s.dbuf) {
+            cudaStreamSynchronize(s.st);
+            cudaFree(s.dbuf);
+            s.dbuf = nullptr;
+            s.cap = 0;
+        }
+        cudaError_t e = cudaMalloc(&s.dbuf, need);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(host-path staging)");
+        s.cap = need;
+    }
+    *out = hp;
+    return TB_OK;
+}
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+int tb_score_mask_pack(const tb_prune_args* args, void* stream) {
+    FusedParams p;
+    int rc = prepare(args, p);
+    if (rc) return rc;
+    return launch_fused(p, args->nm_m, static_cast<cudaStream_t>(stream));
+}
+
+int tb_score_mask_pack_host(const tb_prune_args* a) {
+    FusedParams p;
+    int rc = prepare(a, p);
+    if (rc) return rc;
+    int dev = 0;
+    if ((rc = require_device(&dev))) return rc;
+    const int m = a->nm_m;
+    const size_t N = a->N, S = p.S;
+    const int wb = dtype_bytes(a->w_dtype), gb = dtype_bytes(a->g_dtype);
+    // Chunk: a multiple of 16 elements and of M, about 64 MB of gradients.
+    size_t chunk = (64ull << 20) / std::max<size_t>(1, S * gb + wb + 8);
+    chunk = std::max<size_t>(chunk / 16 / m * 16 * m, static_cast<size_t>(16 * m));
+    chunk = std::min(chunk, round_up(N, static_cast<size_t>(16 * m)));
+    // Staging layout per slot: [W][G (S rows of chunk)][F_in][W'][mask][F_out][s_out]
+    const size_t o_w = 0;
+    const size_t o_g = round_up(o_w + chunk * wb, 256);
+    const size_t o_fi = round_up(o_g + S * chunk * gb, 256);
+    const size_t o_wo = round_up(o_fi + (p.use_fin ? chunk * 4 : 0), 256);
+    const size_t o_m = round_up(o_wo + chunk * 4, 256);
+    const size_t o_fo = round_up(o_m + chunk / m, 256);
+    const size_t o_so = round_up(o_fo + (p.fout ? chunk * 4 : 0), 256);
+    const size_t need = round_up(o_so + (p.sout ? chunk * 4 : 0), 256);
+    HostPipe* hp = nullptr;
+    if ((rc = get_pipe(dev, need, &hp))) return rc;
+    if (p.ties) {
+        cudaError_t e = cudaMemsetAsync(hp->ties, 0, sizeof(unsigned long long), hp->slot[0].st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+        // Every slot stream must see the zeroed counter.
+        cudaStreamSynchronize(hp->slot[0].st);
+    }
+    const char* hw = static_cast<const char*>(a->weights);
+    const char* hg = static_cast<const char*>(a->grads);
+    const size_t gstride = p.gstride;
+    size_t k = 0;
+    for (size_t e0 = 0; e0 < N; e0 += chunk, ++k) {
+        const size_t len = std::min(chunk, N - e0);
+        Slot& sl = hp->slot[k % kSlots];
+        char* d = sl.dbuf;
+        cudaError_t e = cudaMemcpyAsync(d + o_w, hw + e0 * wb, len * wb, cudaMemcpyHostToDevice, sl.st);
+        if (e == cudaSuccess && S)
+            e = cudaMemcpy2DAsync(d + o_g, len * gb, hg + e0 * gb, gstride * gb, len * gb, S, cudaMemcpyHostToDevice, sl.st);
+        if (e == cudaSuccess && p.use_fin)
+            e = cudaMemcpyAsync(d + o_fi, a->fisher_in + e0, len * 4, cudaMemcpyHostToDevice, sl.st);
+        if (e != cudaSuccess) return cuda_fail(e, "host-path H2D copy");
+        FusedParams q = p;
+        q.N = len;
+        q.w = d + o_w;
+        q.g = S ? d + o_g : nullptr;
+        q.gstride = len;
+        q.fin = p.use_fin ? reinterpret_cast<const float*>(d + o_fi) : nullptr;
+        q.wout = reinterpret_cast<float*>(d + o_wo);
+        q.mout = reinterpret_cast<uint8_t*>(d + o_m);
+        q.fout = p.fout ? reinterpret_cast<float*>(d + o_fo) : nullptr;
+        q.sout = p.sout ? reinterpret_cast<float*>(d + o_so) : nullptr;
+        q.ties = p.ties ? hp->ties : nullptr;
+        if ((rc = launch_fused(q, m, sl.st))) return rc;
+        e = cudaMemcpyAsync(a->w_out + e0, q.wout, len * 4, cudaMemcpyDeviceToHost, sl.st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(a->mask_out + e0 / m, q.mout, len / m, cudaMemcpyDeviceToHost, sl.st);
+        if (e == cudaSuccess && q.fout) e = cudaMemcpyAsync(a->fisher_out + e0, q.fout, len * 4, cudaMemcpyDeviceToHost, sl.st);
+        if (e == cudaSuccess && q.sout) e = cudaMemcpyAsync(a->scores_out + e0, q.sout, len * 4, cudaMemcpyDeviceToHost, sl.st);
+        if (e != cudaSuccess) return cuda_fail(e, "host-path D2H copy");
+    }
+    for (auto& sl : hp->slot) {
+        cudaError_t e = cudaStreamSynchronize(sl.st);
+        if (e != cudaSuccess) return cuda_fail(e, "host-path synchronise");
+    }
+    if (p.ties) {
+        unsigned long long t = 0;
+        cudaError_t e = cudaMemcpy(&t, hp->ties, sizeof(t), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_fail(e, "tie counter D2H");
+        *a->near_ties += t;
+    }
+    return TB_OK;
+}
+
+}  // extern "C"

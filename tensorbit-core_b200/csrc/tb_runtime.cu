@@ -1,0 +1,164 @@
+// Library runtime: error reporting, device plumbing and the per-device caches
+// (top-N tie tables, host-path staging buffers).
+#include <cstdarg>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "tb_runtime.h"
+
+namespace tb {
+
+std::vector<uint8_t> build_topn_table(int n, int m);  // tb_lut.cpp
+
+namespace {
+thread_local std::string t_last_error;
+
+struct TableKey {
+    int dev, n, m;
+    bool operator<(const TableKey& o) const { return std::tie(dev, n, m) < std::tie(o.dev, o.n, o.m); }
+};
+
+std::mutex g_mu;
+std::map<TableKey, uint8_t*> g_tables;
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(TB_ERR_CUDA, "%s: %s (%d)", what, cudaGetErrorString(e), static_cast<int>(e));
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, what);
+}
+
+int require_device(int* dev_out) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        return fail(TB_ERR_NO_DEVICE, "no CUDA device available (%s)", cudaGetErrorString(e));
+    }
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev_out) *dev_out = dev;
+    return TB_OK;
+}
+
+int topn_table(int n, int m, const uint8_t** out) {
+    int dev = 0;
+    int rc = require_device(&dev);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_tables.find({dev, n, m});
+    if (it != g_tables.end()) { *out = it->second; return TB_OK; }
+    std::vector<uint8_t> host = build_topn_table(n, m);
+    uint8_t* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, host.size());
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(top-N tie table)");
+    e = cudaMemcpy(d, host.data(), host.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { cudaFree(d); return cuda_fail(e, "cudaMemcpy(top-N tie table)"); }
+    g_tables[{dev, n, m}] = d;
+    *out = d;
+    return TB_OK;
+}
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+int tb_abi_version(void) { return TB_ABI_VERSION; }
+
+const char* tb_last_error(void) { return t_last_error.c_str(); }
+
+int tb_device_count(int* count) {
+    if (!count) return fail(TB_ERR_ARG, "tb_device_count: null pointer");
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    if (e != cudaSuccess) { cudaGetLastError(); c = 0; }
+    *count = c;
+    return TB_OK;
+}
+
+int tb_set_device(int device) {
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    cudaError_t e = cudaSetDevice(device);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaSetDevice");
+}
+
+int tb_malloc(void** ptr, size_t bytes) {
+    if (!ptr) return fail(TB_ERR_ARG, "tb_malloc: null pointer");
+    *ptr = nullptr;
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    if (bytes == 0) return TB_OK;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaMalloc");
+}
+
+int tb_free(void* ptr) {
+    if (!ptr) return TB_OK;
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaFree");
+}
+
+static int copy(void* dst, const void* src, size_t bytes, cudaMemcpyKind kind, void* stream, const char* what) {
+    if (bytes == 0) return TB_OK;
+    if (!dst || !src) return fail(TB_ERR_ARG, "%s: null pointer", what);
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, kind, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, what);
+}
+
+int tb_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+    return copy(dst, src, bytes, cudaMemcpyHostToDevice, stream, "tb_memcpy_h2d");
+}
+int tb_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+    return copy(dst, src, bytes, cudaMemcpyDeviceToHost, stream, "tb_memcpy_d2h");
+}
+int tb_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
+    return copy(dst, src, bytes, cudaMemcpyDeviceToDevice, stream, "tb_memcpy_d2d");
+}
+
+int tb_memset(void* dst, int value, size_t bytes, void* stream) {
+    if (bytes == 0) return TB_OK;
+    if (!dst) return fail(TB_ERR_ARG, "tb_memset: null pointer");
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    cudaError_t e = cudaMemsetAsync(dst, value, bytes, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "tb_memset");
+}
+
+int tb_stream_sync(void* stream) {
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaStreamSynchronize");
+}
+
+int tb_prepare_nm(int n, int m) {
+    if (n <= 0 || m <= 0 || n >= m) return fail(TB_ERR_CONFIG, "invalid N:M %d:%d", n, m);
+    if (m > 8) return fail(TB_ERR_UNSUPPORTED, "M=%d > 8: masks hold one byte per group", m);
+    const uint8_t* t = nullptr;
+    return topn_table(n, m, &t);
+}
+
+}  // extern "C"

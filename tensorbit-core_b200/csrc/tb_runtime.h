@@ -1,0 +1,23 @@
+// Internal runtime helpers shared by the kernel translation units.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "tb_kernels.h"
+
+namespace tb {
+
+// Records printf-style text for tb_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+// TB_ERR_CUDA with the runtime's error string.
+int cuda_fail(cudaError_t e, const char* what);
+// Converts a pending launch error into a status.
+int check_launch(const char* what);
+// TB_ERR_NO_DEVICE unless a device is current; returns its ordinal.
+int require_device(int* dev_out);
+// Device copy of the top-n-of-m tie table for the current device, built on
+// first use (a cudaMalloc + copy, so first use must precede stream capture).
+int topn_table(int n, int m, const uint8_t** out);
+
+}  // namespace tb
