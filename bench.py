@@ -46,6 +46,7 @@ WORKLOAD = "7B-class decoder (32 layers, hidden 4096, inter 14336, 32q/8kv heads
 
 
 def parse():
+    global LAYER, LAYERS, PARAMS_PER_LAYER, PARAMS_PER_STEP
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -54,7 +55,18 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decoder layers per step (profiling a smaller case only; default 32)")
+    ap.add_argument("--matrices", default="",
+                    help="comma list restricting the per-layer matrices (profiling only), e.g. q_proj")
+    a = ap.parse_args()
+    if a.matrices:
+        keep = set(a.matrices.split(","))
+        LAYER = [x for x in LAYER if x[0] in keep]
+    LAYERS = a.layers
+    PARAMS_PER_LAYER = sum(r * c for _, r, c in LAYER)
+    PARAMS_PER_STEP = PARAMS_PER_LAYER * LAYERS
+    return a
 
 
 # ---------------------------------------------------------------------------

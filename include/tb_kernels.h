@@ -112,6 +112,27 @@ int tb_nm_mask(const float* importance, uint8_t* mask_out, size_t N, int n, int 
 int tb_redistribute(float* weights, const uint8_t* mask, const float* importance, size_t N, int m,
                     int mode, void* stream);
 
+/* EHAPPruner::select_pruning_mask (ehap.hpp:290-329): keep = (size_t)(sparsity *
+ * (float)N) (at least 1); the threshold is the (N-keep)-th smallest score and
+ * every score >= it is kept.  Writes 1 byte per element to mask_out (may be
+ * NULL), the threshold and the number of pruned elements to host memory, and
+ * synchronises the stream.  keep >= N keeps everything (threshold 0, pruned 0).
+ * Scratch: about 16 KB of device memory, allocated stream-ordered per call. */
+int tb_threshold_select(const float* scores, size_t N, float sparsity, uint8_t* mask_out,
+                        float* threshold_out, uint64_t* pruned_out, void* stream);
+/* EHAPPruner::apply_mask (ehap.hpp:334-362): zero weights[i] where mask[i] == 0
+ * (1 byte per element); the number zeroed goes to *pruned_out (host, may be
+ * NULL; when given the call synchronises the stream). */
+int tb_ehap_apply_mask(float* weights, const uint8_t* mask, size_t N, uint64_t* pruned_out, void* stream);
+/* apply_fisher_normalization (ehap.hpp:720-731): F /= ||F||_2 with the
+ * reference's serial float sum (one device thread; off by default). */
+int tb_fisher_normalize(float* fisher, size_t N, void* stream);
+/* EHAPPruner::compensate_weights (ehap.hpp:367-403): mode 0 none, 1 bias (serial
+ * sum of pruned weights added to the last weight), 2 redistribution over groups
+ * of 8 in proportion to the kept scores. */
+int tb_compensate(float* weights, const uint8_t* mask, const float* importance, size_t N, int mode,
+                  void* stream);
+
 /* ---- fused score -> mask -> pack pass ------------------------------------ */
 /* One pass over a tensor: Fisher EMA over S gradient samples, importance,
  * CORING N:M mask, apply, redistribution, and emission of the .tb weight and

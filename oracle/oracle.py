@@ -86,6 +86,8 @@ class Oracle:
                                C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p, _sz,
                                C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                C.c_void_p, _u8p, _szp, _szp]
+        self._comp = getattr(L, p + "compensate")
+        self._comp.argtypes = [_f32p, _u8p, _f32p, _sz, C.c_int]
         self._mock = getattr(L, p + "mock_tensor")
         self._mock.argtypes = [_sz, _f32p, _f32p]
         if kind == "port":
@@ -218,6 +220,15 @@ class Oracle:
                                os.path.join(d, "x.safetensors").encode(), out)
                 assert rc == 0, rc
         return out
+
+    def compensate(self, w, mask, s, mode):
+        """EHAPPruner::compensate_weights on a 1-byte-per-element mask; returns new weights."""
+        w = np.array(w, np.float32, copy=True)
+        rc = self._comp(w, np.ascontiguousarray(mask, np.uint8), np.ascontiguousarray(s, np.float32),
+                        w.size, mode)
+        if self.kind == "ref":
+            assert rc == 0, rc
+        return w
 
     def mock_tensor(self, N):
         w = np.zeros(N, np.float32)

@@ -232,6 +232,21 @@ int ref_pipeline(float* w_inout, const float* grads, std::size_t S, std::size_t 
     return 0;
 }
 
+// EHAPPruner::compensate_weights (ehap.hpp:367-403).
+int ref_compensate(float* w_inout, const uint8_t* mask, const float* s, std::size_t N, int mode) {
+    EHAPConfig c;
+    c.compensation_mode = static_cast<CompensationMode>(mode);
+    EHAPPruner<float> ehap(c);
+    auto wt = host_tensor(w_inout, N);
+    auto st = host_tensor(s, N);
+    auto mk = host_bytes(N);
+    std::memcpy(mk.data(), mask, N);
+    auto r = ehap.compensate_weights(wt, mk, st);
+    if (!r) return 100 + static_cast<int>(r.error());
+    std::memcpy(w_inout, wt.data(), N * sizeof(float));
+    return 0;
+}
+
 // TBWriter::write (serialization.hpp:101-151).
 int ref_write_tb(const char* path, const float* w, std::size_t N, const uint8_t* masks,
                  std::size_t G, uint32_t n, uint32_t m) {

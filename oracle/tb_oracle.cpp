@@ -482,6 +482,29 @@ size_t port_near_ties(const float* s, size_t N, int n, int m) {
     return cnt;
 }
 
+// EHAPPruner::compensate_weights (ehap.hpp:367-403) on a 1-byte-per-element mask.
+void port_compensate(float* w, const uint8_t* mask, const float* s, size_t N, int mode) {
+    if (mode == 0 || N == 0) return;
+    if (mode == 1) {
+        float delta = 0.0f;
+        for (size_t i = 0; i < N; ++i)
+            if (!mask[i]) delta += w[i];
+        w[N - 1] += delta;
+        return;
+    }
+    for (size_t g = 0; g < N; g += 8) {
+        const size_t end = (g + 8 < N) ? g + 8 : N;
+        float t_pruned = 0.0f, t_weight = 0.0f;
+        for (size_t i = g; i < end; ++i) {
+            if (!mask[i]) t_pruned += w[i];
+            else t_weight += s[i];
+        }
+        if (t_weight <= 0.0f) continue;
+        for (size_t i = g; i < end; ++i)
+            if (mask[i]) w[i] += t_pruned * s[i] / t_weight;
+    }
+}
+
 void port_topn_group(const float* vals, int n, int m, uint8_t* mask_out) {
     *mask_out = topn_group(vals, n, m);
 }

@@ -41,6 +41,7 @@ void port_tb_header(uint8_t out[4096], uint32_t n, uint32_t m, uint64_t num_weig
 void port_decode_half(const uint16_t* in, size_t n, int is_bf16, float* out);
 void port_mock_tensor(size_t N, float* w_out, float* g_out);
 size_t port_near_ties(const float* s, size_t N, int n, int m);
+void port_compensate(float* w, const uint8_t* mask, const float* s, size_t N, int mode);
 void port_topn_group(const float* vals, int n, int m, uint8_t* mask_out);
 
 #ifdef __cplusplus

@@ -106,6 +106,10 @@ def lib() -> C.CDLL:
             "tb_importance": ([vp, i32, vp, vp, sz, f32, i32, vp], i32),
             "tb_nm_mask": ([vp, vp, sz, i32, i32, i32, i32, i32, vp], i32),
             "tb_redistribute": ([vp, vp, vp, sz, i32, i32, vp], i32),
+            "tb_threshold_select": ([vp, sz, f32, vp, C.POINTER(C.c_float), C.POINTER(C.c_uint64), vp], i32),
+            "tb_ehap_apply_mask": ([vp, vp, sz, C.POINTER(C.c_uint64), vp], i32),
+            "tb_fisher_normalize": ([vp, sz, vp], i32),
+            "tb_compensate": ([vp, vp, vp, sz, i32, vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),
         }
