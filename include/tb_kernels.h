@@ -180,6 +180,28 @@ int tb_score_mask_pack(const tb_prune_args* args, void* stream);
  * several streams, and returns when the outputs are in host memory. */
 int tb_score_mask_pack_host(const tb_prune_args* args);
 
+/* tb_score_mask_pack_host for callers that cannot allocate device memory.
+ * No counterpart in the reference (its pruners run on host memory only).
+ * Who needs it: a process whose GPU memory is already reserved by another
+ * allocator - a framework's caching pool, or a server that fixes its memory
+ * budget at start-up - where a cudaMalloc from this library would fail or
+ * fragment that pool.  This entry point calls no cudaMalloc / cudaFree: it
+ * stages chunks through a static 16 MiB device array that every GPU loading
+ * the library holds until the process exits.  Results are identical to
+ * tb_score_mask_pack_host.
+ *   - Limit: one chunk of 16*M elements with all S samples must fit in the
+ *     16 MiB array; larger requests return TB_ERR_CAPACITY with the sizes.
+ *   - Top-N / iterative masks need the (N, M) tie table already on the
+ *     device (tb_prepare_nm once, where allocation is allowed); otherwise
+ *     TB_ERR_UNSUPPORTED.  TB_MASK_OPTIMAL needs no table.
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Runs on the legacy default stream and returns when the outputs are in
+ *     host memory.  All calls share the one array (it keeps the last call's
+ *     contents; the tie counter is cleared per call): calls that overlap on
+ *     the GPU, e.g. from two host threads, race and must be serialised. */
+int tb_score_mask_pack_host_noalloc(const tb_prune_args* args);
+
 #ifdef __cplusplus
 }
 #endif

@@ -528,3 +528,122 @@ int tb_score_mask_pack_host(const tb_prune_args* a) {
 }
 
 }  // extern "C"
+
+// ---- host-buffer pass without device allocation ----------------------------
+// Some callers cannot let this library call cudaMalloc: a process whose GPU
+// memory is already fully reserved by another allocator (a framework's caching
+// pool, or a serving process that pins its budget at start-up) would see the
+// allocation fail or fragment its pool.  tb_score_mask_pack_host_noalloc stages
+// through the fixed array below instead.  The array is a file-scope device
+// variable, so every GPU that loads this library holds its 16 MiB until the
+// process exits.  Host code must not take its address directly (in host code
+// the name is only a stand-in); the device address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+static __device__ __align__(256) unsigned char g_tb_noalloc_staging[16u << 20];
+
+namespace tb {
+namespace {
+
+constexpr size_t kNoAllocBytes = sizeof(g_tb_noalloc_staging);
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+char* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of the staging array on `dev` (the current device); the
+// first call per device resolves and caches it.
+int noalloc_staging(int dev, char** out) {
+    if (dev < 0 || dev >= kMaxDevices) return fail(TB_ERR_UNSUPPORTED, "device ordinal %d >= %d", dev, kMaxDevices);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_tb_noalloc_staging);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc staging)");
+        g_noalloc_addr[dev] = static_cast<char*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return TB_OK;
+}
+
+}  // namespace
+}  // namespace tb
+
+extern "C" int tb_score_mask_pack_host_noalloc(const tb_prune_args* a) {
+    FusedParams p;
+    int rc = prepare(a, p);
+    if (rc) return rc;
+    int dev = 0;
+    if ((rc = require_device(&dev))) return rc;
+    const int m = a->nm_m;
+    if (p.strategy != TB_MASK_OPTIMAL && !topn_table_ready(p.n, m))
+        return fail(TB_ERR_UNSUPPORTED,
+                    "top-N tie table for %d:%d is not on this device yet and building it would allocate; "
+                    "call tb_prepare_nm(%d, %d) once where allocation is allowed, or use TB_MASK_OPTIMAL",
+                    p.n, m, p.n, m);
+    char* base = nullptr;
+    if ((rc = noalloc_staging(dev, &base))) return rc;
+    const size_t N = a->N, S = p.S;
+    const size_t wb = dtype_bytes(a->w_dtype), gb = dtype_bytes(a->g_dtype);
+    // Bytes one element occupies across the staging regions, and the fixed
+    // overhead: the tie counter and up to 256 bytes of alignment per region.
+    const size_t per_elem = wb + S * gb + (p.use_fin ? 4 : 0) + 4 + 1 + (p.fout ? 4 : 0) + (p.sout ? 4 : 0);
+    const size_t fixed = 256 + 8 * 256;
+    const size_t unit = static_cast<size_t>(16 * m);
+    size_t chunk = kNoAllocBytes > fixed ? (kNoAllocBytes - fixed) / per_elem / unit * unit : 0;
+    if (chunk == 0)
+        return fail(TB_ERR_CAPACITY,
+                    "tb_score_mask_pack_host_noalloc: one %zu-element chunk with %zu samples needs %zu bytes; "
+                    "the static staging array holds %zu bytes",
+                    unit, S, fixed + unit * per_elem, kNoAllocBytes);
+    chunk = std::min(chunk, round_up(N, unit));
+    unsigned long long* ties = reinterpret_cast<unsigned long long*>(base);
+    const size_t o_w = 256;
+    const size_t o_g = round_up(o_w + chunk * wb, 256);
+    const size_t o_fi = round_up(o_g + S * chunk * gb, 256);
+    const size_t o_wo = round_up(o_fi + (p.use_fin ? chunk * 4 : 0), 256);
+    const size_t o_m = round_up(o_wo + chunk * 4, 256);
+    const size_t o_fo = round_up(o_m + chunk / m, 256);
+    const size_t o_so = round_up(o_fo + (p.fout ? chunk * 4 : 0), 256);
+    if (round_up(o_so + (p.sout ? chunk * 4 : 0), 256) > kNoAllocBytes)
+        return fail(TB_ERR_CAPACITY, "tb_score_mask_pack_host_noalloc: staging layout exceeds %zu bytes", kNoAllocBytes);
+    // One sequential pass on the legacy default stream.  The array keeps the
+    // previous call's contents; only the tie counter must start at zero.
+    cudaStream_t st = 0;
+    cudaError_t e = cudaSuccess;
+    if (p.ties) e = cudaMemsetAsync(ties, 0, sizeof(*ties), st);
+    if (e != cudaSuccess) return cuda_fail(e, "no-alloc tie counter reset");
+    const char* hw = static_cast<const char*>(a->weights);
+    const char* hg = static_cast<const char*>(a->grads);
+    for (size_t e0 = 0; e0 < N; e0 += chunk) {
+        const size_t len = std::min(chunk, N - e0);
+        e = cudaMemcpyAsync(base + o_w, hw + e0 * wb, len * wb, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess && S)
+            e = cudaMemcpy2DAsync(base + o_g, len * gb, hg + e0 * gb, p.gstride * gb, len * gb, S,
+                                  cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess && p.use_fin)
+            e = cudaMemcpyAsync(base + o_fi, a->fisher_in + e0, len * 4, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "no-alloc H2D copy");
+        FusedParams q = p;
+        q.N = len;
+        q.w = base + o_w;
+        q.g = S ? base + o_g : nullptr;
+        q.gstride = len;
+        q.fin = p.use_fin ? reinterpret_cast<const float*>(base + o_fi) : nullptr;
+        q.wout = reinterpret_cast<float*>(base + o_wo);
+        q.mout = reinterpret_cast<uint8_t*>(base + o_m);
+        q.fout = p.fout ? reinterpret_cast<float*>(base + o_fo) : nullptr;
+        q.sout = p.sout ? reinterpret_cast<float*>(base + o_so) : nullptr;
+        q.ties = p.ties ? ties : nullptr;
+        if ((rc = launch_fused(q, m, st))) return rc;
+        e = cudaMemcpyAsync(a->w_out + e0, q.wout, len * 4, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(a->mask_out + e0 / m, q.mout, len / m, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess && q.fout) e = cudaMemcpyAsync(a->fisher_out + e0, q.fout, len * 4, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess && q.sout) e = cudaMemcpyAsync(a->scores_out + e0, q.sout, len * 4, cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) return cuda_fail(e, "no-alloc D2H copy");
+    }
+    unsigned long long t = 0;
+    if (p.ties) e = cudaMemcpyAsync(&t, ties, sizeof(t), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "no-alloc synchronise");
+    if (p.ties) *a->near_ties += t;
+    return TB_OK;
+}

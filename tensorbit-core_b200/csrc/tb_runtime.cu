@@ -77,6 +77,13 @@ int topn_table(int n, int m, const uint8_t** out) {
     return TB_OK;
 }
 
+bool topn_table_ready(int n, int m) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g_tables.count({dev, n, m}) != 0;
+}
+
 }  // namespace tb
 
 using namespace tb;

@@ -19,5 +19,8 @@ int require_device(int* dev_out);
 // Device copy of the top-n-of-m tie table for the current device, built on
 // first use (a cudaMalloc + copy, so first use must precede stream capture).
 int topn_table(int n, int m, const uint8_t** out);
+// True when the current device already holds the top-n-of-m tie table
+// (no build, no allocation).
+bool topn_table_ready(int n, int m);
 
 }  // namespace tb

@@ -112,6 +112,7 @@ def lib() -> C.CDLL:
             "tb_compensate": ([vp, vp, vp, sz, i32, vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),
+            "tb_score_mask_pack_host_noalloc": ([C.POINTER(PruneArgs)], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
