@@ -93,6 +93,10 @@ int tb_nm_mask_generic(const float* importance, uint8_t* mask_out, size_t N_elem
 int tb_apply_mask(float* weights, const uint8_t* mask, size_t N, int group_m, void* stream);
 
 /* ---- stage entry points (the pruners' loops, on the device) ------------ */
+/* load_safetensor's element widening (src/main.cpp:204-250): BF16 exactly, F16
+ * as the reference decodes it (exponent 0 keeps the fraction in an FP32 with
+ * exponent 0), F32 copied. */
+int tb_decode_to_f32(const void* in, int dtype, float* out, size_t N, void* stream);
 /* One EHAPPruner::accumulate_fisher call (ehap.hpp:148-201) over N gradients of
  * dtype g_dtype: first_step != 0 gives F = (alpha*g)*g, otherwise
  * F = beta*F + ((alpha*(1-beta))*g)*g with the reference's float rounding. */
@@ -132,6 +136,19 @@ int tb_fisher_normalize(float* fisher, size_t N, void* stream);
  * of 8 in proportion to the kept scores. */
 int tb_compensate(float* weights, const uint8_t* mask, const float* importance, size_t N, int mode,
                   void* stream);
+
+/* EHAPPruner::prune_block_obs (ehap.hpp:502-704): blockwise OBS with
+ * H = diag(F + damping) + U U^T over contiguous blocks of `block` weights.
+ * U holds K gradient snapshots (hist: host array of K device pointers, oldest
+ * first, K <= 16) weighted exp(-(K-1-k)/2), or sqrt(off_diag_alpha) * w when
+ * K == 0.  Per-block prune targets follow the reference's exp(-4 rel)
+ * allocation; each block is pruned greedily by w_i^2 / [H^-1]_ii with OBS
+ * updates and rank-1 deflation.  Weights are updated in place; the number
+ * pruned goes to *pruned_out (host) and the call synchronises the stream.
+ * block <= 224 (the B x B inverse lives in shared memory). */
+int tb_block_obs(float* weights, const float* fisher, const float* const* hist, int K, size_t N,
+                 size_t block, float sparsity, float damping, float off_diag_alpha, uint64_t* pruned_out,
+                 void* stream);
 
 /* ---- fused score -> mask -> pack pass ------------------------------------ */
 /* One pass over a tensor: Fisher EMA over S gradient samples, importance,

@@ -88,6 +88,9 @@ class Oracle:
                                C.c_void_p, _u8p, _szp, _szp]
         self._comp = getattr(L, p + "compensate")
         self._comp.argtypes = [_f32p, _u8p, _f32p, _sz, C.c_int]
+        self._bobs = getattr(L, p + "block_obs")
+        self._bobs.argtypes = [_f32p, C.c_void_p, _sz, C.c_void_p, _sz, _sz, _sz, C.c_float, C.c_float,
+                               C.c_float, C.c_float, C.c_int, _sz, _szp]
         self._mock = getattr(L, p + "mock_tensor")
         self._mock.argtypes = [_sz, _f32p, _f32p]
         if kind == "port":
@@ -229,6 +232,22 @@ class Oracle:
         if self.kind == "ref":
             assert rc == 0, rc
         return w
+
+    def block_obs(self, w, grads, hist=None, block=128, sparsity=0.5, damping=0.01, off_alpha=0.01,
+                  fisher_alpha=0.01, use_fisher=True, hist_size=4):
+        """accumulate_fisher x S, store_gradient x K, prune_block_obs; returns (rc, w', pruned)."""
+        w = np.array(w, np.float32, copy=True).reshape(-1)
+        g = np.ascontiguousarray(grads, np.float32)
+        S = g.shape[0] if g.ndim == 2 else 0
+        K = 0
+        hp = None
+        if hist is not None:
+            hist = np.ascontiguousarray(hist, np.float32)
+            K, hp = hist.shape[0], hist.ctypes.data
+        pr = C.c_size_t(0)
+        rc = self._bobs(w, g.ctypes.data if S else None, S, hp, K, w.size, block, sparsity, damping,
+                        off_alpha, fisher_alpha, int(use_fisher), hist_size, C.byref(pr))
+        return rc, w, pr.value
 
     def mock_tensor(self, N):
         w = np.zeros(N, np.float32)

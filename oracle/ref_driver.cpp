@@ -232,6 +232,33 @@ int ref_pipeline(float* w_inout, const float* grads, std::size_t S, std::size_t 
     return 0;
 }
 
+// Block OBS as tb-prune runs it (src/main.cpp:375-386): accumulate_fisher x S,
+// store_gradient x K, then EHAPPruner::prune_block_obs (ehap.hpp:502-704).
+// block == 0 keeps the config default (128).
+int ref_block_obs(float* w_inout, const float* grads, std::size_t S, const float* hist, std::size_t K,
+                  std::size_t N, std::size_t block, float sparsity, float damping, float off_alpha,
+                  float fisher_alpha, int use_fisher, std::size_t hist_size, std::size_t* pruned_out) {
+    EHAPConfig c = ehap_config(0.99f, damping, 0, use_fisher, 0, sparsity);
+    c.prune_strategy = PruneStrategy::kBlockOBS;
+    if (block) c.obs_block_size = block;
+    c.obs_off_diag_alpha = off_alpha;
+    c.gradient_history_size = hist_size;
+    EHAPPruner<float> ehap(c);
+    int rc = feed_fisher(ehap, grads, S, N, fisher_alpha);
+    if (rc) return rc;
+    for (std::size_t k = 0; k < K; ++k) {
+        auto g = host_tensor(hist + k * N, N);
+        auto r = ehap.store_gradient(g);
+        if (!r) return 150 + static_cast<int>(r.error());
+    }
+    auto wt = host_tensor(w_inout, N);
+    auto r = ehap.prune(wt);
+    if (!r) return 200 + static_cast<int>(r.error());
+    std::memcpy(w_inout, wt.data(), N * sizeof(float));
+    if (pruned_out) *pruned_out = r.value();
+    return 0;
+}
+
 // EHAPPruner::compensate_weights (ehap.hpp:367-403).
 int ref_compensate(float* w_inout, const uint8_t* mask, const float* s, std::size_t N, int mode) {
     EHAPConfig c;

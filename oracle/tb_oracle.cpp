@@ -505,6 +505,195 @@ void port_compensate(float* w, const uint8_t* mask, const float* s, size_t N, in
     }
 }
 
+// ---- block OBS (ehap.hpp:502-704) -------------------------------------------
+// Restated with the operation order of the Eigen stand-in the reference oracle
+// is built with (oracle/eigen_subset/Eigen/Dense): products accumulate over the
+// inner index from zero, the K x K system is solved by pivoted LDL^T.
+
+namespace {
+
+// Symmetric LDL^T with diagonal pivoting of a K x K column-major matrix and
+// solve against the identity: Minv = M^-1.
+void ldlt_inverse(std::vector<float>& a, int n, std::vector<float>& inv) {
+    auto at = [&](std::vector<float>& m, int i, int j) -> float& { return m[static_cast<size_t>(j * n + i)]; };
+    std::vector<int> perm(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) perm[static_cast<size_t>(i)] = i;
+    for (int k = 0; k < n; ++k) {
+        int p = k;
+        float best = std::abs(at(a, k, k));
+        for (int i = k + 1; i < n; ++i)
+            if (std::abs(at(a, i, i)) > best) { best = std::abs(at(a, i, i)); p = i; }
+        if (p != k) {
+            std::swap(perm[static_cast<size_t>(k)], perm[static_cast<size_t>(p)]);
+            std::vector<float> full = a, sw(a.size());
+            auto idx = [&](int i) { return i == k ? p : (i == p ? k : i); };
+            for (int j = 0; j < n; ++j)
+                for (int i = 0; i < n; ++i) {
+                    const int x = idx(i), y = idx(j);
+                    if (j < k) at(sw, i, j) = at(full, x, j);
+                    else at(sw, i, j) = (x >= y) ? at(full, x, y) : at(full, y, x);
+                }
+            a = sw;
+        }
+        const float dk = at(a, k, k);
+        if (dk == 0.0f) continue;
+        for (int i = k + 1; i < n; ++i) at(a, i, k) /= dk;
+        for (int j = k + 1; j < n; ++j)
+            for (int i = j; i < n; ++i) at(a, i, j) -= at(a, i, k) * dk * at(a, j, k);
+    }
+    inv.assign(static_cast<size_t>(n * n), 0.0f);
+    std::vector<float> y(static_cast<size_t>(n));
+    for (int c = 0; c < n; ++c) {
+        for (int i = 0; i < n; ++i) y[static_cast<size_t>(i)] = (perm[static_cast<size_t>(i)] == c) ? 1.0f : 0.0f;
+        for (int i = 0; i < n; ++i)
+            for (int k = 0; k < i; ++k) y[static_cast<size_t>(i)] -= at(a, i, k) * y[static_cast<size_t>(k)];
+        for (int i = 0; i < n; ++i) {
+            const float d = at(a, i, i);
+            if (d != 0.0f) y[static_cast<size_t>(i)] /= d;
+        }
+        for (int i = n - 1; i >= 0; --i)
+            for (int k = i + 1; k < n; ++k) y[static_cast<size_t>(i)] -= at(a, k, i) * y[static_cast<size_t>(k)];
+        for (int i = 0; i < n; ++i) at(inv, perm[static_cast<size_t>(i)], c) = y[static_cast<size_t>(i)];
+    }
+}
+
+size_t block_obs(float* w, const float* fdiag, const std::vector<const float*>& hist, size_t N, size_t B,
+                 float sp, float damp, float alpha) {
+    const size_t num_blocks = (N + B - 1) / B;
+    const size_t prune_total = N - static_cast<size_t>(sp * static_cast<float>(N));
+    if (prune_total == 0) return 0;
+    std::vector<float> block_imp(num_blocks, 0.0f);
+    for (size_t b = 0; b < num_blocks; ++b) {
+        const size_t st = b * B, en = std::min(st + B, N);
+        float sum = 0.0f;
+        for (size_t i = st; i < en; ++i) {
+            float fi = damp;
+            if (fdiag) fi += fdiag[i];
+            sum += w[i] * w[i] * fi;
+        }
+        block_imp[b] = sum / static_cast<float>(en - st);
+    }
+    float mx = 0.0f;
+    for (float v : block_imp) if (v > mx) mx = v;
+    if (mx <= 0.0f) mx = 1.0f;
+    std::vector<float> blk_w(num_blocks);
+    const float tau = 4.0f;
+    for (size_t b = 0; b < num_blocks; ++b) blk_w[b] = std::exp(-tau * (block_imp[b] / mx));
+    std::vector<size_t> target(num_blocks, 0);
+    float total_w = 0.0f;
+    for (float v : blk_w) total_w += v;
+    if (total_w <= 0.0f) total_w = 1.0f;
+    size_t allocated = 0;
+    for (size_t b = 0; b < num_blocks; ++b) {
+        const float share = blk_w[b] / total_w;
+        const size_t bs = (b == num_blocks - 1) ? (N - b * B) : B;
+        target[b] = static_cast<size_t>(share * static_cast<float>(prune_total));
+        if (target[b] >= bs) target[b] = bs > 1 ? bs - 1 : 0;
+        allocated += target[b];
+    }
+    std::ptrdiff_t rem = static_cast<std::ptrdiff_t>(prune_total) - static_cast<std::ptrdiff_t>(allocated);
+    for (size_t b = 0; b < num_blocks && rem > 0; ++b) {
+        const size_t rb = num_blocks - 1 - b;
+        const size_t bs = (rb == num_blocks - 1) ? (N - rb * B) : B;
+        while (rem > 0 && target[rb] + 1 < bs) { ++target[rb]; --rem; }
+    }
+    size_t pruned = 0;
+    const int K = hist.empty() ? 1 : static_cast<int>(hist.size());
+    for (size_t b = 0; b < num_blocks; ++b) {
+        const size_t st = b * B, en = std::min(st + B, N), bs = en - st;
+        if (target[b] == 0 || target[b] >= bs) continue;
+        std::vector<float> Dinv(bs), U(bs * static_cast<size_t>(K));  // U column-major (i + k*bs)
+        for (size_t i = 0; i < bs; ++i) {
+            float d = damp;
+            if (fdiag) d += fdiag[st + i];
+            Dinv[i] = (d > 0.0f) ? (1.0f / d) : 1.0f;
+        }
+        if (!hist.empty()) {
+            for (int k = 0; k < K; ++k) {
+                const float age = static_cast<float>(K - 1 - k);
+                const float wk = std::exp(-age / 2.0f);
+                for (size_t i = 0; i < bs; ++i) U[i + static_cast<size_t>(k) * bs] = wk * hist[static_cast<size_t>(k)][st + i];
+            }
+        } else {
+            for (size_t i = 0; i < bs; ++i) U[i] = std::sqrt(alpha) * w[st + i];
+        }
+        // M = I + 1e-8 I + (U^T D^-1) U
+        std::vector<float> M(static_cast<size_t>(K * K), 0.0f);
+        for (int k = 0; k < K; ++k) M[static_cast<size_t>(k * K + k)] = 1.0f;
+        for (int k = 0; k < K; ++k) M[static_cast<size_t>(k * K + k)] += 1e-8f;
+        for (int j = 0; j < K; ++j)
+            for (int i = 0; i < K; ++i) {
+                float acc = 0.0f;
+                for (size_t x = 0; x < bs; ++x)
+                    acc += (U[x + static_cast<size_t>(i) * bs] * Dinv[x]) * U[x + static_cast<size_t>(j) * bs];
+                M[static_cast<size_t>(j * K + i)] += acc;
+            }
+        std::vector<float> Minv;
+        ldlt_inverse(M, K, Minv);
+        // Hinv = D^-1 - D^-1 S D^-1, S = sum_k1 sum_k2 Minv(k1,k2) u_k1 u_k2^T
+        std::vector<float> H(bs * bs);  // column-major
+        for (size_t j = 0; j < bs; ++j)
+            for (size_t i = 0; i < bs; ++i) {
+                float S = 0.0f;
+                for (int k1 = 0; k1 < K; ++k1)
+                    for (int k2 = 0; k2 < K; ++k2)
+                        S += Minv[static_cast<size_t>(k2 * K + k1)] *
+                             (U[i + static_cast<size_t>(k1) * bs] * U[j + static_cast<size_t>(k2) * bs]);
+                const float h0 = (i == j) ? Dinv[i] : 0.0f;
+                H[i + j * bs] = h0 - Dinv[i] * S * Dinv[j];
+            }
+        std::vector<float> wv(w + st, w + en), col(bs);
+        size_t done = 0;
+        while (done < target[b]) {
+            float min_s = std::numeric_limits<float>::max();
+            size_t best = 0;
+            for (size_t i = 0; i < bs; ++i) {
+                const float hii = H[i + i * bs];
+                if (hii <= 0.0f) continue;
+                const float sc = (wv[i] * wv[i]) / hii;
+                if (sc < min_s) { min_s = sc; best = i; }
+            }
+            if (min_s >= std::numeric_limits<float>::max() / 2) break;
+            const float wi_old = wv[best];
+            const float inv_h = 1.0f / H[best + best * bs];
+            for (size_t j = 0; j < bs; ++j)
+                if (j != best) wv[j] -= wi_old * inv_h * H[j + best * bs];
+            wv[best] = 0.0f;
+            const float hbb = H[best + best * bs];
+            for (size_t i = 0; i < bs; ++i) col[i] = H[i + best * bs];
+            for (size_t j = 0; j < bs; ++j)
+                for (size_t i = 0; i < bs; ++i) H[i + j * bs] -= (col[i] * col[j]) / hbb;
+            ++done;
+        }
+        std::copy(wv.begin(), wv.end(), w + st);
+        pruned += done;
+    }
+    return pruned;
+}
+
+}  // namespace
+
+int port_block_obs(float* w_inout, const float* grads, size_t S, const float* hist, size_t K, size_t N,
+                   size_t block, float sparsity, float damping, float off_alpha, float fisher_alpha,
+                   int use_fisher, size_t hist_size, size_t* pruned_out) {
+    Fisher st;
+    for (size_t s = 0; s < S; ++s) {
+        int rc = fisher_step(st, grads + s * N, N, fisher_alpha, 0.99f, use_fisher != 0);
+        if (rc) return 100 + rc;
+    }
+    std::vector<const float*> h;
+    const size_t keep = hist_size;
+    for (size_t k = 0; k < K && keep > 0; ++k) {
+        if (h.size() >= keep) h.erase(h.begin());
+        h.push_back(hist + k * N);
+    }
+    if (N == 0) return 200 + kZeroSize;
+    const size_t B = block ? block : 128;
+    const size_t p = block_obs(w_inout, st.F.empty() ? nullptr : st.F.data(), h, N, B, sparsity, damping, off_alpha);
+    if (pruned_out) *pruned_out = p;
+    return 0;
+}
+
 void port_topn_group(const float* vals, int n, int m, uint8_t* mask_out) {
     *mask_out = topn_group(vals, n, m);
 }

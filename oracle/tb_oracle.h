@@ -42,6 +42,9 @@ void port_decode_half(const uint16_t* in, size_t n, int is_bf16, float* out);
 void port_mock_tensor(size_t N, float* w_out, float* g_out);
 size_t port_near_ties(const float* s, size_t N, int n, int m);
 void port_compensate(float* w, const uint8_t* mask, const float* s, size_t N, int mode);
+int port_block_obs(float* w_inout, const float* grads, size_t S, const float* hist, size_t K, size_t N,
+                   size_t block, float sparsity, float damping, float off_alpha, float fisher_alpha,
+                   int use_fisher, size_t hist_size, size_t* pruned_out);
 void port_topn_group(const float* vals, int n, int m, uint8_t* mask_out);
 
 #ifdef __cplusplus

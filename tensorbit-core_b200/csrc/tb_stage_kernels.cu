@@ -256,3 +256,30 @@ int tb_redistribute(float* weights, const uint8_t* mask, const float* importance
 }
 
 }  // extern "C"
+
+namespace tb {
+namespace {
+template <int DT>
+__global__ void decode_kernel(const void* __restrict__ in, float* __restrict__ out, size_t N) {
+    TB_GRID_STRIDE(i, N) out[i] = Dtype<DT>::load(in, i);
+}
+}  // namespace
+}  // namespace tb
+
+// Safetensors element widening of load_safetensor (src/main.cpp:204-250) on the
+// device: BF16 exactly, F16 with the reference's handling of exponent 0, F32 copied.
+extern "C" int tb_decode_to_f32(const void* in, int dtype, float* out, size_t N, void* stream) {
+    if (N == 0) return TB_OK;
+    if (!in || !out) return fail(TB_ERR_ARG, "tb_decode_to_f32: null pointer");
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    auto st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = grid_for(N);
+    switch (dtype) {
+    case TB_F32: decode_kernel<TB_F32><<<grid, kThreads, 0, st>>>(in, out, N); break;
+    case TB_BF16: decode_kernel<TB_BF16><<<grid, kThreads, 0, st>>>(in, out, N); break;
+    case TB_F16: decode_kernel<TB_F16><<<grid, kThreads, 0, st>>>(in, out, N); break;
+    default: return fail(TB_ERR_ARG, "bad dtype %d", dtype);
+    }
+    return check_launch("decode_kernel");
+}

@@ -102,6 +102,7 @@ def lib() -> C.CDLL:
             "tb_nm_mask_2_4": ([vp, vp, sz, vp], i32),
             "tb_nm_mask_generic": ([vp, vp, sz, i32, i32, vp], i32),
             "tb_apply_mask": ([vp, vp, sz, i32, vp], i32),
+            "tb_decode_to_f32": ([vp, i32, vp, sz, vp], i32),
             "tb_fisher_ema_step": ([vp, vp, i32, sz, f32, f32, i32, vp], i32),
             "tb_importance": ([vp, i32, vp, vp, sz, f32, i32, vp], i32),
             "tb_nm_mask": ([vp, vp, sz, i32, i32, i32, i32, i32, vp], i32),
@@ -110,6 +111,7 @@ def lib() -> C.CDLL:
             "tb_ehap_apply_mask": ([vp, vp, sz, C.POINTER(C.c_uint64), vp], i32),
             "tb_fisher_normalize": ([vp, sz, vp], i32),
             "tb_compensate": ([vp, vp, vp, sz, i32, vp], i32),
+            "tb_block_obs": ([vp, vp, C.POINTER(vp), i32, sz, sz, f32, f32, f32, C.POINTER(C.c_uint64), vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),
             "tb_score_mask_pack_host_noalloc": ([C.POINTER(PruneArgs)], i32),

@@ -9,7 +9,10 @@ sources) on the seeded inputs of tests/inputs.py and records its outputs:
   pass (weights 128x128 FP32, 8 gradient samples, OBD, 2:4) for each mask
   strategy, of the tb-prune mock run's .tb file, of the BF16/F16 decode of all
   65536 bit patterns, plus the documented pins (docs/TODO.md:101,
-  docs/DOCUMENTATION.md:57-70).
+  docs/DOCUMENTATION.md:57-70), and of the files the reference tb-prune CLI
+  writes for the mock variants of tests/inputs.MOCK_RUNS and for the mixed-dtype
+  checkpoint of tests/inputs.small_model (one .tb per tensor + model.tbm).
+  The BlockOBS run uses the reference built with the test-only Eigen stand-in.
 * ties.npz - the reference's top-N masks for every 2:4-family weak-order
   pattern ({0..3}^4 for n = 1, 2, 3) and for 4096 random tie-heavy 8-element
   groups (n = 1, 2, 4, 6), the cases where std::nth_element's tie order decides.
@@ -88,6 +91,21 @@ def main():
     # Error behaviour of generate_nm_mask (coring.hpp:94-100,321-330).
     cases = [(0, 0, 2, 4), (8, 4, 2, 4), (6, 6, 2, 4), (8, 8, 4, 4), (8, 8, 0, 4), (8, 8, 2, 0)]
     out["mask_status"] = [[*c, R.nm_mask_status(*c)] for c in cases]
+
+    # tb-prune runs of the reference CLI: mock variants and a real-mode checkpoint.
+    runs = {}
+    with tempfile.TemporaryDirectory() as d:
+        for key, args in inputs.MOCK_RUNS.items():
+            path = os.path.join(d, key + ".tb")
+            subprocess.run([REF_CLI, *args, "--output", path], check=True, capture_output=True)
+            runs[key] = sha(open(path, "rb").read())
+        model = os.path.join(d, "model.safetensors")
+        inputs.small_model(model)
+        outdir = os.path.join(d, "out")
+        subprocess.run([REF_CLI, "--model", model, "--output", outdir], check=True, capture_output=True)
+        real = {name: sha(open(os.path.join(outdir, name), "rb").read()) for name in sorted(os.listdir(outdir))}
+    out["tb_prune_mock_runs"] = runs
+    out["tb_prune_real_small_model"] = real
 
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)

@@ -46,3 +46,50 @@ def to_bf16_bits(x):
 
 def bf16_bits_to_f32(b):
     return (np.asarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def write_safetensors(path, tensors):
+    """Writes a .safetensors file: tensors is a list of (name, dtype, shape, raw bytes)."""
+    import json
+    import struct
+    header, off, blobs = {}, 0, []
+    for name, dtype, shape, raw in tensors:
+        header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [off, off + len(raw)]}
+        off += len(raw)
+        blobs.append(raw)
+    text = json.dumps(header, separators=(",", ":")).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(text)))
+        f.write(text)
+        for b in blobs:
+            f.write(b)
+
+
+def small_model(path):
+    """Deterministic mixed-dtype checkpoint for the real-mode tb-prune runs."""
+    q = normal(64 * 64, 0.02, 201)
+    up = to_bf16_bits(normal(128 * 64, 0.02, 202))
+    down = normal(64 * 128, 0.02, 203).astype(np.float16).view(np.uint16)
+    norm = normal(62, 1.0, 204)
+    head = normal(32 * 64, 0.02, 205)
+    tokens = np.arange(10, dtype=np.int64)
+    write_safetensors(path, [
+        ("model.layers.0.self_attn.q_proj.weight", "F32", (64, 64), q.tobytes()),
+        ("model.layers.0.mlp.up_proj.weight", "BF16", (128, 64), up.tobytes()),
+        ("model.layers.0.mlp.down_proj.weight", "F16", (64, 128), down.tobytes()),
+        ("model.norm.weight", "F32", (62,), norm.tobytes()),
+        ("tokens", "I64", (10,), tokens.tobytes()),
+        ("lm_head.weight", "F32", (32, 64), head.tobytes()),
+    ])
+
+
+MOCK_RUNS = {
+    "oneshot_2of4": ["--mock-size", "16384", "--sparsity", "2:4"],
+    "iterative_2of4": ["--mock-size", "16384", "--sparsity", "2:4", "--strategy", "Iterative"],
+    "blockobs_2of4": ["--mock-size", "16384", "--sparsity", "2:4", "--strategy", "BlockOBS"],
+    "magnitude_2of4": ["--mock-size", "16384", "--sparsity", "2:4", "--method", "Magnitude"],
+    "oneshot_1of4": ["--mock-size", "8192", "--sparsity", "1:4"],
+    "oneshot_2of8": ["--mock-size", "8192", "--sparsity", "2:8"],
+    "oneshot_4of8": ["--mock-size", "8192", "--sparsity", "4:8"],
+    "damping_10000": ["--mock-size", "10000", "--sparsity", "2:4", "--damping", "0.05"],
+}

@@ -204,3 +204,17 @@ def test_port_vs_reference_tie_heavy_pipeline(port, ref):
             assert a[0] == b[0] and a[5:] == b[5:]
             for x, y in zip(a[1:5], b[1:5]):
                 assert same(x, y)
+
+
+@pytest.mark.parametrize("N,block,K,S,use_fisher,sp", [
+    (1024, 128, 4, 1, True, 0.5), (1000, 128, 4, 2, True, 0.5), (4096, 128, 0, 1, True, 0.5),
+    (2048, 64, 2, 3, True, 0.3), (777, 100, 4, 1, True, 0.5), (4096, 128, 4, 1, False, 0.5),
+    (5000, 224, 3, 1, True, 0.7), (3000, 32, 1, 1, True, 0.9)])
+def test_port_vs_reference_block_obs(port, ref, N, block, K, S, use_fisher, sp):
+    w = inputs.normal(N, 0.5, N)
+    g = inputs.normal((S, N), 0.05, N + 1)
+    hist = (np.stack([g[0] * (np.float32(0.9) + np.float32(0.02) * np.float32(k)) for k in range(K)])
+            .astype(np.float32) if K else None)
+    a = port.block_obs(w, g, hist, block=block, sparsity=sp, use_fisher=use_fisher, hist_size=max(K, 1))
+    b = ref.block_obs(w, g, hist, block=block, sparsity=sp, use_fisher=use_fisher, hist_size=max(K, 1))
+    assert a[0] == b[0] == 0 and a[2] == b[2] and same(a[1], b[1])
