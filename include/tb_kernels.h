@@ -102,6 +102,15 @@ int tb_decode_to_f32(const void* in, int dtype, float* out, size_t N, void* stre
  * F = beta*F + ((alpha*(1-beta))*g)*g with the reference's float rounding. */
 int tb_fisher_ema_step(float* fisher, const void* gradients, int g_dtype, size_t N, float alpha,
                        float beta, int first_step, void* stream);
+/* Sample-split Fisher: F (+)= sum_s weights[s] * g_s^2 over S samples of dtype
+ * g_dtype ([S][g_stride], g_stride 0 = N); weights is a host array.  With the
+ * EMA weights c_0 = alpha beta^(S-1), c_t = alpha (1-beta) beta^(S-1-t) this is
+ * the accumulate_fisher recurrence (ehap.hpp:190-197) regrouped, so ranks holding
+ * disjoint samples can sum their partials with one all-reduce.  Agrees with the
+ * serial recurrence to FP32 rounding (different association), not bit for bit.
+ * accumulate == 0 overwrites F. */
+int tb_fisher_weighted_sum(float* fisher, const void* gradients, int g_dtype, size_t S, size_t g_stride,
+                           size_t N, const float* weights, int accumulate, void* stream);
 /* EHAPPruner::compute_importance (ehap.hpp:206-285) for all three modes; F may be
  * NULL (no Fisher state: s = w*w).  Weights of dtype w_dtype are widened as the
  * reference's safetensors loader does (src/main.cpp:213-245). */

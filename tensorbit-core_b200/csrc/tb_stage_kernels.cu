@@ -283,3 +283,63 @@ extern "C" int tb_decode_to_f32(const void* in, int dtype, float* out, size_t N,
     }
     return check_launch("decode_kernel");
 }
+
+// ---- sample-split Fisher partial sums ----------------------------------------
+// When calibration samples are split across ranks, the EMA
+//   F_S = beta F_{S-1} + (alpha (1-beta)) g_{S-1}^2,  F_1 = alpha g_0^2
+// is rewritten as the weighted sum F = sum_t c_t g_t^2 with
+//   c_0 = alpha beta^(S-1),  c_t = alpha (1-beta) beta^(S-1-t)  (t >= 1),
+// which each rank evaluates over its own samples before one all-reduce.  The
+// association differs from the serial recurrence, so F agrees with it to
+// FP32 rounding, not bit for bit.
+namespace tb {
+namespace {
+constexpr int kMaxWeights = 64;
+struct SampleWeights {
+    float c[kMaxWeights];
+};
+
+template <int GDT>
+__global__ void weighted_sq_sum_kernel(float* __restrict__ F, const void* __restrict__ g, size_t S, size_t gstride,
+                                       size_t N, SampleWeights cw, int accumulate) {
+    TB_GRID_STRIDE(i, N) {
+        float acc = accumulate ? F[i] : 0.0f;
+        for (size_t s = 0; s < S; ++s) {
+            const float x = Dtype<GDT>::load(g, s * gstride + i);
+            acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(cw.c[s], x), x));
+        }
+        F[i] = acc;
+    }
+}
+}  // namespace
+}  // namespace tb
+
+extern "C" int tb_fisher_weighted_sum(float* fisher, const void* gradients, int g_dtype, size_t S, size_t g_stride,
+                                      size_t N, const float* weights_host, int accumulate, void* stream) {
+    if (N == 0) return TB_OK;
+    if (!fisher || (S && (!gradients || !weights_host))) return fail(TB_ERR_ARG, "tb_fisher_weighted_sum: null pointer");
+    if (g_dtype < TB_F32 || g_dtype > TB_BF16) return fail(TB_ERR_ARG, "bad gradient dtype %d", g_dtype);
+    const size_t stride = g_stride ? g_stride : N;
+    if (stride < N) return fail(TB_ERR_ARG, "g_stride < N");
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    auto st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = grid_for(N);
+    const int esize = g_dtype == TB_F32 ? 4 : 2;
+    size_t done = 0;
+    do {  // batches of up to 64 samples, the first overwriting unless accumulating
+        const size_t n = std::min<size_t>(S - done, kMaxWeights);
+        SampleWeights cw{};
+        for (size_t k = 0; k < n; ++k) cw.c[k] = weights_host[done + k];
+        const void* gp = S ? static_cast<const char*>(gradients) + done * stride * esize : gradients;
+        const int acc = (done > 0 || accumulate) ? 1 : 0;
+        switch (g_dtype) {
+        case TB_F32: weighted_sq_sum_kernel<TB_F32><<<grid, kThreads, 0, st>>>(fisher, gp, n, stride, N, cw, acc); break;
+        case TB_BF16: weighted_sq_sum_kernel<TB_BF16><<<grid, kThreads, 0, st>>>(fisher, gp, n, stride, N, cw, acc); break;
+        default: weighted_sq_sum_kernel<TB_F16><<<grid, kThreads, 0, st>>>(fisher, gp, n, stride, N, cw, acc); break;
+        }
+        if ((rc = check_launch("weighted_sq_sum_kernel"))) return rc;
+        done += n;
+    } while (done < S);
+    return TB_OK;
+}

@@ -103,6 +103,7 @@ def lib() -> C.CDLL:
             "tb_nm_mask_generic": ([vp, vp, sz, i32, i32, vp], i32),
             "tb_apply_mask": ([vp, vp, sz, i32, vp], i32),
             "tb_decode_to_f32": ([vp, i32, vp, sz, vp], i32),
+            "tb_fisher_weighted_sum": ([vp, vp, i32, sz, sz, sz, vp, i32, vp], i32),
             "tb_fisher_ema_step": ([vp, vp, i32, sz, f32, f32, i32, vp], i32),
             "tb_importance": ([vp, i32, vp, vp, sz, f32, i32, vp], i32),
             "tb_nm_mask": ([vp, vp, sz, i32, i32, i32, i32, i32, vp], i32),

@@ -1,0 +1,155 @@
+"""Multi-GPU pruning: one process per GPU, torch.distributed for the plumbing.
+
+Two ways to spread one tensor's pass over P ranks (the reference has none; its
+docs prune shards in separate processes, docs/CLOUD.md:155-170):
+
+* **group sharding** (`prune_group_sharded`): rank r owns a contiguous range of
+  N:M groups (row blocks of the matrix).  Groups are independent, so each rank
+  runs the fused pass on its range with no communication and writes its slice
+  of the shared `.tb` file in place: weights at 4096 + 4*e0, mask bytes at
+  masks_offset + e0/M.  Results are bit-identical to a single-GPU pass.
+* **sample splitting** (`prune_sample_split`): rank r holds a subset of the S
+  calibration gradients for all elements.  The EMA recurrence
+  F_S = beta F_{S-1} + alpha (1-beta) g^2 (ehap.hpp:190-197) is regrouped as
+  F = sum_t c_t g_t^2; each rank sums its own samples (tb_fisher_weighted_sum),
+  one NCCL all-reduce adds the partials over NVLink, and every rank then scores,
+  masks and packs its group range from the summed Fisher.  F matches the serial
+  recurrence to FP32 rounding (the association differs), so masks can differ
+  only in near-tie groups, which the pass counts.
+
+Ranks read RANK / WORLD_SIZE / LOCAL_RANK from the environment like torchrun.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+import os
+
+import numpy as np
+
+import tbabi as tb
+
+TB_HEADER = 4096
+
+
+def group_shard(N: int, m: int, world: int, rank: int) -> tuple[int, int]:
+    """Element range [e0, e1) of `rank`: contiguous, balanced by whole units of
+    lcm(M, 16) elements (so every rank but the last keeps the 16-element vector
+    path aligned); the last rank also takes the ragged tail."""
+    if N % m:
+        raise ValueError(f"numel {N} not divisible by M={m}")
+    unit = m * 16 // math.gcd(m, 16)
+    units = N // unit
+    e0 = units * rank // world * unit
+    e1 = units * (rank + 1) // world * unit if rank < world - 1 else N
+    return e0, e1
+
+
+def sample_shard(S: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous sample range [s0, s1) of `rank`."""
+    return S * rank // world, S * (rank + 1) // world
+
+
+def ema_weights(S: int, alpha: float, beta: float) -> np.ndarray:
+    """c_t such that sum_t c_t g_t^2 equals S steps of accumulate_fisher:
+    c_0 = alpha beta^(S-1), c_t = alpha (1-beta) beta^(S-1-t) for t >= 1, with
+    alpha (1-beta) formed in FP32 as the reference does (ehap.hpp:164-165,195)."""
+    a, b = np.float32(alpha), np.float32(beta)
+    contrib = np.float32(a * (np.float32(1.0) - b))
+    c = np.empty(S, np.float32)
+    for t in range(S):
+        powb = float(b) ** (S - 1 - t)
+        c[t] = np.float32((float(a) if t == 0 else float(contrib)) * powb)
+    return c
+
+
+def tb_header(n: int, m: int, num_weights: int) -> bytes:
+    """The 4096-byte .tb header TBWriter writes for FP32 weights
+    (serialization.hpp:30-54,115-134)."""
+    h = bytearray(TB_HEADER)
+    num_mask = num_weights // m
+    fields = [(0, "<I", 0x31304254), (4, "<I", 1), (8, "<I", n), (12, "<I", m), (16, "<Q", num_weights),
+              (24, "<Q", num_mask), (32, "<Q", TB_HEADER), (40, "<Q", TB_HEADER + 4 * num_weights)]
+    import struct
+    for off, fmt, v in fields:
+        struct.pack_into(fmt, h, off, v)
+    h[48] = 0
+    return bytes(h)
+
+
+def create_tb(path: str, N: int, n: int, m: int) -> None:
+    """Rank 0: writes the header and sizes the file so ranks can fill their slices."""
+    with open(path, "wb") as f:
+        f.write(tb_header(n, m, N))
+        f.truncate(TB_HEADER + 4 * N + N // m)
+
+
+def write_tb_slice(path: str, N: int, m: int, e0: int, w_out: np.ndarray, mask: np.ndarray) -> None:
+    """Writes one rank's weights and mask bytes at their offsets in the .tb."""
+    fd = os.open(path, os.O_WRONLY)
+    try:
+        os.pwrite(fd, np.ascontiguousarray(w_out, np.float32).tobytes(), TB_HEADER + 4 * e0)
+        os.pwrite(fd, np.ascontiguousarray(mask, np.uint8).tobytes(), TB_HEADER + 4 * N + e0 // m)
+    finally:
+        os.close(fd)
+
+
+def _check(rc: int) -> None:
+    tb.check(rc)
+
+
+def prune_group_sharded(dist, w: np.ndarray, w_dtype: int, g: np.ndarray, g_dtype: int, out_path: str, *,
+                        n=2, m=4, **cfg) -> dict:
+    """Group-sharded pass of one tensor held in host memory on every rank
+    (w [N], g [S, N]); each rank prunes its range through the host-buffer entry
+    and writes its slice of `out_path`.  Returns this rank's counters."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    N = w.size
+    S = g.shape[0] if g is not None and g.size else 0
+    e0, e1 = group_shard(N, m, world, rank)
+    if rank == 0:
+        create_tb(out_path, N, n, m)
+    dist.barrier()
+    L = e1 - e0
+    w_out = np.empty(L, np.float32)
+    mask = np.empty(L // m, np.uint8)
+    ties = np.zeros(1, np.uint64)
+    wsz = 4 if w_dtype == tb.F32 else 2
+    gsz = 4 if g_dtype == tb.F32 else 2
+    if L:
+        a = tb.prune_args(weights=w.ctypes.data + e0 * wsz, w_dtype=w_dtype,
+                          grads=(g.ctypes.data + e0 * gsz) if S else None, g_dtype=g_dtype, S=S, N=L,
+                          g_stride=N if S else 0, n=n, m=m, w_out=w_out.ctypes.data, mask_out=mask.ctypes.data,
+                          near_ties=ties.ctypes.data, **cfg)
+        _check(tb.score_mask_pack_host(a))
+        write_tb_slice(out_path, N, m, e0, w_out, mask)
+    dist.barrier()
+    return {"e0": e0, "e1": e1, "near_ties": int(ties[0])}
+
+
+def prune_sample_split(dist, torch, w_dev, w_dtype: int, g_local_dev, g_dtype: int, S_total: int, s0: int,
+                       out_w, out_mask, *, n=2, m=4, alpha=0.01, beta=0.99, fisher_out=None, **cfg) -> dict:
+    """Sample-split pass of one tensor on the device: g_local_dev holds this
+    rank's samples [s0, s0 + S_local) of all N elements.  Partial Fisher, NCCL
+    all-reduce (sum), then the fused pass over this rank's group range from the
+    summed Fisher.  out_w / out_mask are full-size device tensors; this rank
+    fills [e0, e1).  Returns the range and near-tie count."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    N = w_dev.numel()
+    S_local = g_local_dev.shape[0] if g_local_dev is not None else 0
+    stream = torch.cuda.current_stream().cuda_stream
+    F = fisher_out if fisher_out is not None else torch.empty(N, dtype=torch.float32, device=w_dev.device)
+    c = ema_weights(S_total, alpha, beta)[s0:s0 + S_local].copy()
+    _check(tb.lib().tb_fisher_weighted_sum(F.data_ptr(), g_local_dev.data_ptr() if S_local else None, g_dtype,
+                                           S_local, N, N, c.ctypes.data if S_local else None, 0, stream))
+    dist.all_reduce(F)
+    e0, e1 = group_shard(N, m, world, rank)
+    ties = torch.zeros(1, dtype=torch.int64, device=w_dev.device)
+    if e1 > e0:
+        wsz = w_dev.element_size()
+        a = tb.prune_args(weights=w_dev.data_ptr() + e0 * wsz, w_dtype=w_dtype, grads=None, g_dtype=g_dtype, S=0,
+                          N=e1 - e0, fisher_in=F.data_ptr() + 4 * e0, fisher_steps_in=S_total, alpha=alpha, beta=beta,
+                          n=n, m=m, w_out=out_w.data_ptr() + 4 * e0, mask_out=out_mask.data_ptr() + e0 // m,
+                          near_ties=ties.data_ptr(), **cfg)
+        _check(tb.score_mask_pack(a, stream))
+    return {"e0": e0, "e1": e1, "near_ties": ties, "fisher": F}

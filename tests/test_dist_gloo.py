@@ -1,0 +1,103 @@
+"""CPU: the multi-rank host logic of tensorbit-core_b200/tbdist.py with two gloo
+ranks (no GPU).  The kernels themselves are exercised by test_gpu_dist.py;
+here the per-rank results are produced by the oracle, so what is checked is
+the sharding plan, the regrouped EMA weights with the all-reduce, and the .tb
+assembled from slices written by different processes."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import inputs
+import tbdist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+
+@pytest.mark.parametrize("N,m", [(4096, 4), (4100, 4), (64, 4), (16384 + 8, 8), (96, 2), (7 * 48, 3)])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_group_shards_cover_and_align(N, m, world):
+    ranges = [tbdist.group_shard(N, m, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == N
+    unit = m * 16 // np.gcd(m, 16)
+    for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+        assert a1 == b0
+    for r, (e0, e1) in enumerate(ranges):
+        assert e0 <= e1 and e0 % unit == 0 and (e1 - e0) % m == 0
+        if r < world - 1:
+            assert e1 % unit == 0
+
+
+def test_ema_weights_equal_the_recurrence(port):
+    g = inputs.normal((64, 5000), 1e-3, 3)
+    rc, F = port.fisher(g, alpha=0.01, beta=0.99)
+    c = tbdist.ema_weights(64, 0.01, 0.99).astype(np.float64)
+    Fw = (c[:, None] * g.astype(np.float64) ** 2).sum(0)
+    assert rc == 0
+    np.testing.assert_allclose(Fw, F, rtol=1e-5, atol=0)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port_no, tmpdir, results):
+    sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tensorbit-core_b200"), HERE]
+    import torch
+    import torch.distributed as dist
+    import inputs as inp
+    import tbdist as td
+    from oracle import Oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    O = Oracle("port")
+    # --- sample split: partial sums over this rank's samples, all-reduced ---
+    S, N = 32, 6000
+    g = inp.normal((S, N), 1e-3, 11)
+    s0, s1 = td.sample_shard(S, world, rank)
+    c = td.ema_weights(S, 0.01, 0.99)
+    part = np.zeros(N, np.float32)
+    for t in range(s0, s1):
+        part = (part + (c[t] * g[t]) * g[t]).astype(np.float32)
+    F = torch.from_numpy(part)
+    dist.all_reduce(F)
+    results[f"F{rank}"] = F.numpy().copy()
+    # --- group sharding: each rank writes its slice of one .tb ---
+    w, gg = inp.cfg1()
+    path = os.path.join(tmpdir, "sharded.tb")
+    N2, m = w.size, 4
+    e0, e1 = td.group_shard(N2, m, world, rank)
+    if rank == 0:
+        td.create_tb(path, N2, 2, m)
+    dist.barrier()
+    rc, wp, mk, *_ = O.pipeline(w[e0:e1], gg[:, e0:e1], strategy="optimal", redist="proportional")
+    assert rc == 0
+    td.write_tb_slice(path, N2, m, e0, wp, mk)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gloo_ranks(port, tmp_path):
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), results), nprocs=2, join=True,
+                       start_method="spawn")
+    # all-reduced partial sums == the serial EMA within FP32 rounding, same on both ranks
+    g = inputs.normal((32, 6000), 1e-3, 11)
+    rc, F = port.fisher(g)
+    assert np.array_equal(results["F0"], results["F1"])
+    np.testing.assert_allclose(results["F0"], F, rtol=1e-5, atol=0)
+    # the .tb assembled from two ranks' slices == the single-process file
+    w, gg = inputs.cfg1()
+    rc, wp, mk, *_ = port.pipeline(w, gg, strategy="optimal", redist="proportional")
+    assert open(tmp_path / "sharded.tb", "rb").read() == port.tb_bytes(wp, mk, 2, 4)

@@ -1,0 +1,95 @@
+"""GPU, two or more devices: group sharding and NCCL sample splitting of one
+tensor's pass (tensorbit-core_b200/tbdist.py), checked against the single-GPU
+pass.  Group sharding must give the identical .tb file; sample splitting must
+give a Fisher within 1e-5 relative and masks equal outside near-tie groups."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+import inputs
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port_no, tmpdir):
+    sys.path[:0] = [os.path.join(ROOT, "tensorbit-core_b200"), HERE]
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    import inputs as inp
+    import tbabi as tb
+    import tbdist as td
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    # group sharding through the host-buffer entry, one shared .tb
+    w = inp.normal(1 << 20, 0.02, 5)
+    g = inp.to_bf16_bits(inp.normal((8, 1 << 20), 1e-3, 6))
+    td.prune_group_sharded(dist, w, tb.F32, g, tb.BF16, os.path.join(tmpdir, "group.tb"), strategy="optimal")
+    # sample splitting on the device: rank r holds samples [s0, s1) of all elements
+    S, N = 16, 1 << 20
+    wd = torch.from_numpy(inp.to_bf16_bits(inp.normal(N, 0.02, 7)).view(np.int16)).cuda()
+    gall = inp.to_bf16_bits(inp.normal((S, N), 1e-3, 8))
+    s0, s1 = td.sample_shard(S, world, rank)
+    gd = torch.from_numpy(np.ascontiguousarray(gall[s0:s1]).view(np.int16)).cuda()
+    out_w = torch.zeros(N, dtype=torch.float32, device="cuda")
+    out_m = torch.zeros(N // 4, dtype=torch.uint8, device="cuda")
+    r = td.prune_sample_split(dist, torch, wd, tb.BF16, gd, tb.BF16, S, s0, out_w, out_m, strategy="optimal",
+                              redist="proportional", mode="obd")
+    torch.cuda.synchronize()
+    e0, e1 = r["e0"], r["e1"]
+    np.save(os.path.join(tmpdir, f"ss_w{rank}.npy"), out_w[e0:e1].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"ss_m{rank}.npy"), out_m[e0 // 4:e1 // 4].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"ss_F{rank}.npy"), r["fisher"].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"ss_t{rank}.npy"), np.array([int(r["near_ties"].item()), e0, e1]))
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+
+
+def test_two_rank_group_shard_and_sample_split(cuda, tblib, port, tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    # group sharding: identical file to one process
+    w = inputs.normal(1 << 20, 0.02, 5)
+    gbits = inputs.to_bf16_bits(inputs.normal((8, 1 << 20), 1e-3, 6))
+    rc, wp, mk, *_ = port.pipeline(w, inputs.bf16_bits_to_f32(gbits), strategy="optimal", redist="proportional")
+    assert rc == 0
+    assert open(tmp_path / "group.tb", "rb").read() == port.tb_bytes(wp, mk, 2, 4)
+    # sample splitting: Fisher within 1e-5 relative; masks equal outside near-ties
+    S, N = 16, 1 << 20
+    w32 = inputs.bf16_bits_to_f32(inputs.to_bf16_bits(inputs.normal(N, 0.02, 7)))
+    g32 = inputs.bf16_bits_to_f32(inputs.to_bf16_bits(inputs.normal((S, N), 1e-3, 8)))
+    rc, wo, mo, Fo, so, *_ = port.pipeline(w32, g32, strategy="optimal", redist="proportional")
+    F0 = np.load(tmp_path / "ss_F0.npy")
+    assert np.array_equal(F0, np.load(tmp_path / "ss_F1.npy"))
+    np.testing.assert_allclose(F0, Fo, rtol=1e-5, atol=0)
+    masks = np.concatenate([np.load(tmp_path / f"ss_m{r}.npy") for r in range(world)])
+    wgot = np.concatenate([np.load(tmp_path / f"ss_w{r}.npy") for r in range(world)])
+    differ = masks != mo
+    srt = -np.sort(-so.reshape(-1, 4), axis=1)
+    a, b = srt[:, 1], srt[:, 2]
+    near = np.abs(a - b) <= np.float32(1e-6) * np.maximum(np.abs(a), np.finfo(np.float32).tiny)
+    assert not (differ & ~near).any(), "a mask differs outside the near-tie groups"
+    same = np.repeat(~differ, 4)
+    assert np.array_equal(wgot[same], wo[same])
