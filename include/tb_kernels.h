@@ -159,6 +159,47 @@ int tb_block_obs(float* weights, const float* fisher, const float* const* hist, 
                  size_t block, float sparsity, float damping, float off_diag_alpha, uint64_t* pruned_out,
                  void* stream);
 
+/* ---- stage 3 building blocks: tcgen05 tensor-core GEMM (sm_100a) --------- */
+/* Splits x into hi = tf32(x) (round to nearest) and lo = x - hi, the operand
+ * form of the FP32-accurate TF32 GEMM below. */
+int tb_split_tf32(const float* x, float* hi, float* lo, size_t n, void* stream);
+/* C[M,N] = alpha * A[M,K] * B[N,K]^T + beta * Cin, A and B row-major FP32 given
+ * as hi/lo pairs (tb_split_tf32); products hi*hi + hi*lo + lo*hi on TF32 tensor
+ * cores with FP32 accumulation in tensor memory.  M, N multiples of 128, K of 32;
+ * 16-byte aligned operands with ld*4 % 16 == 0.  lower_only computes only the
+ * 128x128 tiles on or below the diagonal. */
+int tb_gemm_nt_tf32x3(const float* a_hi, const float* a_lo, long long lda, const float* b_hi,
+                      const float* b_lo, long long ldb, int M, int N, int K, float alpha, float beta,
+                      const float* c_in, long long ldcin, float* c, long long ldc, int lower_only,
+                      void* stream);
+/* Same with BF16 operands (K a multiple of 64), FP32 accumulation. */
+int tb_gemm_nt_bf16(const void* a, long long lda, const void* b, long long ldb, int M, int N, int K,
+                    float alpha, float beta, const float* c_in, long long ldcin, float* c, long long ldc,
+                    int lower_only, void* stream);
+/* TB_ERR_TIMEOUT if a bounded pipeline wait inside a GEMM launched since the
+ * last call expired (the kernel then skipped its output); synchronises. */
+int tb_gemm_status(void* stream);
+
+/* ---- stage 3: column-block exact OBS against calibration activations ----- */
+/* No counterpart in the reference (docs/EHAP.md:248-250 lists activation
+ * Hessians as missing); the OBS saliency and update follow ehap.hpp:683-691.
+ * H = X^T X / n from X^T given as BF16 [d][n] (row-major, d % 128 == 0,
+ * n % 64 == 0); only the 128x128 tiles on or below the diagonal are written. */
+int tb_obs_hessian(const void* xt_bf16, int d, int n, float* H, void* stream);
+/* Prunes W [r][d] (FP32, in place; r, d multiples of 128) to N:4 against H
+ * (lower tiles valid, e.g. from tb_obs_hessian): lambda = damp_frac *
+ * mean(diag H) is added to the diagonal, U = chol_upper((H + lambda I)^-1) is
+ * formed on tensor cores (3xTF32 tcgen05 GEMMs), and columns are processed in
+ * blocks of 128: per group of 4 the 4 - n_keep smallest w^2 / U_qq^2 are
+ * pruned, each column's error updates the rest of its block, and the block's
+ * errors update the remaining columns through one tcgen05 GEMM.  mask gets
+ * r*d/4 bytes (bit k = keep column 4g+k, the .tb convention).  ut_out (d x d,
+ * may be NULL) receives U^T.  Workspace ~11 d^2 floats is allocated
+ * stream-ordered.  Synchronises the stream.  TB_ERR_CONFIG if H + lambda I is
+ * not positive definite in FP32. */
+int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float damp_frac, int n_keep, int m,
+                     uint8_t* mask, float* ut_out, void* stream);
+
 /* ---- fused score -> mask -> pack pass ------------------------------------ */
 /* One pass over a tensor: Fisher EMA over S gradient samples, importance,
  * CORING N:M mask, apply, redistribution, and emission of the .tb weight and

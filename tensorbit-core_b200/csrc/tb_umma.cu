@@ -1,0 +1,472 @@
+// tcgen05 NT GEMM for sm_100a (see tb_umma.cuh for the contract).
+//
+// Descriptor encodings follow the sm100 UMMA definitions (matrix descriptor:
+// start address >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride
+// byte offset >> 4 in 32-45, version 1 in 46-47, layout type in 61-63 with
+// 2 = 128-byte swizzle; instruction descriptor: D format bits 4-5, A/B formats
+// bits 7-9 / 10-12, K-major bits 15/16 = 0, N >> 3 in bits 17-22, M >> 4 in
+// bits 24-28).  Operand tiles are 128 rows x 128 bytes loaded by TMA with the
+// 128-byte swizzle, which is the canonical K-major SW128 layout: 8-row groups
+// 1024 bytes apart (SBO = 64), and each 32-byte K step of one MMA is a +2
+// advance of the descriptor's start address.
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "tb_runtime.h"
+#include "tb_umma.cuh"
+
+namespace tb {
+namespace umma {
+namespace {
+
+constexpr int kTile = 128;              // rows of A / B per tile, M = N = 128
+constexpr int kTileBytes = kTile * 128; // one 128-row x 128-byte operand slice
+constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
+
+__device__ int g_umma_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Bounded wait for the barrier phase `parity` to complete.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.b32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (globaltimer() - t0 > kWaitNs) return false;
+    }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+template <int KIND>
+__device__ __forceinline__ void mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    if constexpr (KIND == kTF32x3) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+            ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+            ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u));
+    }
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+__device__ __forceinline__ float tf32_hi(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// Warps 0-3 accumulate and store the tile (warp w owns TMEM lanes / rows
+// 32w..32w+31), warp 4 lane 0 issues TMA, warp 5 lane 0 issues tcgen05.mma.
+// The tensor core's FP32 accumulation truncates, so the K loop is cut into
+// groups of kGroup 128-byte slices: each group accumulates in one of two TMEM
+// buffers, and warps 0-3 add the finished buffer into FP32 registers (round to
+// nearest) while the next group runs in the other buffer.
+constexpr int kGroup = 4;
+constexpr int kThreadsGemm = 192;
+
+template <int KIND, int STAGES>
+__global__ void __launch_bounds__(kThreadsGemm, 1)
+gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
+               const __grid_constant__ CUtensorMap tB0, const __grid_constant__ CUtensorMap tB1, const int nk,
+               const GemmOut out) {
+    const int tm = blockIdx.y, tn = blockIdx.x;
+    if (out.lower_only && tn > tm) return;
+    constexpr int kOps = (KIND == kTF32x3) ? 4 : 2;
+    constexpr int kElems = (KIND == kTF32x3) ? 32 : 64;  // K elements per 128-byte slice
+    constexpr uint32_t kFmt = (KIND == kTF32x3) ? 2u : 1u;
+    constexpr uint32_t kIdesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((kTile >> 3) << 17) | ((kTile >> 4) << 24);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kOps * kTileBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accfull = empty + STAGES;   // [2] group finished in TMEM buffer b
+    uint64_t* accempty = accfull + 2;     // [2] buffer b drained by warps 0-3
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ngroups = (nk + kGroup - 1) / kGroup;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&accfull[b]), 1);
+            mbar_init(smem_u32(&accempty[b]), 4);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(2 * kTile));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto tile = [&](int s, int op) { return smem_u32(smem + (s * kOps + op) * kTileBytes); };
+
+    if (warp == 4) {
+        if (lane == 0) {  // TMA producer
+            int issued = 0;
+            for (int kc = 0; kc < nk; ++kc) {
+                const int s = kc % STAGES;
+                if (kc >= STAGES && !mbar_wait(smem_u32(&empty[s]), ((kc / STAGES) - 1) & 1)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                if (*abort_flag) break;
+                const uint32_t bar = smem_u32(&full[s]);
+                mbar_expect_tx(bar, kOps * kTileBytes);
+                const int x = kc * kElems;
+                tma_load_2d(tile(s, 0), &tA0, x, tm * kTile, bar);
+                tma_load_2d(tile(s, 1), &tB0, x, tn * kTile, bar);
+                if constexpr (KIND == kTF32x3) {
+                    tma_load_2d(tile(s, 2), &tA1, x, tm * kTile, bar);
+                    tma_load_2d(tile(s, 3), &tB1, x, tn * kTile, bar);
+                }
+                issued = kc + 1;
+            }
+            // Bounded drain of loads still in flight after an abort.
+            if (*abort_flag)
+                for (int kc = std::max(0, issued - STAGES); kc < issued; ++kc)
+                    mbar_wait(smem_u32(&full[kc % STAGES]), (kc / STAGES) & 1);
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        if (lane == 0) {  // MMA issuer
+            bool ok = true;
+            for (int g = 0; g < ngroups && ok; ++g) {
+                const int b = g & 1;
+                if (g >= 2 && !mbar_wait(smem_u32(&accempty[b]), ((g >> 1) - 1) & 1)) { ok = false; break; }
+                fence_after();
+                const uint32_t acc_t = tmem + static_cast<uint32_t>(b * kTile);
+                const int k_end = std::min(nk, (g + 1) * kGroup);
+                for (int kc = g * kGroup; kc < k_end; ++kc) {
+                    const int s = kc % STAGES;
+                    if (*abort_flag || !mbar_wait(smem_u32(&full[s]), (kc / STAGES) & 1)) { ok = false; break; }
+                    fence_after();
+                    const uint64_t a0 = sw128_desc(tile(s, 0)), b0 = sw128_desc(tile(s, 1));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t adv = static_cast<uint64_t>(kk * 2);  // +32 bytes along K
+                        const uint32_t acc = (kc != g * kGroup || kk) ? 1u : 0u;
+                        if constexpr (KIND == kTF32x3) {
+                            const uint64_t a1 = sw128_desc(tile(s, 2)), b1 = sw128_desc(tile(s, 3));
+                            mma<KIND>(acc_t, a0 + adv, b1 + adv, kIdesc, acc);
+                            mma<KIND>(acc_t, a1 + adv, b0 + adv, kIdesc, 1u);
+                            mma<KIND>(acc_t, a0 + adv, b0 + adv, kIdesc, 1u);
+                        } else {
+                            mma<KIND>(acc_t, a0 + adv, b0 + adv, kIdesc, acc);
+                        }
+                    }
+                    mma_commit(smem_u32(&empty[s]));
+                }
+                mma_commit(smem_u32(&accfull[b]));  // arrives when this group's MMAs are done
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                // Release any accumulator waiters: commits arrive once issued MMAs complete.
+                mma_commit(smem_u32(&accfull[0]));
+                mma_commit(smem_u32(&accfull[1]));
+            }
+        }
+        __syncwarp();
+    } else {
+        // Warps 0-3: promote each finished group into FP32 registers, then store.
+        const int row = warp * 32 + lane;
+        float acc[kTile];
+#pragma unroll
+        for (int j = 0; j < kTile; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        for (int g = 0; g < ngroups; ++g) {
+            const int b = g & 1;
+            if (!mbar_wait(smem_u32(&accfull[b]), (g >> 1) & 1) || *abort_flag) { ok = false; break; }
+            fence_after();
+            const uint32_t base = tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(b * kTile);
+#pragma unroll
+            for (int c = 0; c < kTile / 32; ++c) {
+                float v[32];
+                tmem_ld32(base + static_cast<uint32_t>(c * 32), v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], v[j]);
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&accempty[b])) : "memory");
+        }
+        if (!ok) {
+            if (lane == 0) atomicExch(&g_umma_error, 1);
+        } else {
+            const long long grow = static_cast<long long>(tm) * kTile + row;
+#pragma unroll
+            for (int c = 0; c < kTile / 32; ++c) {
+                const long long gcol = static_cast<long long>(tn) * kTile + c * 32;
+                float o[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = out.alpha * acc[c * 32 + j];
+                if (out.beta != 0.0f) {
+                    const float4* cin = reinterpret_cast<const float4*>(out.Cin + grow * out.ldcin + gcol);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 x = cin[q];
+                        o[4 * q + 0] += out.beta * x.x;
+                        o[4 * q + 1] += out.beta * x.y;
+                        o[4 * q + 2] += out.beta * x.z;
+                        o[4 * q + 3] += out.beta * x.w;
+                    }
+                }
+                if (out.C) {
+                    float4* dst = reinterpret_cast<float4*>(out.C + grow * out.ldc + gcol);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) dst[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                }
+                if (out.C_hi) {
+                    float4* hi = reinterpret_cast<float4*>(out.C_hi + grow * out.ld_split + gcol);
+                    float4* lo = reinterpret_cast<float4*>(out.C_lo + grow * out.ld_split + gcol);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        float h[4], l[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            h[e] = tf32_hi(o[4 * q + e]);
+                            l[e] = o[4 * q + e] - h[e];
+                        }
+                        hi[q] = make_float4(h[0], h[1], h[2], h[3]);
+                        lo[q] = make_float4(l[0], l[1], l[2], l[3]);
+                    }
+                }
+                if (out.Ct) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) out.Ct[(gcol + j) * out.ldct + grow] = o[j];
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTile));
+    }
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+    static EncodeFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeFn>(p);
+    }();
+    return fn;
+}
+
+// Row-major [rows, k] operand, 128-row x 128-byte boxes with the 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, bool bf16, long long rows, long long k, long long ld) {
+    EncodeFn enc = encode_fn();
+    if (!enc) return fail(TB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const int esize = bf16 ? 2 : 4;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(kTile)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TB_ERR_ARG, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return TB_OK;
+}
+
+template <int KIND, int STAGES>
+int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0, const CUtensorMap& b1, int M, int N,
+           int nk, const GemmOut& out, cudaStream_t st) {
+    constexpr int kOps = (KIND == kTF32x3) ? 4 : 2;
+    const size_t smem = static_cast<size_t>(STAGES) * kOps * kTileBytes + 1024 + 256;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [&] {
+        attr = cudaFuncSetAttribute(gemm_nt_kernel<KIND, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem));
+    });
+    if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute(gemm_nt_kernel)");
+    dim3 grid(N / kTile, M / kTile);
+    gemm_nt_kernel<KIND, STAGES><<<grid, kThreadsGemm, smem, st>>>(a0, a1, b0, b1, nk, out);
+    return check_launch("gemm_nt_kernel");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int gemm_nt(Kind kind, const Operand& A, const Operand& B, int M, int N, int K, const GemmOut& out,
+            cudaStream_t stream) {
+    const int kstep = kind == kTF32x3 ? 32 : 64;
+    if (M <= 0 || N <= 0 || K <= 0 || M % kTile || N % kTile || K % kstep)
+        return fail(TB_ERR_SHAPE, "gemm_nt: M=%d N=%d K=%d must be multiples of 128/128/%d", M, N, K, kstep);
+    const int esize = kind == kTF32x3 ? 4 : 2;
+    if (!A.hi || !B.hi || (kind == kTF32x3 && (!A.lo || !B.lo)) || !aligned16(A.hi) || !aligned16(B.hi) ||
+        (kind == kTF32x3 && (!aligned16(A.lo) || !aligned16(B.lo))) || (A.ld * esize) % 16 || (B.ld * esize) % 16 ||
+        A.ld < K || B.ld < K)
+        return fail(TB_ERR_ARG, "gemm_nt: operands must be non-null, 16-byte aligned, ld >= K, ld*elem % 16 == 0");
+    if ((out.C && (!aligned16(out.C) || out.ldc % 4 || out.ldc < N)) ||
+        (out.beta != 0.0f && (!out.Cin || !aligned16(out.Cin) || out.ldcin % 4 || out.ldcin < N)) ||
+        (out.C_hi && (!out.C_lo || !aligned16(out.C_hi) || !aligned16(out.C_lo) || out.ld_split % 4 || out.ld_split < N)) ||
+        (out.Ct && out.ldct < M))
+        return fail(TB_ERR_ARG, "gemm_nt: output pointers must be 16-byte aligned with ld >= N and ld % 4 == 0");
+    const bool bf16 = kind == kBF16;
+    CUtensorMap a0{}, a1{}, b0{}, b1{};
+    int rc = make_map(&a0, A.hi, bf16, M, K, A.ld);
+    if (!rc) rc = make_map(&b0, B.hi, bf16, N, K, B.ld);
+    if (!rc && !bf16) rc = make_map(&a1, A.lo, false, M, K, A.ld);
+    if (!rc && !bf16) rc = make_map(&b1, B.lo, false, N, K, B.ld);
+    if (rc) return rc;
+    if (bf16) { a1 = a0; b1 = b0; }
+    const int nk = K / kstep;
+    return bf16 ? launch<kBF16, 4>(a0, a1, b0, b1, M, N, nk, out, stream)
+                : launch<kTF32x3, 3>(a0, a1, b0, b1, M, N, nk, out, stream);
+}
+
+int gemm_take_error(cudaStream_t stream) {
+    int h = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&h, g_umma_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_umma_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return -1;
+    return h;
+}
+
+}  // namespace umma
+}  // namespace tb
+
+// ---- C ABI --------------------------------------------------------------------
+namespace tb {
+namespace {
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                                  size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        uint32_t r;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+        const float h = __uint_as_float(r);
+        hi[i] = h;
+        lo[i] = v - h;
+    }
+}
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" int tb_split_tf32(const float* x, float* hi, float* lo, size_t n, void* stream) {
+    if (n == 0) return TB_OK;
+    if (!x || !hi || !lo) return fail(TB_ERR_ARG, "tb_split_tf32: null pointer");
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    const unsigned grid = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 148u * 32u));
+    split_tf32_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, hi, lo, n);
+    return check_launch("split_tf32_kernel");
+}
+
+extern "C" int tb_gemm_nt_tf32x3(const float* a_hi, const float* a_lo, long long lda, const float* b_hi,
+                                 const float* b_lo, long long ldb, int M, int N, int K, float alpha, float beta,
+                                 const float* c_in, long long ldcin, float* c, long long ldc, int lower_only,
+                                 void* stream) {
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    umma::GemmOut o{};
+    o.C = c;
+    o.ldc = ldc;
+    o.Cin = c_in;
+    o.ldcin = ldcin;
+    o.alpha = alpha;
+    o.beta = beta;
+    o.lower_only = lower_only;
+    return umma::gemm_nt(umma::kTF32x3, {a_hi, a_lo, lda}, {b_hi, b_lo, ldb}, M, N, K, o,
+                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tb_gemm_nt_bf16(const void* a, long long lda, const void* b, long long ldb, int M, int N, int K,
+                               float alpha, float beta, const float* c_in, long long ldcin, float* c, long long ldc,
+                               int lower_only, void* stream) {
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    umma::GemmOut o{};
+    o.C = c;
+    o.ldc = ldc;
+    o.Cin = c_in;
+    o.ldcin = ldcin;
+    o.alpha = alpha;
+    o.beta = beta;
+    o.lower_only = lower_only;
+    return umma::gemm_nt(umma::kBF16, {a, nullptr, lda}, {b, nullptr, ldb}, M, N, K, o,
+                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tb_gemm_status(void* stream) {
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    const int e = umma::gemm_take_error(static_cast<cudaStream_t>(stream));
+    if (e < 0) return fail(TB_ERR_CUDA, "reading the GEMM status failed");
+    return e ? fail(TB_ERR_TIMEOUT, "a tcgen05 GEMM pipeline wait expired") : TB_OK;
+}

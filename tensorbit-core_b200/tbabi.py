@@ -113,6 +113,14 @@ def lib() -> C.CDLL:
             "tb_fisher_normalize": ([vp, sz, vp], i32),
             "tb_compensate": ([vp, vp, vp, sz, i32, vp], i32),
             "tb_block_obs": ([vp, vp, C.POINTER(vp), i32, sz, sz, f32, f32, f32, C.POINTER(C.c_uint64), vp], i32),
+            "tb_split_tf32": ([vp, vp, vp, sz, vp], i32),
+            "tb_gemm_nt_tf32x3": ([vp, vp, C.c_longlong, vp, vp, C.c_longlong, i32, i32, i32, f32, f32, vp,
+                                   C.c_longlong, vp, C.c_longlong, i32, vp], i32),
+            "tb_gemm_nt_bf16": ([vp, C.c_longlong, vp, C.c_longlong, i32, i32, i32, f32, f32, vp, C.c_longlong,
+                                 vp, C.c_longlong, i32, vp], i32),
+            "tb_gemm_status": ([vp], i32),
+            "tb_obs_hessian": ([vp, i32, i32, vp, vp], i32),
+            "tb_obs_sparsegpt": ([vp, i32, i32, vp, f32, i32, i32, vp, vp, vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),
             "tb_score_mask_pack_host_noalloc": ([C.POINTER(PruneArgs)], i32),
