@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-obs", action="store_true", help="skip the configuration-4 OBS measurement")
+    ap.add_argument("--obs-only", action="store_true", help="only the configuration-4 OBS measurement")
+    ap.add_argument("--obs-steps", type=int, default=3)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers per step (profiling a smaller case only; default 32)")
     ap.add_argument("--matrices", default="",
@@ -179,6 +182,14 @@ def run_ours(args):
     tb.lib()
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
+    if args.obs_only:
+        obs = run_obs(torch, tb, dev, args.obs_steps)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "obs": obs, "n_gpus": world}), flush=True)
+        if world > 1:
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
+        return
 
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     sets = [make_layer_set(torch, gen, dev), make_layer_set(torch, gen, dev)]
@@ -244,6 +255,11 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = run_e2e(torch, tb, dev, gen, args, world, rank, local)
 
+    # ---- configuration 4 (OBS on tensor cores), per rank -------------------
+    obs = None
+    if not args.no_obs:
+        obs = run_obs(torch, tb, dev, args.obs_steps)
+
     # ---- CPU baseline (rank 0, single GPU only) ----------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -278,6 +294,7 @@ def run_ours(args):
             "gpu_launches": launches,
             "clocks": clk,
             "e2e": e2e,
+            "obs": obs,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -329,6 +346,84 @@ def run_e2e(torch, tb, dev, gen, args, world, rank, local):
     return {"value": round(value, 4), "unit": "Gparams/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": args.e2e_steps, "step": "one decoder layer (7 matrices) via tb_score_mask_pack_host, pinned host memory",
             "s_per_step": round(el / args.e2e_steps, 4)}
+
+
+# ---------------------------------------------------------------------------
+# configuration 4: column-block exact OBS on tensor cores
+# ---------------------------------------------------------------------------
+OBS_D, OBS_R, OBS_N, OBS_B = 14336, 4096, 2048, 128
+
+
+def obs_flops(d, r, n, B=OBS_B):
+    """Executed FLOPs of tb_obs_hessian + tb_obs_sparsegpt, each product once
+    (the 3xTF32 split triples the tensor-core work behind the FP32 GEMMs):
+    lower-tile X^T X, recursive Cholesky (recursive triangular solve + lower-tile
+    Schur updates), recursive triangular inverse, in-block sweep, lazy updates."""
+    T = d // 128
+    f = 2 * 128 * 128 * n * (T * (T + 1) // 2)
+    half = lambda m: (m // 128 // 2) * 128
+    def trsm(m, k):
+        if k == 128:
+            return 2 * m * 128 * 128
+        k1 = half(k)
+        return trsm(m, k1) + 2 * m * (k - k1) * k1 + trsm(m, k - k1)
+    def chol(m):
+        if m == 128:
+            return 2 * 128 ** 3 // 3
+        m1 = half(m)
+        m2 = m - m1
+        t2 = m2 // 128
+        return chol(m1) + trsm(m2, m1) + 2 * 128 * 128 * m1 * (t2 * (t2 + 1) // 2) + chol(m2)
+    def trtri(m):
+        if m == 128:
+            return 0
+        m1 = half(m)
+        m2 = m - m1
+        return trtri(m1) + trtri(m2) + 2 * m1 * m2 * m1 + 2 * m2 * m1 * m2
+    f += chol(d) + trtri(d)
+    for i1 in range(0, d, B):
+        f += r * B * B + 2 * r * B * (d - i1 - B)
+    return f
+
+
+def run_obs(torch, tb, dev, steps):
+    gen = torch.Generator(device=dev).manual_seed(4)
+    X = torch.randn(OBS_N, OBS_D, device=dev, generator=gen)
+    hot = torch.randperm(OBS_D, device=dev, generator=gen)[: OBS_D // 100]
+    X[:, hot] *= 20
+    xt = X.t().contiguous().to(torch.bfloat16)
+    del X
+    W0 = (torch.randn(OBS_R, OBS_D, device=dev, generator=gen) * 0.02).to(torch.bfloat16).float()
+    W = torch.empty_like(W0)
+    H = torch.zeros(OBS_D, OBS_D, device=dev)
+    mask = torch.empty(OBS_R * OBS_D // 4, dtype=torch.uint8, device=dev)
+    L = tb.lib()
+    sptr = torch.cuda.current_stream().cuda_stream
+    ms = []
+    for k in range(steps + 1):  # the first pass warms up (workspace, module load)
+        W.copy_(W0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        tb.check(L.tb_obs_hessian(xt.data_ptr(), OBS_D, OBS_N, H.data_ptr(), sptr))
+        tb.check(L.tb_obs_sparsegpt(W.data_ptr(), OBS_R, OBS_D, H.data_ptr(), 0.01, 2, 4, mask.data_ptr(), None, sptr))
+        e1.record()
+        torch.cuda.synchronize()
+        if k:
+            ms.append(e0.elapsed_time(e1))
+    pop = sum(((mask >> b) & 1).int() for b in range(4))
+    assert bool((pop == 2).all()), "OBS mask is not 2:4"
+    f = obs_flops(OBS_D, OBS_R, OBS_N)
+    t = sum(ms) / len(ms)
+    bf16_peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+    tflops = f / (t / 1e3) / 1e12
+    return {"workload": f"cfg4: {OBS_R}x{OBS_D} down_proj (BF16 -> FP32), X {OBS_N}x{OBS_D} BF16 N(0,1) with 1% columns x20, "
+                        "damp 0.01 mean(diag), 128-column blocks, 2:4",
+            "ms_per_pass": round(t, 2), "passes": steps, "flops_per_pass": f, "tflops": round(tflops, 1),
+            "unit": "TFLOP/s", "flop_count": "executed, each 3xTF32 product counted once (bench.obs_flops)",
+            "tensor_peak_bf16_tflops": bf16_peak,
+            "frac_of_bf16_peak": round(tflops / bf16_peak, 4),
+            "frac_of_3xtf32_ceiling": round(tflops / (bf16_peak / 2 / 3), 4)}
 
 
 # ---------------------------------------------------------------------------

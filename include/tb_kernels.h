@@ -194,8 +194,9 @@ int tb_obs_hessian(const void* xt_bf16, int d, int n, float* H, void* stream);
  * pruned, each column's error updates the rest of its block, and the block's
  * errors update the remaining columns through one tcgen05 GEMM.  mask gets
  * r*d/4 bytes (bit k = keep column 4g+k, the .tb convention).  ut_out (d x d,
- * may be NULL) receives U^T.  Workspace ~11 d^2 floats is allocated
- * stream-ordered.  Synchronises the stream.  TB_ERR_CONFIG if H + lambda I is
+ * may be NULL) receives U^T.  A workspace of ~11 d^2 floats is allocated on
+ * first use and kept per device for later calls (grow-only; ~9 GB at d = 14336).
+ * Synchronises the stream.  TB_ERR_CONFIG if H + lambda I is
  * not positive definite in FP32. */
 int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float damp_frac, int n_keep, int m,
                      uint8_t* mask, float* ut_out, void* stream);

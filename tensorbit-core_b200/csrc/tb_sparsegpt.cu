@@ -9,19 +9,24 @@
 //   2. lambda = frac * mean(diag H); H += lambda I.
 //   3. U = chol_upper(H^-1) without forming H^-1: with P the index reversal,
 //      chol_lower(P H P) = L gives H^-1 = (P L^-1 P)^T (P L^-1 P), so
-//      U = P L^-1 P.  L and L^-1 come from one recursive Cholesky-and-inverse
-//      whose off-diagonal work is four FP32-accurate (3xTF32) tcgen05 GEMMs per
-//      level; 128 x 128 diagonal blocks are factored in shared memory.
+//      U = P L^-1 P.  L comes from a recursive Cholesky whose panel solve is a
+//      recursive triangular solve (only 128 x 128 diagonal blocks are inverted,
+//      so the factorisation keeps the stability of a triangular solve even when
+//      H is rank-deficient plus lambda I), then L^-1 from a recursive
+//      triangular inverse; all off-diagonal work is FP32-accurate (3xTF32)
+//      tcgen05 GEMMs, the 128 x 128 diagonal blocks are factored in shared
+//      memory.
 //   4. Column blocks of 128: per row (one warp per row, rows independent), for
 //      each group of M columns prune the M-N smallest w^2 / U_qq^2 (lowest index
 //      on ties), then for each column q: err = (w_q - kept_q) / U_qq,
 //      w_j -= err U_qj (j >= q in the block); the block's errors E then update
 //      the remaining columns lazily, W[:, i2:] -= E U[i1:i2, i2:], a tcgen05
 //      GEMM.
-// All FP32; algorithmic FLOPs: n d^2 (lower XtX) + ~4/3 d^3 (dense-tile
-// recursion) + 2 r d^2 / 2 (lazy updates) + r d B (in-block).
+// All FP32; executed FLOPs are counted by bench.obs_flops (lower-tile XtX,
+// the recursions' GEMMs on dense tiles, the in-block and lazy updates).
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 #include <vector>
 
 #include "tb_device.cuh"
@@ -256,28 +261,54 @@ int gemm(const float* ah, const float* al, long long lda, const float* bh, const
     return umma::gemm_nt(umma::kTF32x3, {ah, al, lda}, {bh, bl, ldb}, M, N, K, o, st);
 }
 
-// Recursive Cholesky + inverse of the block [off, off+n) of A (see file comment).
-int chol_inv(Work& w, int off, int n, cudaStream_t st, size_t base_smem) {
+long long half_blocks(int n) { return static_cast<long long>(n / kB / 2) * kB; }
+
+// Solves X L^T = B in place for B = A[r0 : r0+m, c0 : c0+n] (and its split),
+// L = the lower factor in A[c0 : c0+n, c0 : c0+n].  Recursive on L: only the
+// 128 x 128 diagonal blocks are inverted (their inverses sit in V), the rest is
+// GEMM updates, which keeps the solve as stable as a triangular solve.
+int trsm(Work& w, long long r0, int m, long long c0, int n, cudaStream_t st) {
+    const long long d = w.d;
+    auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
+    int rc;
+    if (n == kB) {  // B <- B V_cc^T, in place (one 128-column output tile per row block)
+        umma::GemmOut o{};
+        o.C = at(w.A, r0, c0); o.ldc = d;
+        o.C_hi = at(w.A_hi, r0, c0); o.C_lo = at(w.A_lo, r0, c0); o.ld_split = d;
+        o.alpha = 1.0f; o.beta = 0.0f;
+        return gemm(at(w.A_hi, r0, c0), at(w.A_lo, r0, c0), d, at(w.V_hi, c0, c0), at(w.V_lo, c0, c0), d, m, kB, kB,
+                    o, st);
+    }
+    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
+    if ((rc = trsm(w, r0, m, c0, n1, st))) return rc;
+    {  // B2 -= B1 L21^T
+        umma::GemmOut o{};
+        o.C = at(w.A, r0, c0 + n1); o.ldc = d;
+        o.Cin = at(w.A, r0, c0 + n1); o.ldcin = d;
+        o.C_hi = at(w.A_hi, r0, c0 + n1); o.C_lo = at(w.A_lo, r0, c0 + n1); o.ld_split = d;
+        o.alpha = -1.0f; o.beta = 1.0f;
+        if ((rc = gemm(at(w.A_hi, r0, c0), at(w.A_lo, r0, c0), d, at(w.A_hi, c0 + n1, c0), at(w.A_lo, c0 + n1, c0),
+                       d, m, n2, n1, o, st)))
+            return rc;
+    }
+    return trsm(w, r0, m, c0 + n1, n2, st);
+}
+
+// Recursive Cholesky of A[off : off+n] (lower, in place, with split); the
+// 128 x 128 diagonal blocks also get their inverses in V / VT.
+int chol(Work& w, int off, int n, cudaStream_t st, size_t base_smem) {
     const long long d = w.d;
     if (n == kB) {
         base_chol_inv_kernel<<<1, 1024, base_smem, st>>>(w.A, w.V, w.V_hi, w.V_lo, w.VT, w.VT_hi, w.VT_lo, w.d, off,
                                                          w.bad);
         return check_launch("base_chol_inv_kernel");
     }
-    const int n1 = (n / kB / 2) * kB, n2 = n - n1;
-    int rc = chol_inv(w, off, n1, st, base_smem);
+    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
+    int rc = chol(w, off, n1, st, base_smem);
     if (rc) return rc;
-    auto at = [&](float* p, long long r0, long long c0) { return p + r0 * d + c0; };
     const long long o1 = off + n1;
-    {  // L21 = A21 V11^T, written over A21 with its split
-        umma::GemmOut o{};
-        o.C = at(w.A, o1, off); o.ldc = d;
-        o.C_hi = at(w.A_hi, o1, off); o.C_lo = at(w.A_lo, o1, off); o.ld_split = d;
-        o.alpha = 1.0f; o.beta = 0.0f;
-        if ((rc = gemm(at(w.A_hi, o1, off), at(w.A_lo, o1, off), d, at(w.V_hi, off, off), at(w.V_lo, off, off), d,
-                       n2, n1, n1, o, st)))
-            return rc;
-    }
+    if ((rc = trsm(w, o1, n2, off, n1, st))) return rc;  // L21 = A21 L11^-T
+    auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
     {  // A22 -= L21 L21^T on the lower tiles, with split
         umma::GemmOut o{};
         o.C = at(w.A, o1, o1); o.ldc = d;
@@ -288,7 +319,20 @@ int chol_inv(Work& w, int off, int n, cudaStream_t st, size_t base_smem) {
                        n2, n1, o, st)))
             return rc;
     }
-    if ((rc = chol_inv(w, off + n1, n2, st, base_smem))) return rc;
+    return chol(w, off + n1, n2, st, base_smem);
+}
+
+// Recursive inverse V = L^-1 of the factor in A (diagonal 128-blocks already
+// inverted by the base kernel): V21 = -V22 (L21 V11), with V^T kept alongside.
+int trtri(Work& w, int off, int n, cudaStream_t st) {
+    if (n == kB) return TB_OK;
+    const long long d = w.d;
+    auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
+    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
+    const long long o1 = off + n1;
+    int rc = trtri(w, off, n1, st);
+    if (!rc) rc = trtri(w, off + n1, n2, st);
+    if (rc) return rc;
     {  // T^T = V11^T L21^T  (n1 x n2), split only
         umma::GemmOut o{};
         o.C_hi = w.T_hi; o.C_lo = w.T_lo; o.ld_split = n2;
@@ -305,7 +349,6 @@ int chol_inv(Work& w, int off, int n, cudaStream_t st, size_t base_smem) {
         o.alpha = -1.0f; o.beta = 0.0f;
         if ((rc = gemm(at(w.V_hi, o1, o1), at(w.V_lo, o1, o1), d, w.T_hi, w.T_lo, n2, n2, n1, n2, o, st))) return rc;
     }
-    // VT12's split (used as an operand one level up)
     return tb_split_tf32_2d(at(w.VT, off, o1), at(w.VT_hi, off, o1), at(w.VT_lo, off, o1), n1, n2, d, st);
 }
 
@@ -331,6 +374,49 @@ int tb_split_tf32_2d(const float* x, float* hi, float* lo, int rows, int cols, l
     return check_launch("split2d_kernel");
 }
 
+namespace {
+
+// Per-device workspace kept between calls (grow-only): the d x d matrices of a
+// 14336-wide layer take ~9 GB, and re-mapping that much per call costs more
+// than the factorisation.
+struct Workspace {
+    int dev = -1;
+    float* ptr = nullptr;
+    size_t floats = 0;
+};
+std::mutex g_ws_mu;
+std::vector<Workspace> g_ws;
+
+int workspace(size_t floats, float** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    for (auto& w : g_ws)
+        if (w.dev == dev) {
+            if (w.floats < floats) {
+                cudaDeviceSynchronize();
+                cudaFree(w.ptr);
+                w.ptr = nullptr;
+                w.floats = 0;
+                e = cudaMalloc(reinterpret_cast<void**>(&w.ptr), floats * sizeof(float));
+                if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt workspace");
+                w.floats = floats;
+            }
+            *out = w.ptr;
+            return TB_OK;
+        }
+    Workspace w;
+    w.dev = dev;
+    e = cudaMalloc(reinterpret_cast<void**>(&w.ptr), floats * sizeof(float));
+    if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt workspace");
+    w.floats = floats;
+    g_ws.push_back(w);
+    *out = w.ptr;
+    return TB_OK;
+}
+
+}  // namespace
 }  // namespace tb
 
 using namespace tb;
@@ -360,8 +446,8 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     // Workspace: 11 d x d FP32 matrices, the error panel split and two scalars.
     float* ws = nullptr;
     const size_t ws_floats = 11 * dd + 2 * static_cast<size_t>(r) * kB + 64;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), ws_floats * sizeof(float), st);
-    if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt workspace");
+    if ((rc = workspace(ws_floats, &ws))) return rc;
+    cudaError_t e = cudaSuccess;
     Work w{};
     w.d = d;
     w.A = ws; w.A_hi = ws + dd; w.A_lo = ws + 2 * dd;
@@ -379,11 +465,12 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
         e = cudaFuncSetAttribute(inblock_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(u1_smem));
     if (e == cudaSuccess) e = cudaMemsetAsync(w.V, 0, 6 * dd * sizeof(float), st);  // V and VT (+ splits) triangles
     if (e == cudaSuccess) e = cudaMemsetAsync(w.bad, 0, sizeof(int), st);
-    if (e != cudaSuccess) { cudaFreeAsync(ws, st); return cuda_fail(e, "tb_obs_sparsegpt setup"); }
+    if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt setup");
     diag_sum_kernel<<<1, 1024, 0, st>>>(H, d, dsum);
     reverse_damp_kernel<<<148 * 16, 256, 0, st>>>(H, d, dsum, damp_frac, w.A, w.A_hi, w.A_lo);
     rc = check_launch("hessian prep");
-    if (!rc) rc = chol_inv(w, 0, d, st, base_smem);
+    if (!rc) rc = chol(w, 0, d, st, base_smem);
+    if (!rc) rc = trtri(w, 0, d, st);
     // Ut (lower) = (P V P)^T into A's buffers (A is no longer needed).
     float *Ut = w.A, *Ut_hi = w.A_hi, *Ut_lo = w.A_lo;
     if (!rc) {
@@ -414,7 +501,6 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
         if (e == cudaSuccess) e = cudaStreamSynchronize(st);
         if (e != cudaSuccess) rc = cuda_fail(e, "tb_obs_sparsegpt sync");
     }
-    cudaFreeAsync(ws, st);
     if (!rc) {
         const int ge = umma::gemm_take_error(st);
         if (ge) rc = fail(TB_ERR_TIMEOUT, "a tcgen05 GEMM pipeline wait expired");

@@ -36,8 +36,11 @@ def run(torch, tb, W, X, n_keep=2, damp=0.01):
     return Wd.cpu().numpy(), mask.cpu().numpy().reshape(r, d // 4), ut.cpu().numpy()
 
 
-@pytest.mark.parametrize("r,d,n,n_keep", [(256, 512, 512, 2), (512, 1024, 2048, 2), (256, 768, 1024, 1)])
+@pytest.mark.parametrize("r,d,n,n_keep", [(256, 512, 512, 2), (512, 1024, 2048, 2), (256, 768, 1024, 1),
+                                          (256, 2048, 512, 2), (256, 3072, 640, 3)])
 def test_sparsegpt_against_float64(cuda, tblib, r, d, n, n_keep):
+    """Includes fewer tokens than features (n < d): H is rank-deficient plus
+    lambda I, the ill-conditioned regime of the 4096 x 14336 layer."""
     X = activations(n, d, d + n)
     W = inputs.normal(r * d, 0.02, r + d).reshape(r, d)
     Wg, mg, ut = run(cuda, tblib, W, X, n_keep)
