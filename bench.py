@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--no-obs", action="store_true", help="skip the configuration-4 OBS measurement")
     ap.add_argument("--obs-only", action="store_true", help="only the configuration-4 OBS measurement")
     ap.add_argument("--obs-steps", type=int, default=3)
+    ap.add_argument("--gemm-probe", type=int, nargs=3, metavar=("M", "N", "K"),
+                    help="time the tcgen05 NT GEMM (3xTF32 and BF16) at one shape and exit")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers per step (profiling a smaller case only; default 32)")
     ap.add_argument("--matrices", default="",
@@ -182,6 +184,10 @@ def run_ours(args):
     tb.lib()
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
+    if args.gemm_probe:
+        if rank == 0:
+            print(json.dumps({"gemm_probe": gemm_probe(torch, tb, dev, *args.gemm_probe)}), flush=True)
+        return
     if args.obs_only:
         obs = run_obs(torch, tb, dev, args.obs_steps)
         if rank == 0:
@@ -384,6 +390,39 @@ def obs_flops(d, r, n, B=OBS_B):
     for i1 in range(0, d, B):
         f += r * B * B + 2 * r * B * (d - i1 - B)
     return f
+
+
+def gemm_probe(torch, tb, dev, M, N, K, reps=5):
+    """TFLOP/s of the tcgen05 NT GEMM at one shape (each product counted once)."""
+    L = tb.lib()
+    sptr = torch.cuda.current_stream().cuda_stream
+    A = torch.randn(M, K, device=dev)
+    B = torch.randn(N, K, device=dev)
+    C = torch.empty(M, N, device=dev)
+    ah, al, bh, bl = (torch.empty_like(A), torch.empty_like(A), torch.empty_like(B), torch.empty_like(B))
+    tb.check(L.tb_split_tf32(A.data_ptr(), ah.data_ptr(), al.data_ptr(), A.numel(), sptr))
+    tb.check(L.tb_split_tf32(B.data_ptr(), bh.data_ptr(), bl.data_ptr(), B.numel(), sptr))
+    Ab, Bb = A.bfloat16(), B.bfloat16()
+    out = {"shape": [M, N, K]}
+    for kind in ("tf32x3", "bf16"):
+        def once():
+            if kind == "tf32x3":
+                return L.tb_gemm_nt_tf32x3(ah.data_ptr(), al.data_ptr(), K, bh.data_ptr(), bl.data_ptr(), K, M, N, K,
+                                           1.0, 0.0, None, N, C.data_ptr(), N, 0, sptr)
+            return L.tb_gemm_nt_bf16(Ab.data_ptr(), K, Bb.data_ptr(), K, M, N, K, 1.0, 0.0, None, N, C.data_ptr(), N,
+                                     0, sptr)
+        tb.check(once())
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            tb.check(once())
+        e1.record()
+        torch.cuda.synchronize()
+        tb.check(L.tb_gemm_status(sptr))
+        ms = e0.elapsed_time(e1) / reps
+        out[kind] = {"ms": round(ms, 3), "tflops": round(2 * M * N * K / ms / 1e9, 1)}
+    return out
 
 
 def run_obs(torch, tb, dev, steps):
