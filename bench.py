@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--no-obs", action="store_true", help="skip the configuration-4 OBS measurement")
     ap.add_argument("--obs-only", action="store_true", help="only the configuration-4 OBS measurement")
     ap.add_argument("--obs-steps", type=int, default=3)
+    ap.add_argument("--obs-shape", type=int, nargs=3, metavar=("R", "D", "N"),
+                    help="rows, columns and tokens of the exact-OBS pass (default: the 4096 x 14336, 2048-token down_proj)")
     ap.add_argument("--gemm-probe", type=int, nargs=3, metavar=("M", "N", "K"),
                     help="time the tcgen05 NT GEMM (3xTF32 and BF16) at one shape and exit")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -189,7 +191,7 @@ def run_ours(args):
             print(json.dumps({"gemm_probe": gemm_probe(torch, tb, dev, *args.gemm_probe)}), flush=True)
         return
     if args.obs_only:
-        obs = run_obs(torch, tb, dev, args.obs_steps)
+        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape)
         if rank == 0:
             print(json.dumps({"metric": METRIC, "obs": obs, "n_gpus": world}), flush=True)
         if world > 1:
@@ -264,7 +266,7 @@ def run_ours(args):
     # ---- configuration 4 (OBS on tensor cores), per rank -------------------
     obs = None
     if not args.no_obs:
-        obs = run_obs(torch, tb, dev, args.obs_steps)
+        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape)
 
     # ---- CPU baseline (rank 0, single GPU only) ----------------------------
     cpu = None
@@ -360,36 +362,13 @@ def run_e2e(torch, tb, dev, gen, args, world, rank, local):
 OBS_D, OBS_R, OBS_N, OBS_B = 14336, 4096, 2048, 128
 
 
-def obs_flops(d, r, n, B=OBS_B):
-    """Executed FLOPs of tb_obs_hessian + tb_obs_sparsegpt, each product once
-    (the 3xTF32 split triples the tensor-core work behind the FP32 GEMMs):
-    lower-tile X^T X, recursive Cholesky (recursive triangular solve + lower-tile
-    Schur updates), recursive triangular inverse, in-block sweep, lazy updates."""
-    T = d // 128
-    f = 2 * 128 * 128 * n * (T * (T + 1) // 2)
-    half = lambda m: (m // 128 // 2) * 128
-    def trsm(m, k):
-        if k == 128:
-            return 2 * m * 128 * 128
-        k1 = half(k)
-        return trsm(m, k1) + 2 * m * (k - k1) * k1 + trsm(m, k - k1)
-    def chol(m):
-        if m == 128:
-            return 2 * 128 ** 3 // 3
-        m1 = half(m)
-        m2 = m - m1
-        t2 = m2 // 128
-        return chol(m1) + trsm(m2, m1) + 2 * 128 * 128 * m1 * (t2 * (t2 + 1) // 2) + chol(m2)
-    def trtri(m):
-        if m == 128:
-            return 0
-        m1 = half(m)
-        m2 = m - m1
-        return trtri(m1) + trtri(m2) + 2 * m1 * m2 * m1 + 2 * m2 * m1 * m2
-    f += chol(d) + trtri(d)
-    for i1 in range(0, d, B):
-        f += r * B * B + 2 * r * B * (d - i1 - B)
-    return f
+def obs_flops(d, r, n):
+    """Algorithmic FLOPs of one exact-OBS pass, independent of how the kernels
+    split the work: X^T X on the lower triangle (d(d+1)/2 dot products of
+    length n, 2 flops per term), Cholesky d^3/3, triangular inverse d^3/3, and
+    the column sweep r d^2 (column q's error updates the d-q later columns of
+    its row: sum over q of 2 r (d - q))."""
+    return d * (d + 1) * n + 2 * d ** 3 // 3 + r * d * d
 
 
 def gemm_probe(torch, tb, dev, M, N, K, reps=5):
@@ -425,7 +404,8 @@ def gemm_probe(torch, tb, dev, M, N, K, reps=5):
     return out
 
 
-def run_obs(torch, tb, dev, steps):
+def run_obs(torch, tb, dev, steps, shape=None):
+    OBS_R, OBS_D, OBS_N = shape or (globals()["OBS_R"], globals()["OBS_D"], globals()["OBS_N"])
     gen = torch.Generator(device=dev).manual_seed(4)
     X = torch.randn(OBS_N, OBS_D, device=dev, generator=gen)
     hot = torch.randperm(OBS_D, device=dev, generator=gen)[: OBS_D // 100]
@@ -459,7 +439,7 @@ def run_obs(torch, tb, dev, steps):
     return {"workload": f"cfg4: {OBS_R}x{OBS_D} down_proj (BF16 -> FP32), X {OBS_N}x{OBS_D} BF16 N(0,1) with 1% columns x20, "
                         "damp 0.01 mean(diag), 128-column blocks, 2:4",
             "ms_per_pass": round(t, 2), "passes": steps, "flops_per_pass": f, "tflops": round(tflops, 1),
-            "unit": "TFLOP/s", "flop_count": "executed, each 3xTF32 product counted once (bench.obs_flops)",
+            "unit": "TFLOP/s", "flop_count": "algorithmic: d(d+1)n + 2d^3/3 + r d^2 (bench.obs_flops)",
             "tensor_peak_bf16_tflops": bf16_peak,
             "frac_of_bf16_peak": round(tflops / bf16_peak, 4),
             "frac_of_3xtf32_ceiling": round(tflops / (bf16_peak / 2 / 3), 4)}

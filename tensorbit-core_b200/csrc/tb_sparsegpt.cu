@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "tb_device.cuh"
+#include "tb_pdl.cuh"
 #include "tb_runtime.h"
 #include "tb_umma.cuh"
 
@@ -40,7 +41,6 @@ int tb_split_tf32_2d(const float* x, float* hi, float* lo, int rows, int cols, l
 namespace {
 
 constexpr int kB = 128;  // diagonal / column block
-constexpr int kU1Ld = kB + 4;
 
 __device__ __forceinline__ float tf32_round(float x) {
     uint32_t r;
@@ -51,6 +51,8 @@ __device__ __forceinline__ float tf32_round(float x) {
 // diag sum of the lower-tile H (one block reduction, deterministic order per block).
 __global__ void diag_sum_kernel(const float* __restrict__ H, int d, double* __restrict__ out) {
     __shared__ double part[1024];
+    pdl_wait();
+    pdl_trigger();
     double s = 0.0;
     for (int i = threadIdx.x; i < d; i += blockDim.x) s += static_cast<double>(H[static_cast<size_t>(i) * d + i]);
     part[threadIdx.x] = s;
@@ -62,101 +64,236 @@ __global__ void diag_sum_kernel(const float* __restrict__ H, int d, double* __re
     if (threadIdx.x == 0) *out = part[0];
 }
 
-// A = P (H + lambda I) P on the lower triangle (H valid on lower tiles), plus
-// its tf32 hi/lo split; upper triangle zero.
-__global__ void reverse_damp_kernel(const float* __restrict__ H, int d, const double* __restrict__ diag_sum, float frac,
-                                    float* __restrict__ A, float* __restrict__ A_hi, float* __restrict__ A_lo) {
+// A = P (H + lambda I) P on the lower triangle, plus its tf32 hi/lo split:
+// A[i][j] = H[d-1-j][d-1-i] (j <= i), read from H's lower tiles through a
+// 32 x 32 shared-memory transpose so that both the reads and the writes are
+// coalesced.  Tiles above the diagonal 128-blocks are never read and are not
+// written; inside a diagonal 128-block the upper part is written as zero.
+__global__ void __launch_bounds__(256) reverse_damp_kernel(const float* __restrict__ H, int d,
+                                                           const double* __restrict__ diag_sum, float frac,
+                                                           float* __restrict__ A, float* __restrict__ A_hi,
+                                                           float* __restrict__ A_lo) {
+    __shared__ float tile[32][33];
+    const int I = blockIdx.y, J = blockIdx.x;  // output tile: rows 32I.., columns 32J..
+    pdl_wait();
+    pdl_trigger();
+    if (J > I && (J >> 2) != (I >> 2)) return;
     const float lambda = static_cast<float>(frac * (*diag_sum / d));
-    const size_t total = static_cast<size_t>(d) * d;
-    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-        const int i = static_cast<int>(e / d), j = static_cast<int>(e % d);
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    if (J <= I) {
+        const int sr0 = d - 32 * (J + 1), sc0 = d - 32 * (I + 1);  // source rows d-1-j, columns d-1-i
+        for (int k = ty; k < 32; k += 8) tile[k][tx] = H[static_cast<size_t>(sr0 + k) * d + sc0 + tx];
+    }
+    __syncthreads();
+    for (int k = ty; k < 32; k += 8) {
+        const int i = 32 * I + k, j = 32 * J + tx;
         float v = 0.0f;
         if (j <= i) {
-            const int a = d - 1 - j, b = d - 1 - i;  // H[a][b] with a >= b: lower
-            v = H[static_cast<size_t>(a) * d + b];
+            v = tile[31 - tx][31 - k];
             if (i == j) v += lambda;
         }
-        A[e] = v;
+        const size_t g = static_cast<size_t>(i) * d + j;
         const float h = tf32_round(v);
-        A_hi[e] = h;
-        A_lo[e] = v - h;
+        A[g] = v;
+        A_hi[g] = h;
+        A_lo[g] = v - h;
     }
 }
 
-// Cholesky and inverse of one 128 x 128 diagonal block held in shared memory.
-// A block (lower) -> L (written back, lower); V = L^-1 (lower) to V with its
-// split, and V^T (upper) to VT with its split.  Sets *bad if a pivot is not
-// positive.
-__global__ void __launch_bounds__(1024) base_chol_inv_kernel(float* __restrict__ A, float* __restrict__ V,
-                                                             float* __restrict__ V_hi, float* __restrict__ V_lo,
-                                                             float* __restrict__ VT, float* __restrict__ VT_hi,
-                                                             float* __restrict__ VT_lo, int ld, int off,
-                                                             int* __restrict__ bad) {
+constexpr unsigned kFull = 0xFFFFFFFFu;
+constexpr int kLd = kB + 1;          // shared-memory pitch of the 128 x 128 blocks
+constexpr int kBaseThreads = 512;
+constexpr int kSLd = 33;
+
+// Cholesky factor and inverse of one 32 x 32 diagonal block by one warp.
+// Lane i keeps row i in registers relative to the current column j
+// (a[k] = D[i][j+k]) and shifts the row by one after each column, so the
+// column loop stays rolled with constant register indices: the kernel runs
+// once per launch, and compact code matters more than unrolling here.
+// D (pitch kLd) holds the Schur-updated block on and below the diagonal; on
+// return it holds L_kk with zeros above, Q (pitch kLd) holds L_kk^-1 with
+// zeros above.  Pivots <= 0 set *bad (and continue with 1).
+__device__ __noinline__ void diag32(float* D, float* Q, int lane, int* bad) {
+    float a[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) a[k] = (k <= lane) ? D[lane * kLd + k] : 0.0f;
+    float my_rinv = 1.0f;
+    bool all_ok = true;
+#pragma unroll 1
+    for (int j = 0; j < 32; ++j) {
+        const float djj = __shfl_sync(kFull, a[0], j);
+        const bool ok = djj > 0.0f;
+        all_ok = all_ok && ok;
+        const float rj = ok ? rsqrtf(djj) : 1.0f;
+        // lanes above j hold a[0] = 0 (upper triangle)
+        const float l = (lane == j) ? (ok ? djj * rj : 1.0f) : a[0] * rj;
+        if (lane == j) my_rinv = rj;
+        D[lane * kLd + j] = l;
+#pragma unroll
+        for (int k = 1; k < 32; ++k) {  // branch-free: the shuffles issue back to back
+            const float lk = __shfl_sync(kFull, l, (j + k) & 31);
+            if (lane >= j + k) a[k] = fmaf(-l, lk, a[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < 31; ++k) a[k] = a[k + 1];
+        a[31] = 0.0f;
+    }
+    if (!all_ok && lane == 0) atomicExch(bad, 1);
+    __syncwarp();
+    // column c = lane of L^-1 by forward elimination of L x = e_c; x[k] is row j+k
+    float x[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) x[k] = (k == lane) ? 1.0f : 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < 32; ++j) {
+        const float xj = x[0] * __shfl_sync(kFull, my_rinv, j);
+        Q[j * kLd + lane] = xj;
+#pragma unroll
+        for (int k = 1; k < 32; ++k)  // slots past row 31 hold values that are never stored
+            x[k] = fmaf(-xj, D[min(j + k, 31) * kLd + j], x[k]);
+#pragma unroll
+        for (int k = 0; k < 31; ++k) x[k] = x[k + 1];
+        x[31] = 0.0f;
+    }
+    __syncwarp();
+}
+
+// 32-term dot product of two shared-memory rows (four partial sums).
+__device__ __forceinline__ float dot32(const float* x, const float* y) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 2
+    for (int k = 0; k < 32; k += 4) {
+        a0 = fmaf(x[k], y[k], a0);
+        a1 = fmaf(x[k + 1], y[k + 1], a1);
+        a2 = fmaf(x[k + 2], y[k + 2], a2);
+        a3 = fmaf(x[k + 3], y[k + 3], a3);
+    }
+    return (a0 + a1) + (a2 + a3);
+}
+
+// Cholesky and inverse of one 128 x 128 diagonal block in shared memory,
+// blocked by 32: per 32-column step, the diagonal block is factored and
+// inverted by one warp (diag32), the panel below is L_ik = A_ik L_kk^-T and
+// the trailing lower blocks take the Schur update; then the off-diagonal
+// blocks of V = L^-1 are V_ij = -V_ii sum_{k=j}^{i-1} L_ik V_kj.
+// Writes L (lower part of A), V with its split (zeros above the diagonal) and
+// V^T with its split (zeros below), all over the full 128 x 128 block.
+__global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __restrict__ A, float* __restrict__ V,
+                                                                     float* __restrict__ V_hi,
+                                                                     float* __restrict__ V_lo,
+                                                                     float* __restrict__ VT,
+                                                                     float* __restrict__ VT_hi,
+                                                                     float* __restrict__ VT_lo, int ld, int off,
+                                                                     int* __restrict__ bad) {
     extern __shared__ float sm[];
-    float* sA = sm;                    // 128 x 129
-    float* sV = sm + kB * (kB + 1);    // 128 x 129
+    float* sA = sm;                 // 128 x kLd
+    float* sV = sA + kB * kLd;      // 128 x kLd
+    float* sS = sV + kB * kLd;      // 96 x kSLd scratch
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const size_t base = static_cast<size_t>(off) * ld + off;
-    for (int e = t; e < kB * kB; e += blockDim.x) {
-        const int i = e / kB, j = e % kB;
-        sA[i * (kB + 1) + j] = (j <= i) ? A[base + static_cast<size_t>(i) * ld + j] : 0.0f;
-        sV[i * (kB + 1) + j] = 0.0f;
+    pdl_wait();
+    pdl_trigger();
+#pragma unroll 4
+    for (int e = t; e < kB * kB; e += kBaseThreads) {
+        const int i = e >> 7, j = e & 127;
+        sA[i * kLd + j] = (j <= i) ? A[base + static_cast<size_t>(i) * ld + j] : 0.0f;
+        sV[i * kLd + j] = 0.0f;
     }
     __syncthreads();
-    for (int j = 0; j < kB; ++j) {
-        if (t == 0) {
-            const float dj = sA[j * (kB + 1) + j];
-            if (!(dj > 0.0f)) atomicExch(bad, 1);
-            sA[j * (kB + 1) + j] = dj > 0.0f ? __fsqrt_rn(dj) : 1.0f;
-        }
+#pragma unroll 1
+    for (int kb = 0; kb < 4; ++kb) {
+        const int o = 32 * kb;
+        if (warp == 0) diag32(sA + o * kLd + o, sV + o * kLd + o, lane, bad);
         __syncthreads();
-        const float piv = sA[j * (kB + 1) + j];
-        for (int i = j + 1 + t; i < kB; i += blockDim.x) sA[i * (kB + 1) + j] = __fdiv_rn(sA[i * (kB + 1) + j], piv);
+        const int prow = kB - o - 32;
+        if (prow == 0) break;
+        // panel: L[o+32+i][o+c] = sum_k A[o+32+i][o+k] V_kk[c][k], via the scratch
+#pragma unroll 1
+        for (int i = warp; i < prow; i += 16)
+            sS[i * kSLd + lane] = dot32(sA + (o + 32 + i) * kLd + o, sV + (o + lane) * kLd + o);
         __syncthreads();
-        for (int i = j + 1 + warp; i < kB; i += 32) {
-            const float lij = sA[i * (kB + 1) + j];
-            for (int k = j + 1 + lane; k <= i; k += 32)
-                sA[i * (kB + 1) + k] = __fsub_rn(sA[i * (kB + 1) + k], __fmul_rn(lij, sA[k * (kB + 1) + j]));
-        }
+#pragma unroll 1
+        for (int i = warp; i < prow; i += 16) sA[(o + 32 + i) * kLd + o + lane] = sS[i * kSLd + lane];
+        __syncthreads();
+        // trailing lower blocks: A[i][j] -= sum_k L[i][o+k] L[j][o+k]
+        const int nbt = prow / 32;
+#pragma unroll 1
+        for (int ib = 0; ib < nbt; ++ib)
+#pragma unroll 1
+            for (int jb = 0; jb <= ib; ++jb)
+#pragma unroll 1
+                for (int q = 0; q < 2; ++q) {
+                    const int i = o + 32 + 32 * ib + warp + 16 * q, j = o + 32 + 32 * jb + lane;
+                    sA[i * kLd + j] -= dot32(sA + i * kLd + o, sA + j * kLd + o);
+                }
         __syncthreads();
     }
-    // V = L^-1 by forward substitution, one column per thread.
-    if (t < kB) {
-        const int c = t;
-        sV[c * (kB + 1) + c] = __fdiv_rn(1.0f, sA[c * (kB + 1) + c]);
-        for (int i = c + 1; i < kB; ++i) {
-            float s = 0.0f;
-            for (int k = c; k < i; ++k) s = __fadd_rn(s, __fmul_rn(sA[i * (kB + 1) + k], sV[k * (kB + 1) + c]));
-            sV[i * (kB + 1) + c] = __fdiv_rn(-s, sA[i * (kB + 1) + i]);
-        }
+    // off-diagonal blocks of V, block row by block row
+#pragma unroll 1
+    for (int ib = 1; ib < 4; ++ib) {
+#pragma unroll 1
+        for (int jb = 0; jb < ib; ++jb)
+#pragma unroll 1
+            for (int q = 0; q < 2; ++q) {
+                const int i = warp + 16 * q;
+                const float* xr = sA + (32 * ib + i) * kLd;
+                const float* yc = sV + 32 * jb + lane;
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 2
+                for (int m = 32 * jb; m < 32 * ib; m += 4) {
+                    a0 = fmaf(xr[m], yc[m * kLd], a0);
+                    a1 = fmaf(xr[m + 1], yc[(m + 1) * kLd], a1);
+                    a2 = fmaf(xr[m + 2], yc[(m + 2) * kLd], a2);
+                    a3 = fmaf(xr[m + 3], yc[(m + 3) * kLd], a3);
+                }
+                sS[(jb * 32 + i) * kSLd + lane] = (a0 + a1) + (a2 + a3);
+            }
+        __syncthreads();
+#pragma unroll 1
+        for (int jb = 0; jb < ib; ++jb)
+#pragma unroll 1
+            for (int q = 0; q < 2; ++q) {
+                const int i = warp + 16 * q;
+                const float* vr = sV + (32 * ib + i) * kLd + 32 * ib;
+                const float* sc = sS + jb * 32 * kSLd + lane;
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 2
+                for (int m = 0; m < 32; m += 4) {
+                    a0 = fmaf(vr[m], sc[m * kSLd], a0);
+                    a1 = fmaf(vr[m + 1], sc[(m + 1) * kSLd], a1);
+                    a2 = fmaf(vr[m + 2], sc[(m + 2) * kSLd], a2);
+                    a3 = fmaf(vr[m + 3], sc[(m + 3) * kSLd], a3);
+                }
+                sV[(32 * ib + i) * kLd + 32 * jb + lane] = -((a0 + a1) + (a2 + a3));
+            }
+        __syncthreads();
     }
-    __syncthreads();
-    for (int e = t; e < kB * kB; e += blockDim.x) {
-        const int i = e / kB, j = e % kB;
+#pragma unroll 2
+    for (int e = t; e < kB * kB; e += kBaseThreads) {
+        const int i = e >> 7, j = e & 127;
         const size_t g = base + static_cast<size_t>(i) * ld + j;
-        if (j <= i) {
-            A[g] = sA[i * (kB + 1) + j];
-            const float v = sV[i * (kB + 1) + j];
-            const float h = tf32_round(v);
-            V[g] = v;
-            V_hi[g] = h;
-            V_lo[g] = v - h;
-        }
-        if (j >= i) {  // VT[i][j] = V[j][i]
-            const float v = sV[j * (kB + 1) + i];
-            const float h = tf32_round(v);
-            VT[g] = v;
-            VT_hi[g] = h;
-            VT_lo[g] = v - h;
-        }
+        if (j <= i) A[g] = sA[i * kLd + j];
+        const float v = sV[i * kLd + j];
+        const float h = tf32_round(v);
+        V[g] = v;
+        V_hi[g] = h;
+        V_lo[g] = v - h;
+        const float vt = sV[j * kLd + i];
+        const float ht = tf32_round(vt);
+        VT[g] = vt;
+        VT_hi[g] = ht;
+        VT_lo[g] = vt - ht;
     }
 }
+constexpr size_t kBaseSmem = (2 * kB * kLd + 3 * 32 * kSLd) * sizeof(float);
 
 // Ut = (P V P)^T on the lower triangle: Ut[i][j] = V[d-1-j][d-1-i], with split.
 __global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, float* __restrict__ Ut,
                                          float* __restrict__ Ut_hi, float* __restrict__ Ut_lo) {
     __shared__ float tile[32][33];
     const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // output tile (rows by.., cols bx..)
+    pdl_wait();
+    pdl_trigger();
     // source rows d-1-(bx+..), cols d-1-(by+..)
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
         const int sr = d - 1 - (bx + k), sc = d - 1 - (by + threadIdx.x);
@@ -174,80 +311,138 @@ __global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, flo
     }
 }
 
-// In-block OBS sweep of columns [i1, i1+128) for every row: one warp per row,
-// lane l holding columns 4l..4l+3 of the block.  M must be 4 here (the lane's
-// four columns are one group); N:4 with N in {1, 2, 3}.
-__global__ void __launch_bounds__(256) inblock_kernel(float* __restrict__ W, int r, int d, int i1,
-                                                      const float* __restrict__ Ut, int n_keep,
-                                                      uint8_t* __restrict__ mask, float* __restrict__ E_hi,
-                                                      float* __restrict__ E_lo) {
-    extern __shared__ float u1_raw[];
-    float (*U1)[kU1Ld] = reinterpret_cast<float (*)[kU1Ld]>(u1_raw);  // U1[q][j] = U[i1+q][i1+j] = Ut[i1+j][i1+q]
-    for (int e = threadIdx.x; e < kB * kB; e += blockDim.x) {
-        const int q = e % kB, j = e / kB;
-        U1[q][j] = (j >= q) ? Ut[static_cast<size_t>(i1 + j) * d + i1 + q] : 0.0f;
+// In-block OBS sweep of columns [i1, i1+128) for every row: one warp per two
+// rows (two independent dependency chains per warp), lane l holding columns
+// 4l..4l+3 of both rows.  M must be 4 here (the lane's four columns are one
+// group); N:4 with N in {1, 2, 3}.  The block of U sits in shared memory with
+// column j of row q at q*kLd + (j%4)*32 + j/4, so that the four values a lane
+// needs are bank-conflict free; 1/U_qq follows it.  Only pruned columns carry
+// an error (err = w_q / U_qq; a kept column's error is 0), so the propagation
+// loop runs over the pruned columns of either row.  Errors go to E (row pitch
+// ldE) at the block's own columns, with their tf32 split.
+constexpr int kIbThreads = 512;
+constexpr int kIbRows = 2 * (kIbThreads / 32);
+constexpr size_t kIbSmem = (kB * kLd + kB) * sizeof(float);
+
+__device__ __forceinline__ uint32_t obs_keep_bits(const float (&w)[4], const float* rv, int n_keep) {
+    float s[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float x = w[k] * rv[k];
+        s[k] = x * x;
+    }
+    uint32_t bits = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        int rank = 0;
+#pragma unroll
+        for (int o = 0; o < 4; ++o) rank += (s[o] < s[k] || (o < k && s[o] == s[k])) ? 1 : 0;
+        if (rank >= 4 - n_keep) bits |= 1u << k;
+    }
+    return bits;
+}
+
+__global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, int d, int i1,
+                                                             const float* __restrict__ Ut, int n_keep,
+                                                             uint8_t* __restrict__ mask, float* __restrict__ E_hi,
+                                                             float* __restrict__ E_lo, long long ldE) {
+    extern __shared__ float u1[];
+    float* rinv = u1 + kB * kLd;
+    pdl_wait();
+    pdl_trigger();
+    // U[i1+q][i1+j] = Ut[i1+j][i1+q] (j >= q), eight loads in flight per thread
+    for (int b = threadIdx.x; b < kB * kB; b += kIbThreads * 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
+            v[u] = (j >= q) ? Ut[static_cast<size_t>(i1 + j) * d + i1 + q] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
+            u1[q * kLd + (j & 3) * 32 + (j >> 2)] = v[u];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < kB) {
+        const int q = threadIdx.x;
+        rinv[q] = __frcp_rn(u1[q * kLd + (q & 3) * 32 + (q >> 2)]);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (row >= r) return;
-    float* wr = W + static_cast<size_t>(row) * d + i1;
-    float w[4];
+    const size_t row0 = static_cast<size_t>(blockIdx.x) * kIbRows + 2 * warp;
+    float* wr0 = W + row0 * d + i1;
+    float* wr1 = wr0 + d;
+    float w0[4], w1[4];
     {
-        const float4 x = reinterpret_cast<const float4*>(wr)[lane];
-        w[0] = x.x; w[1] = x.y; w[2] = x.z; w[3] = x.w;
+        const float4 x = reinterpret_cast<const float4*>(wr0)[lane];
+        const float4 y = reinterpret_cast<const float4*>(wr1)[lane];
+        w0[0] = x.x; w0[1] = x.y; w0[2] = x.z; w0[3] = x.w;
+        w1[0] = y.x; w1[1] = y.y; w1[2] = y.z; w1[3] = y.w;
     }
-    float err[4] = {0, 0, 0, 0};
-    uint32_t keep_bits = 0;
+    float e0[4] = {0, 0, 0, 0}, e1[4] = {0, 0, 0, 0};
+    uint32_t own0 = 0, own1 = 0;
     for (int g = 0; g < kB / 4; ++g) {
+        uint32_t b0 = 0, b1 = 0;
         if (lane == g) {
-            // saliency w^2 / U_qq^2 for the group; prune the 4 - n_keep smallest, lowest index first
-            float s[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float u = U1[4 * g + k][4 * g + k];
-                s[k] = __fdiv_rn(__fmul_rn(w[k], w[k]), __fmul_rn(u, u));
-            }
-            uint32_t bits = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                int rank = 0;
-#pragma unroll
-                for (int o = 0; o < 4; ++o) rank += (s[o] < s[k] || (o < k && s[o] == s[k])) ? 1 : 0;
-                if (rank >= 4 - n_keep) bits |= 1u << k;
-            }
-            keep_bits = bits;
+            b0 = obs_keep_bits(w0, rinv + 4 * g, n_keep);
+            b1 = obs_keep_bits(w1, rinv + 4 * g, n_keep);
+            own0 = b0;
+            own1 = b1;
         }
-        const uint32_t bits = __shfl_sync(0xFFFFFFFFu, keep_bits, g);
+        b0 = __shfl_sync(kFull, b0, g);
+        b1 = __shfl_sync(kFull, b1, g);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
+            const bool p0 = !((b0 >> k) & 1u), p1 = !((b1 >> k) & 1u);  // warp-uniform
+            if (!p0 && !p1) continue;
             const int q = 4 * g + k;
-            float e = 0.0f;
+            float x0 = 0.0f, x1 = 0.0f;
             if (lane == g) {
-                const float kept = ((bits >> k) & 1u) ? w[k] : 0.0f;
-                e = __fdiv_rn(__fsub_rn(w[k], kept), U1[q][q]);
-                err[k] = e;
+                const float rq = rinv[q];
+                x0 = p0 ? w0[k] * rq : 0.0f;
+                x1 = p1 ? w1[k] * rq : 0.0f;
+                e0[k] = x0;
+                e1[k] = x1;
             }
-            e = __shfl_sync(0xFFFFFFFFu, e, g);
-            // w_j -= e * U[q][j] for j >= q (columns of later lanes, and this lane's k' >= k)
+            x0 = __shfl_sync(kFull, x0, g);
+            x1 = __shfl_sync(kFull, x1, g);
+            const float* ur = u1 + q * kLd + lane;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-                const int j = 4 * lane + kk;
-                if (j >= q) w[kk] = __fsub_rn(w[kk], __fmul_rn(e, U1[q][j]));
+                if (4 * lane + kk > q) {
+                    const float u = ur[kk * 32];
+                    w0[kk] = fmaf(-x0, u, w0[kk]);
+                    w1[kk] = fmaf(-x1, u, w1[kk]);
+                }
             }
-            if (lane == g) w[k] = ((bits >> k) & 1u) ? w[k] : 0.0f;
+        }
+        if (lane == g) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (!((b0 >> k) & 1u)) w0[k] = 0.0f;
+                if (!((b1 >> k) & 1u)) w1[k] = 0.0f;
+            }
         }
     }
-    // w now holds the kept (updated) values of this lane's group; pruned ones are 0
-    reinterpret_cast<float4*>(wr)[lane] = make_float4(w[0], w[1], w[2], w[3]);
-    mask[(static_cast<size_t>(row) * d + i1) / 4 + lane] = static_cast<uint8_t>(keep_bits);
+    reinterpret_cast<float4*>(wr0)[lane] = make_float4(w0[0], w0[1], w0[2], w0[3]);
+    reinterpret_cast<float4*>(wr1)[lane] = make_float4(w1[0], w1[1], w1[2], w1[3]);
+    mask[(row0 * d + i1) / 4 + lane] = static_cast<uint8_t>(own0);
+    mask[((row0 + 1) * d + i1) / 4 + lane] = static_cast<uint8_t>(own1);
     float4 h, l;
-    h.x = tf32_round(err[0]); l.x = err[0] - h.x;
-    h.y = tf32_round(err[1]); l.y = err[1] - h.y;
-    h.z = tf32_round(err[2]); l.z = err[2] - h.z;
-    h.w = tf32_round(err[3]); l.w = err[3] - h.w;
-    reinterpret_cast<float4*>(E_hi + static_cast<size_t>(row) * kB)[lane] = h;
-    reinterpret_cast<float4*>(E_lo + static_cast<size_t>(row) * kB)[lane] = l;
+    h.x = tf32_round(e0[0]); l.x = e0[0] - h.x;
+    h.y = tf32_round(e0[1]); l.y = e0[1] - h.y;
+    h.z = tf32_round(e0[2]); l.z = e0[2] - h.z;
+    h.w = tf32_round(e0[3]); l.w = e0[3] - h.w;
+    reinterpret_cast<float4*>(E_hi + row0 * ldE + i1)[lane] = h;
+    reinterpret_cast<float4*>(E_lo + row0 * ldE + i1)[lane] = l;
+    h.x = tf32_round(e1[0]); l.x = e1[0] - h.x;
+    h.y = tf32_round(e1[1]); l.y = e1[1] - h.y;
+    h.z = tf32_round(e1[2]); l.z = e1[2] - h.z;
+    h.w = tf32_round(e1[3]); l.w = e1[3] - h.w;
+    reinterpret_cast<float4*>(E_hi + (row0 + 1) * ldE + i1)[lane] = h;
+    reinterpret_cast<float4*>(E_lo + (row0 + 1) * ldE + i1)[lane] = l;
 }
 
 struct Work {
@@ -296,15 +491,15 @@ int trsm(Work& w, long long r0, int m, long long c0, int n, cudaStream_t st) {
 
 // Recursive Cholesky of A[off : off+n] (lower, in place, with split); the
 // 128 x 128 diagonal blocks also get their inverses in V / VT.
-int chol(Work& w, int off, int n, cudaStream_t st, size_t base_smem) {
+int chol(Work& w, int off, int n, cudaStream_t st) {
     const long long d = w.d;
     if (n == kB) {
-        base_chol_inv_kernel<<<1, 1024, base_smem, st>>>(w.A, w.V, w.V_hi, w.V_lo, w.VT, w.VT_hi, w.VT_lo, w.d, off,
-                                                         w.bad);
-        return check_launch("base_chol_inv_kernel");
+        const cudaError_t e = launch_pdl(base_chol_inv_kernel, dim3(1), dim3(kBaseThreads), kBaseSmem, st, w.A, w.V,
+                                         w.V_hi, w.V_lo, w.VT, w.VT_hi, w.VT_lo, w.d, off, w.bad);
+        return e == cudaSuccess ? check_launch("base_chol_inv_kernel") : cuda_fail(e, "base_chol_inv_kernel launch");
     }
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
-    int rc = chol(w, off, n1, st, base_smem);
+    int rc = chol(w, off, n1, st);
     if (rc) return rc;
     const long long o1 = off + n1;
     if ((rc = trsm(w, o1, n2, off, n1, st))) return rc;  // L21 = A21 L11^-T
@@ -319,11 +514,14 @@ int chol(Work& w, int off, int n, cudaStream_t st, size_t base_smem) {
                        n2, n1, o, st)))
             return rc;
     }
-    return chol(w, off + n1, n2, st, base_smem);
+    return chol(w, off + n1, n2, st);
 }
 
 // Recursive inverse V = L^-1 of the factor in A (diagonal 128-blocks already
 // inverted by the base kernel): V21 = -V22 (L21 V11), with V^T kept alongside.
+// Both products take a triangular left operand, so each output tile row runs
+// only over the K tiles inside the triangle (half the dense work); tiles
+// outside it are never read and need not be zero.
 int trtri(Work& w, int off, int n, cudaStream_t st) {
     if (n == kB) return TB_OK;
     const long long d = w.d;
@@ -337,6 +535,7 @@ int trtri(Work& w, int off, int n, cudaStream_t st) {
         umma::GemmOut o{};
         o.C_hi = w.T_hi; o.C_lo = w.T_lo; o.ld_split = n2;
         o.alpha = 1.0f; o.beta = 0.0f;
+        o.tri_a = 1;  // V11^T upper
         if ((rc = gemm(at(w.VT_hi, off, off), at(w.VT_lo, off, off), d, at(w.A_hi, o1, off), at(w.A_lo, o1, off), d,
                        n1, n2, n1, o, st)))
             return rc;
@@ -347,9 +546,45 @@ int trtri(Work& w, int off, int n, cudaStream_t st) {
         o.C_hi = at(w.V_hi, o1, off); o.C_lo = at(w.V_lo, o1, off); o.ld_split = d;
         o.Ct = at(w.VT, off, o1); o.ldct = d;
         o.alpha = -1.0f; o.beta = 0.0f;
+        o.tri_a = 2;  // V22 lower
         if ((rc = gemm(at(w.V_hi, o1, o1), at(w.V_lo, o1, o1), d, w.T_hi, w.T_lo, n2, n2, n1, n2, o, st))) return rc;
     }
     return tb_split_tf32_2d(at(w.VT, off, o1), at(w.VT_hi, off, o1), at(w.VT_lo, off, o1), n1, n2, d, st);
+}
+
+struct Sweep {
+    float* W;
+    int r, d, n_keep;
+    const float *Ut, *Ut_hi, *Ut_lo;
+    uint8_t* mask;
+    float *E_hi, *E_lo;  // r x d, pitch d
+};
+
+// Column sweep of [a, a+n): recursive on the columns, like the triangular
+// solve.  After the left half is swept, its errors update the right half in
+// one GEMM, W[:, a+n1 : a+n] -= E[:, a : a+n1] U[a : a+n1, a+n1 : a+n], with
+// U[a : a+n1, a+n1 : a+n] = (Ut[a+n1 : a+n, a : a+n1])^T.  Every column block
+// therefore sees all earlier errors before its own sweep, as in the
+// block-by-block lazy update, but W is read and written once per level
+// instead of once per block, and the products have K up to d/2.
+int sweep(const Sweep& s, int a, int n, cudaStream_t st) {
+    const long long d = s.d;
+    if (n == kB) {
+        const cudaError_t e = launch_pdl(inblock_kernel, dim3(s.r / kIbRows), dim3(kIbThreads), kIbSmem, st, s.W, s.d,
+                                         a, s.Ut, s.n_keep, s.mask, s.E_hi, s.E_lo, d);
+        return e == cudaSuccess ? check_launch("inblock_kernel") : cuda_fail(e, "inblock_kernel launch");
+    }
+    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
+    int rc = sweep(s, a, n1, st);
+    if (rc) return rc;
+    umma::GemmOut o{};
+    o.C = s.W + a + n1; o.ldc = d;
+    o.Cin = s.W + a + n1; o.ldcin = d;
+    o.alpha = -1.0f; o.beta = 1.0f;
+    if ((rc = umma::gemm_nt(umma::kTF32x3, {s.E_hi + a, s.E_lo + a, d},
+                            {s.Ut_hi + (a + n1) * d + a, s.Ut_lo + (a + n1) * d + a, d}, s.r, n2, n1, o, st)))
+        return rc;
+    return sweep(s, a + n1, n2, st);
 }
 
 }  // namespace
@@ -357,6 +592,8 @@ int trtri(Work& w, int off, int n, cudaStream_t st) {
 // Strided 2-D tf32 split (rows x cols block with leading dimension ld).
 __global__ void split2d_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo, int rows,
                                int cols, long long ld) {
+    pdl_wait();
+    pdl_trigger();
     const size_t total = static_cast<size_t>(rows) * cols;
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
         const size_t g = (e / cols) * ld + e % cols;
@@ -370,8 +607,8 @@ __global__ void split2d_kernel(const float* __restrict__ x, float* __restrict__ 
 int tb_split_tf32_2d(const float* x, float* hi, float* lo, int rows, int cols, long long ld, cudaStream_t st) {
     const size_t total = static_cast<size_t>(rows) * cols;
     const unsigned grid = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 148u * 16u));
-    split2d_kernel<<<grid, 256, 0, st>>>(x, hi, lo, rows, cols, ld);
-    return check_launch("split2d_kernel");
+    const cudaError_t e = launch_pdl(split2d_kernel, dim3(grid), dim3(256), 0, st, x, hi, lo, rows, cols, ld);
+    return e == cudaSuccess ? check_launch("split2d_kernel") : cuda_fail(e, "split2d_kernel launch");
 }
 
 namespace {
@@ -443,9 +680,12 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     if (rc) return rc;
     auto st = static_cast<cudaStream_t>(stream);
     const size_t dd = static_cast<size_t>(d) * d;
-    // Workspace: 11 d x d FP32 matrices, the error panel split and two scalars.
+    const size_t rd = static_cast<size_t>(r) * d;
+    // Workspace: 9 d x d FP32 matrices (A, V, V^T with their splits), the
+    // trtri temporary T (at most d^2 / 4, with split), the error matrix E
+    // (r x d, with split) and two scalars.
     float* ws = nullptr;
-    const size_t ws_floats = 11 * dd + 2 * static_cast<size_t>(r) * kB + 64;
+    const size_t ws_floats = 9 * dd + 2 * (dd / 4) + 2 * rd + 64;
     if ((rc = workspace(ws_floats, &ws))) return rc;
     cudaError_t e = cudaSuccess;
     Work w{};
@@ -453,44 +693,32 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     w.A = ws; w.A_hi = ws + dd; w.A_lo = ws + 2 * dd;
     w.V = ws + 3 * dd; w.V_hi = ws + 4 * dd; w.V_lo = ws + 5 * dd;
     w.VT = ws + 6 * dd; w.VT_hi = ws + 7 * dd; w.VT_lo = ws + 8 * dd;
-    w.T_hi = ws + 9 * dd; w.T_lo = ws + 10 * dd;
-    float* E_hi = ws + 11 * dd;
-    float* E_lo = E_hi + static_cast<size_t>(r) * kB;
-    double* dsum = reinterpret_cast<double*>(E_lo + static_cast<size_t>(r) * kB);
+    w.T_hi = ws + 9 * dd; w.T_lo = w.T_hi + dd / 4;
+    float* E_hi = w.T_lo + dd / 4;
+    float* E_lo = E_hi + rd;
+    double* dsum = reinterpret_cast<double*>(E_lo + rd);
     w.bad = reinterpret_cast<int*>(dsum + 1);
-    const size_t base_smem = 2 * kB * (kB + 1) * sizeof(float);
-    const size_t u1_smem = kB * kU1Ld * sizeof(float);
-    e = cudaFuncSetAttribute(base_chol_inv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(base_smem));
+    e = cudaFuncSetAttribute(base_chol_inv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kBaseSmem));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(inblock_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(u1_smem));
-    if (e == cudaSuccess) e = cudaMemsetAsync(w.V, 0, 6 * dd * sizeof(float), st);  // V and VT (+ splits) triangles
+        e = cudaFuncSetAttribute(inblock_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kIbSmem));
     if (e == cudaSuccess) e = cudaMemsetAsync(w.bad, 0, sizeof(int), st);
     if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt setup");
-    diag_sum_kernel<<<1, 1024, 0, st>>>(H, d, dsum);
-    reverse_damp_kernel<<<148 * 16, 256, 0, st>>>(H, d, dsum, damp_frac, w.A, w.A_hi, w.A_lo);
-    rc = check_launch("hessian prep");
-    if (!rc) rc = chol(w, 0, d, st, base_smem);
+    e = launch_pdl(diag_sum_kernel, dim3(1), dim3(1024), 0, st, H, d, dsum);
+    if (e == cudaSuccess)
+        e = launch_pdl(reverse_damp_kernel, dim3(d / 32, d / 32), dim3(32, 8), 0, st, H, d,
+                       static_cast<const double*>(dsum), damp_frac, w.A, w.A_hi, w.A_lo);
+    rc = e == cudaSuccess ? check_launch("hessian prep") : cuda_fail(e, "hessian prep launch");
+    if (!rc) rc = chol(w, 0, d, st);
     if (!rc) rc = trtri(w, 0, d, st);
     // Ut (lower) = (P V P)^T into A's buffers (A is no longer needed).
     float *Ut = w.A, *Ut_hi = w.A_hi, *Ut_lo = w.A_lo;
     if (!rc) {
-        reverse_transpose_kernel<<<dim3(d / 32, d / 32), dim3(32, 8), 0, st>>>(w.V, d, Ut, Ut_hi, Ut_lo);
-        rc = check_launch("reverse_transpose_kernel");
+        e = launch_pdl(reverse_transpose_kernel, dim3(d / 32, d / 32), dim3(32, 8), 0, st,
+                       static_cast<const float*>(w.V), d, Ut, Ut_hi, Ut_lo);
+        rc = e == cudaSuccess ? check_launch("reverse_transpose_kernel") : cuda_fail(e, "reverse_transpose launch");
     }
-    for (int i1 = 0; !rc && i1 < d; i1 += kB) {
-        inblock_kernel<<<r / 8, 256, u1_smem, st>>>(W, r, d, i1, Ut, n_keep, mask, E_hi, E_lo);
-        if ((rc = check_launch("inblock_kernel"))) break;
-        const int i2 = i1 + kB;
-        if (i2 < d) {  // W[:, i2:] -= E U[i1:i2, i2:] = E (Ut[i2:, i1:i2])^T
-            umma::GemmOut o{};
-            o.C = W + i2; o.ldc = d;
-            o.Cin = W + i2; o.ldcin = d;
-            o.alpha = -1.0f; o.beta = 1.0f;
-            rc = umma::gemm_nt(umma::kTF32x3, {E_hi, E_lo, kB},
-                               {Ut_hi + static_cast<size_t>(i2) * d + i1, Ut_lo + static_cast<size_t>(i2) * d + i1, d},
-                               r, d - i2, kB, o, st);
-        }
-    }
+    if (!rc) rc = sweep(Sweep{W, r, d, n_keep, Ut, Ut_hi, Ut_lo, mask, E_hi, E_lo}, 0, d, st);
     int bad = 0;
     if (!rc && ut_out) {
         e = cudaMemcpyAsync(ut_out, Ut, dd * sizeof(float), cudaMemcpyDeviceToDevice, st);

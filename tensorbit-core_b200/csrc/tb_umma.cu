@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <mutex>
 
+#include "tb_pdl.cuh"
 #include "tb_runtime.h"
 #include "tb_umma.cuh"
 
@@ -115,6 +116,7 @@ __device__ __forceinline__ float tf32_hi(float x) {
 // nearest) while the next group runs in the other buffer.
 constexpr int kGroup = 4;
 constexpr int kThreadsGemm = 192;
+constexpr int kStagePitch = kTile + 4;  // epilogue staging pitch (floats): float4 rows without bank conflicts
 
 template <int KIND, int STAGES>
 __global__ void __launch_bounds__(kThreadsGemm, 1)
@@ -136,8 +138,22 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ngroups = (nk + kGroup - 1) / kGroup;
+    // K slices [kc0, kc0 + nkr) of this tile row (all of them unless A is triangular)
+    constexpr int kPerTile = kTile / kElems;
+    int kc0 = 0, kc1 = nk;
+    if (out.tri_a == 1) kc0 = min(nk, tm * kPerTile);
+    else if (out.tri_a == 2) kc1 = min(nk, (tm + 1) * kPerTile);
+    const int nkr = max(0, kc1 - kc0);
+    const int ngroups = (nkr + kGroup - 1) / kGroup;
 
+    if (threadIdx.x == 32 * 4) {  // the TMA thread: fetch the descriptors while the CTA sets up
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tB0)) : "memory");
+        if constexpr (KIND == kTF32x3) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA1)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tB1)) : "memory");
+        }
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
@@ -159,12 +175,16 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Everything above touched no global memory; the operands and outputs may
+    // belong to the kernel before this one in the stream.
+    pdl_wait();
+    pdl_trigger();
     auto tile = [&](int s, int op) { return smem_u32(smem + (s * kOps + op) * kTileBytes); };
 
     if (warp == 4) {
         if (lane == 0) {  // TMA producer
             int issued = 0;
-            for (int kc = 0; kc < nk; ++kc) {
+            for (int kc = 0; kc < nkr; ++kc) {
                 const int s = kc % STAGES;
                 if (kc >= STAGES && !mbar_wait(smem_u32(&empty[s]), ((kc / STAGES) - 1) & 1)) {
                     *abort_flag = 1;
@@ -173,7 +193,7 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
                 if (*abort_flag) break;
                 const uint32_t bar = smem_u32(&full[s]);
                 mbar_expect_tx(bar, kOps * kTileBytes);
-                const int x = kc * kElems;
+                const int x = (kc0 + kc) * kElems;
                 tma_load_2d(tile(s, 0), &tA0, x, tm * kTile, bar);
                 tma_load_2d(tile(s, 1), &tB0, x, tn * kTile, bar);
                 if constexpr (KIND == kTF32x3) {
@@ -196,7 +216,7 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
                 if (g >= 2 && !mbar_wait(smem_u32(&accempty[b]), ((g >> 1) - 1) & 1)) { ok = false; break; }
                 fence_after();
                 const uint32_t acc_t = tmem + static_cast<uint32_t>(b * kTile);
-                const int k_end = std::min(nk, (g + 1) * kGroup);
+                const int k_end = std::min(nkr, (g + 1) * kGroup);
                 for (int kc = g * kGroup; kc < k_end; ++kc) {
                     const int s = kc % STAGES;
                     if (*abort_flag || !mbar_wait(smem_u32(&full[s]), (kc / STAGES) & 1)) { ok = false; break; }
@@ -229,7 +249,6 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
         __syncwarp();
     } else {
         // Warps 0-3: promote each finished group into FP32 registers, then store.
-        const int row = warp * 32 + lane;
         float acc[kTile];
 #pragma unroll
         for (int j = 0; j < kTile; ++j) acc[j] = 0.0f;
@@ -253,47 +272,64 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
         if (!ok) {
             if (lane == 0) atomicExch(&g_umma_error, 1);
         } else {
-            const long long grow = static_cast<long long>(tm) * kTile + row;
+            // All MMAs have completed, so the operand ring is free: stage this
+            // warp's 32 x 128 block (row = lane) with a 132-float pitch, then
+            // handle one output row per step with lane l on columns 4l..4l+3.
+            static_assert(4 * 32 * kStagePitch * 4 <= STAGES * kOps * kTileBytes, "epilogue staging exceeds the ring");
+            float* sbuf = reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch;
 #pragma unroll
-            for (int c = 0; c < kTile / 32; ++c) {
-                const long long gcol = static_cast<long long>(tn) * kTile + c * 32;
-                float o[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) o[j] = out.alpha * acc[c * 32 + j];
+            for (int c = 0; c < kTile / 4; ++c)
+                *reinterpret_cast<float4*>(sbuf + lane * kStagePitch + 4 * c) =
+                    make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+            __syncwarp();
+            const long long grow0 = static_cast<long long>(tm) * kTile + warp * 32;
+            const long long gcol = static_cast<long long>(tn) * kTile + 4 * lane;
+            constexpr int kBatch = 8;  // rows whose Cin loads are in flight together
+            for (int rb = 0; rb < 32; rb += kBatch) {
+                float4 cin[kBatch];
                 if (out.beta != 0.0f) {
-                    const float4* cin = reinterpret_cast<const float4*>(out.Cin + grow * out.ldcin + gcol);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 x = cin[q];
-                        o[4 * q + 0] += out.beta * x.x;
-                        o[4 * q + 1] += out.beta * x.y;
-                        o[4 * q + 2] += out.beta * x.z;
-                        o[4 * q + 3] += out.beta * x.w;
+                    for (int u = 0; u < kBatch; ++u)
+                        cin[u] = *reinterpret_cast<const float4*>(out.Cin + (grow0 + rb + u) * out.ldcin + gcol);
+                }
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) {
+                    const long long grow = grow0 + rb + u;
+                    float4* sp = reinterpret_cast<float4*>(sbuf + (rb + u) * kStagePitch + 4 * lane);
+                    const float4 a = *sp;
+                    float o[4] = {out.alpha * a.x, out.alpha * a.y, out.alpha * a.z, out.alpha * a.w};
+                    if (out.beta != 0.0f) {
+                        o[0] += out.beta * cin[u].x;
+                        o[1] += out.beta * cin[u].y;
+                        o[2] += out.beta * cin[u].z;
+                        o[3] += out.beta * cin[u].w;
                     }
-                }
-                if (out.C) {
-                    float4* dst = reinterpret_cast<float4*>(out.C + grow * out.ldc + gcol);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) dst[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-                }
-                if (out.C_hi) {
-                    float4* hi = reinterpret_cast<float4*>(out.C_hi + grow * out.ld_split + gcol);
-                    float4* lo = reinterpret_cast<float4*>(out.C_lo + grow * out.ld_split + gcol);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
+                    const float4 ov = make_float4(o[0], o[1], o[2], o[3]);
+                    if (out.C) *reinterpret_cast<float4*>(out.C + grow * out.ldc + gcol) = ov;
+                    if (out.C_hi) {
                         float h[4], l[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            h[e] = tf32_hi(o[4 * q + e]);
-                            l[e] = o[4 * q + e] - h[e];
+                            h[e] = tf32_hi(o[e]);
+                            l[e] = o[e] - h[e];
                         }
-                        hi[q] = make_float4(h[0], h[1], h[2], h[3]);
-                        lo[q] = make_float4(l[0], l[1], l[2], l[3]);
+                        *reinterpret_cast<float4*>(out.C_hi + grow * out.ld_split + gcol) = make_float4(h[0], h[1], h[2], h[3]);
+                        *reinterpret_cast<float4*>(out.C_lo + grow * out.ld_split + gcol) = make_float4(l[0], l[1], l[2], l[3]);
                     }
+                    if (out.Ct) *sp = ov;  // final values back for the transposed copy
                 }
-                if (out.Ct) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) out.Ct[(gcol + j) * out.ldct + grow] = o[j];
+            }
+            if (out.Ct) {  // Ct[col][row]: lane = row again, 32 consecutive rows per store
+                __syncwarp();
+#pragma unroll 4
+                for (int c = 0; c < kTile / 4; ++c) {
+                    const float4 x = *reinterpret_cast<const float4*>(sbuf + lane * kStagePitch + 4 * c);
+                    const long long col = static_cast<long long>(tn) * kTile + 4 * c;
+                    const long long row = grow0 + lane;
+                    out.Ct[(col + 0) * out.ldct + row] = x.x;
+                    out.Ct[(col + 1) * out.ldct + row] = x.y;
+                    out.Ct[(col + 2) * out.ldct + row] = x.z;
+                    out.Ct[(col + 3) * out.ldct + row] = x.w;
                 }
             }
         }
@@ -350,9 +386,9 @@ int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0, 
                                     static_cast<int>(smem));
     });
     if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute(gemm_nt_kernel)");
-    dim3 grid(N / kTile, M / kTile);
-    gemm_nt_kernel<KIND, STAGES><<<grid, kThreadsGemm, smem, st>>>(a0, a1, b0, b1, nk, out);
-    return check_launch("gemm_nt_kernel");
+    const cudaError_t e = launch_pdl(gemm_nt_kernel<KIND, STAGES>, dim3(N / kTile, M / kTile), dim3(kThreadsGemm),
+                                     smem, st, a0, a1, b0, b1, nk, out);
+    return e == cudaSuccess ? check_launch("gemm_nt_kernel") : cuda_fail(e, "gemm_nt_kernel launch");
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -374,6 +410,8 @@ int gemm_nt(Kind kind, const Operand& A, const Operand& B, int M, int N, int K, 
         (out.C_hi && (!out.C_lo || !aligned16(out.C_hi) || !aligned16(out.C_lo) || out.ld_split % 4 || out.ld_split < N)) ||
         (out.Ct && out.ldct < M))
         return fail(TB_ERR_ARG, "gemm_nt: output pointers must be 16-byte aligned with ld >= N and ld % 4 == 0");
+    if (out.tri_a && (out.tri_a > 2 || M != K))
+        return fail(TB_ERR_ARG, "gemm_nt: a triangular A must be square (M == K)");
     const bool bf16 = kind == kBF16;
     CUtensorMap a0{}, a1{}, b0{}, b1{};
     int rc = make_map(&a0, A.hi, bf16, M, K, A.ld);

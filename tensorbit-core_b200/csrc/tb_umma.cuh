@@ -12,7 +12,8 @@
 //   warps 0-3      read each finished buffer with tcgen05.ld (warp w owns TMEM
 //                  lanes 32w..32w+31 = output rows), add it into FP32 registers
 //                  with round-to-nearest (the tensor core's own accumulation
-//                  truncates), and apply the epilogue.
+//                  truncates), and apply the epilogue through shared memory
+//                  (the drained operand ring), one coalesced row at a time.
 // Kinds:
 //   kTF32x3  FP32-accurate product from TF32 tensor cores: every operand is
 //            given as hi = tf32(x) and lo = x - hi, and the tile accumulates
@@ -42,6 +43,8 @@ struct GemmOut {
     long long ldct;
     float alpha, beta;
     int lower_only;      // compute only tiles with tile_row >= tile_col
+    int tri_a;           // A is square and triangular (M == K): 1 = upper, so output tile row
+                         // t runs over K tiles t.. only; 2 = lower, K tiles ..t only; 0 = dense
 };
 
 // Operand view for the host wrapper: row-major [rows, K] with leading dimension ld (elements).
