@@ -101,22 +101,29 @@ __global__ void __launch_bounds__(256) reverse_damp_kernel(const float* __restri
 }
 
 constexpr unsigned kFull = 0xFFFFFFFFu;
-constexpr int kLd = kB + 1;          // shared-memory pitch of the 128 x 128 blocks
+constexpr int kP = kB + 4;           // shared-memory pitch of the 128 x 128 blocks (16-byte rows)
 constexpr int kBaseThreads = 512;
-constexpr int kSLd = 33;
+constexpr int kSP = 36;              // pitch of the 32 x 32 scratch blocks
 
 // Cholesky factor and inverse of one 32 x 32 diagonal block by one warp.
 // Lane i keeps row i in registers relative to the current column j
 // (a[k] = D[i][j+k]) and shifts the row by one after each column, so the
 // column loop stays rolled with constant register indices: the kernel runs
 // once per launch, and compact code matters more than unrolling here.
-// D (pitch kLd) holds the Schur-updated block on and below the diagonal; on
-// return it holds L_kk with zeros above, Q (pitch kLd) holds L_kk^-1 with
-// zeros above.  Pivots <= 0 set *bad (and continue with 1).
-__device__ __noinline__ void diag32(float* D, float* Q, int lane, int* bad) {
+// D (pitch kP) holds the Schur-updated block on and below the diagonal; on
+// return it holds L_kk with zeros above; Q gets L_kk^-1 (zeros above) and QT
+// its transpose (zeros below), both pitch kP.  Pivots <= 0 set *bad (and
+// continue with 1).
+__device__ __noinline__ void diag32(float* D, float* Q, float* QT, int lane, int* bad) {
     float a[32];
 #pragma unroll
-    for (int k = 0; k < 32; ++k) a[k] = (k <= lane) ? D[lane * kLd + k] : 0.0f;
+    for (int k = 0; k < 32; k += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(D + lane * kP + k);
+        a[k] = (k <= lane) ? v.x : 0.0f;
+        a[k + 1] = (k + 1 <= lane) ? v.y : 0.0f;
+        a[k + 2] = (k + 2 <= lane) ? v.z : 0.0f;
+        a[k + 3] = (k + 3 <= lane) ? v.w : 0.0f;
+    }
     float my_rinv = 1.0f;
     bool all_ok = true;
 #pragma unroll 1
@@ -128,7 +135,7 @@ __device__ __noinline__ void diag32(float* D, float* Q, int lane, int* bad) {
         // lanes above j hold a[0] = 0 (upper triangle)
         const float l = (lane == j) ? (ok ? djj * rj : 1.0f) : a[0] * rj;
         if (lane == j) my_rinv = rj;
-        D[lane * kLd + j] = l;
+        D[lane * kP + j] = l;
 #pragma unroll
         for (int k = 1; k < 32; ++k) {  // branch-free: the shuffles issue back to back
             const float lk = __shfl_sync(kFull, l, (j + k) & 31);
@@ -147,10 +154,11 @@ __device__ __noinline__ void diag32(float* D, float* Q, int lane, int* bad) {
 #pragma unroll 1
     for (int j = 0; j < 32; ++j) {
         const float xj = x[0] * __shfl_sync(kFull, my_rinv, j);
-        Q[j * kLd + lane] = xj;
+        Q[j * kP + lane] = xj;
+        QT[lane * kP + j] = xj;
 #pragma unroll
         for (int k = 1; k < 32; ++k)  // slots past row 31 hold values that are never stored
-            x[k] = fmaf(-xj, D[min(j + k, 31) * kLd + j], x[k]);
+            x[k] = fmaf(-xj, D[min(j + k, 31) * kP + j], x[k]);
 #pragma unroll
         for (int k = 0; k < 31; ++k) x[k] = x[k + 1];
         x[31] = 0.0f;
@@ -158,24 +166,33 @@ __device__ __noinline__ void diag32(float* D, float* Q, int lane, int* bad) {
     __syncwarp();
 }
 
-// 32-term dot product of two shared-memory rows (four partial sums).
-__device__ __forceinline__ float dot32(const float* x, const float* y) {
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+// Four rows by one column of a row-by-row product: acc[r] = sum_{k<K}
+// X[r*px + k] Y[k], with 128-bit shared-memory loads (X broadcast across the
+// warp, Y one row per lane); K is a multiple of 4 and the rows 16-byte aligned.
+__device__ __forceinline__ void dot4x1(const float* X, int px, const float* Y, int K, float (&acc)[4]) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r] = 0.0f;
 #pragma unroll 2
-    for (int k = 0; k < 32; k += 4) {
-        a0 = fmaf(x[k], y[k], a0);
-        a1 = fmaf(x[k + 1], y[k + 1], a1);
-        a2 = fmaf(x[k + 2], y[k + 2], a2);
-        a3 = fmaf(x[k + 3], y[k + 3], a3);
+    for (int k = 0; k < K; k += 4) {
+        const float4 y = *reinterpret_cast<const float4*>(Y + k);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float4 x = *reinterpret_cast<const float4*>(X + r * px + k);
+            acc[r] = fmaf(x.x, y.x, acc[r]);
+            acc[r] = fmaf(x.y, y.y, acc[r]);
+            acc[r] = fmaf(x.z, y.z, acc[r]);
+            acc[r] = fmaf(x.w, y.w, acc[r]);
+        }
     }
-    return (a0 + a1) + (a2 + a3);
 }
 
 // Cholesky and inverse of one 128 x 128 diagonal block in shared memory,
 // blocked by 32: per 32-column step, the diagonal block is factored and
 // inverted by one warp (diag32), the panel below is L_ik = A_ik L_kk^-T and
 // the trailing lower blocks take the Schur update; then the off-diagonal
-// blocks of V = L^-1 are V_ij = -V_ii sum_{k=j}^{i-1} L_ik V_kj.
+// blocks of V = L^-1 are V_ij = -V_ii sum_{k=j}^{i-1} L_ik V_kj.  Every
+// product is written as rows times rows (V^T and S^T are kept for that), each
+// thread computing four rows of one column.
 // Writes L (lower part of A), V with its split (zeros above the diagonal) and
 // V^T with its split (zeros below), all over the full 128 x 128 block.
 __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __restrict__ A, float* __restrict__ V,
@@ -185,10 +202,11 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
                                                                      float* __restrict__ VT_hi,
                                                                      float* __restrict__ VT_lo, int ld, int off,
                                                                      int* __restrict__ bad) {
-    extern __shared__ float sm[];
-    float* sA = sm;                 // 128 x kLd
-    float* sV = sA + kB * kLd;      // 128 x kLd
-    float* sS = sV + kB * kLd;      // 96 x kSLd scratch
+    extern __shared__ __align__(16) float sm[];
+    float* sA = sm;                 // 128 x kP: A -> L
+    float* sV = sA + kB * kP;       // 128 x kP: V = L^-1
+    float* sVT = sV + kB * kP;      // 128 x kP: V^T
+    float* sST = sVT + kB * kP;     // 3 x 32 x kSP: S^T blocks
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const size_t base = static_cast<size_t>(off) * ld + off;
     pdl_wait();
@@ -196,96 +214,87 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
 #pragma unroll 4
     for (int e = t; e < kB * kB; e += kBaseThreads) {
         const int i = e >> 7, j = e & 127;
-        sA[i * kLd + j] = (j <= i) ? A[base + static_cast<size_t>(i) * ld + j] : 0.0f;
-        sV[i * kLd + j] = 0.0f;
+        sA[i * kP + j] = (j <= i) ? A[base + static_cast<size_t>(i) * ld + j] : 0.0f;
+        sV[i * kP + j] = 0.0f;
+        sVT[i * kP + j] = 0.0f;
     }
     __syncthreads();
 #pragma unroll 1
     for (int kb = 0; kb < 4; ++kb) {
         const int o = 32 * kb;
-        if (warp == 0) diag32(sA + o * kLd + o, sV + o * kLd + o, lane, bad);
+        if (warp == 0) diag32(sA + o * kP + o, sV + o * kP + o, sVT + o * kP + o, lane, bad);
         __syncthreads();
         const int prow = kB - o - 32;
         if (prow == 0) break;
-        // panel: L[o+32+i][o+c] = sum_k A[o+32+i][o+k] V_kk[c][k], via the scratch
+        // panel, in place (a warp owns its four rows): L[i][o+c] = sum_k A[i][o+k] V_kk[c][k]
 #pragma unroll 1
-        for (int i = warp; i < prow; i += 16)
-            sS[i * kSLd + lane] = dot32(sA + (o + 32 + i) * kLd + o, sV + (o + lane) * kLd + o);
-        __syncthreads();
-#pragma unroll 1
-        for (int i = warp; i < prow; i += 16) sA[(o + 32 + i) * kLd + o + lane] = sS[i * kSLd + lane];
+        for (int g = warp; g < prow / 4; g += 16) {
+            const int i = o + 32 + 4 * g;
+            float acc[4];
+            dot4x1(sA + i * kP + o, kP, sV + (o + lane) * kP + o, 32, acc);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) sA[(i + r) * kP + o + lane] = acc[r];
+        }
         __syncthreads();
         // trailing lower blocks: A[i][j] -= sum_k L[i][o+k] L[j][o+k]
         const int nbt = prow / 32;
+        const int ntask = nbt * (nbt + 1) / 2 * 8;  // (block pair, four-row group)
 #pragma unroll 1
-        for (int ib = 0; ib < nbt; ++ib)
-#pragma unroll 1
-            for (int jb = 0; jb <= ib; ++jb)
-#pragma unroll 1
-                for (int q = 0; q < 2; ++q) {
-                    const int i = o + 32 + 32 * ib + warp + 16 * q, j = o + 32 + 32 * jb + lane;
-                    sA[i * kLd + j] -= dot32(sA + i * kLd + o, sA + j * kLd + o);
-                }
+        for (int task = warp; task < ntask; task += 16) {
+            int pair = task >> 3, ib = 0;
+            while (pair > ib) { pair -= ib + 1; ++ib; }
+            const int jb = pair;
+            const int i = o + 32 + 32 * ib + 4 * (task & 7), j = o + 32 + 32 * jb + lane;
+            float acc[4];
+            dot4x1(sA + i * kP + o, kP, sA + j * kP + o, 32, acc);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) sA[(i + r) * kP + j] -= acc[r];
+        }
         __syncthreads();
     }
     // off-diagonal blocks of V, block row by block row
 #pragma unroll 1
     for (int ib = 1; ib < 4; ++ib) {
+        // S_j^T[c][i] = sum_{m=32jb}^{32ib-1} L[32ib+i][m] V^T[32jb+c][m]
 #pragma unroll 1
-        for (int jb = 0; jb < ib; ++jb)
-#pragma unroll 1
-            for (int q = 0; q < 2; ++q) {
-                const int i = warp + 16 * q;
-                const float* xr = sA + (32 * ib + i) * kLd;
-                const float* yc = sV + 32 * jb + lane;
-                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 2
-                for (int m = 32 * jb; m < 32 * ib; m += 4) {
-                    a0 = fmaf(xr[m], yc[m * kLd], a0);
-                    a1 = fmaf(xr[m + 1], yc[(m + 1) * kLd], a1);
-                    a2 = fmaf(xr[m + 2], yc[(m + 2) * kLd], a2);
-                    a3 = fmaf(xr[m + 3], yc[(m + 3) * kLd], a3);
-                }
-                sS[(jb * 32 + i) * kSLd + lane] = (a0 + a1) + (a2 + a3);
-            }
+        for (int task = warp; task < ib * 8; task += 16) {
+            const int jb = task >> 3, i = 4 * (task & 7);
+            float acc[4];
+            dot4x1(sA + (32 * ib + i) * kP + 32 * jb, kP, sVT + (32 * jb + lane) * kP + 32 * jb, 32 * (ib - jb), acc);
+            *reinterpret_cast<float4*>(sST + (jb * 32 + lane) * kSP + i) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        }
         __syncthreads();
+        // V[32ib+i][32jb+c] = -sum_m V[32ib+i][32ib+m] S_j^T[c][m], and its transpose
 #pragma unroll 1
-        for (int jb = 0; jb < ib; ++jb)
-#pragma unroll 1
-            for (int q = 0; q < 2; ++q) {
-                const int i = warp + 16 * q;
-                const float* vr = sV + (32 * ib + i) * kLd + 32 * ib;
-                const float* sc = sS + jb * 32 * kSLd + lane;
-                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 2
-                for (int m = 0; m < 32; m += 4) {
-                    a0 = fmaf(vr[m], sc[m * kSLd], a0);
-                    a1 = fmaf(vr[m + 1], sc[(m + 1) * kSLd], a1);
-                    a2 = fmaf(vr[m + 2], sc[(m + 2) * kSLd], a2);
-                    a3 = fmaf(vr[m + 3], sc[(m + 3) * kSLd], a3);
-                }
-                sV[(32 * ib + i) * kLd + 32 * jb + lane] = -((a0 + a1) + (a2 + a3));
-            }
+        for (int task = warp; task < ib * 8; task += 16) {
+            const int jb = task >> 3, i = 4 * (task & 7);
+            float acc[4];
+            dot4x1(sV + (32 * ib + i) * kP + 32 * ib, kP, sST + (jb * 32 + lane) * kSP, 32, acc);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) sV[(32 * ib + i + r) * kP + 32 * jb + lane] = -acc[r];
+            *reinterpret_cast<float4*>(sVT + (32 * jb + lane) * kP + 32 * ib + i) =
+                make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
+        }
         __syncthreads();
     }
 #pragma unroll 2
     for (int e = t; e < kB * kB; e += kBaseThreads) {
         const int i = e >> 7, j = e & 127;
         const size_t g = base + static_cast<size_t>(i) * ld + j;
-        if (j <= i) A[g] = sA[i * kLd + j];
-        const float v = sV[i * kLd + j];
+        if (j <= i) A[g] = sA[i * kP + j];
+        const float v = sV[i * kP + j];
         const float h = tf32_round(v);
         V[g] = v;
         V_hi[g] = h;
         V_lo[g] = v - h;
-        const float vt = sV[j * kLd + i];
+        const float vt = sVT[i * kP + j];
         const float ht = tf32_round(vt);
         VT[g] = vt;
         VT_hi[g] = ht;
         VT_lo[g] = vt - ht;
     }
 }
-constexpr size_t kBaseSmem = (2 * kB * kLd + 3 * 32 * kSLd) * sizeof(float);
+constexpr size_t kBaseSmem = (3 * kB * kP + 3 * 32 * kSP) * sizeof(float);
 
 // Ut = (P V P)^T on the lower triangle: Ut[i][j] = V[d-1-j][d-1-i], with split.
 __global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, float* __restrict__ Ut,
@@ -315,14 +324,17 @@ __global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, flo
 // rows (two independent dependency chains per warp), lane l holding columns
 // 4l..4l+3 of both rows.  M must be 4 here (the lane's four columns are one
 // group); N:4 with N in {1, 2, 3}.  The block of U sits in shared memory with
-// column j of row q at q*kLd + (j%4)*32 + j/4, so that the four values a lane
+// column j of row q at q*kU1 + (j%4)*32 + j/4, so that the four values a lane
 // needs are bank-conflict free; 1/U_qq follows it.  Only pruned columns carry
-// an error (err = w_q / U_qq; a kept column's error is 0), so the propagation
-// loop runs over the pruned columns of either row.  Errors go to E (row pitch
-// ldE) at the block's own columns, with their tf32 split.
+// an error (err = w_q / U_qq; a kept column's error is 0).  Per group, the
+// group's lane selects the mask and eliminates the group's pruned columns in
+// its own registers, then one broadcast round hands their errors to the lanes
+// of the later groups.  Errors go to E (row pitch ldE) at the block's own
+// columns, with their tf32 split.
+constexpr int kU1 = kB + 1;  // pitch of the in-block copy of U
 constexpr int kIbThreads = 512;
 constexpr int kIbRows = 2 * (kIbThreads / 32);
-constexpr size_t kIbSmem = (kB * kLd + kB) * sizeof(float);
+constexpr size_t kIbSmem = (kB * kU1 + kB) * sizeof(float);
 
 __device__ __forceinline__ uint32_t obs_keep_bits(const float (&w)[4], const float* rv, int n_keep) {
     float s[4];
@@ -342,32 +354,50 @@ __device__ __forceinline__ uint32_t obs_keep_bits(const float (&w)[4], const flo
     return bits;
 }
 
+// Eliminates the pruned columns of one group inside its lane: for k in order,
+// a pruned column's error x = w_k / U_qq updates the group's later columns.
+__device__ __forceinline__ void obs_group_solve(float (&w)[4], float (&e)[4], uint32_t bits, const float* u1,
+                                                const float* rinv, int g) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int q = 4 * g + k;
+        float x = 0.0f;
+        if (!((bits >> k) & 1u)) {
+            x = w[k] * rinv[q];
+#pragma unroll
+            for (int kk = k + 1; kk < 4; ++kk) w[kk] = fmaf(-x, u1[q * kU1 + kk * 32 + g], w[kk]);
+            w[k] = 0.0f;
+        }
+        e[k] = x;
+    }
+}
+
 __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, int d, int i1,
                                                              const float* __restrict__ Ut, int n_keep,
                                                              uint8_t* __restrict__ mask, float* __restrict__ E_hi,
                                                              float* __restrict__ E_lo, long long ldE) {
     extern __shared__ float u1[];
-    float* rinv = u1 + kB * kLd;
+    float* rinv = u1 + kB * kU1;
     pdl_wait();
     pdl_trigger();
-    // U[i1+q][i1+j] = Ut[i1+j][i1+q] (j >= q), eight loads in flight per thread
-    for (int b = threadIdx.x; b < kB * kB; b += kIbThreads * 8) {
-        float v[8];
+    // U[i1+q][i1+j] = Ut[i1+j][i1+q] (j >= q), sixteen loads in flight per thread
+    for (int b = threadIdx.x; b < kB * kB; b += kIbThreads * 16) {
+        float v[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
             const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
             v[u] = (j >= q) ? Ut[static_cast<size_t>(i1 + j) * d + i1 + q] : 0.0f;
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
             const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
-            u1[q * kLd + (j & 3) * 32 + (j >> 2)] = v[u];
+            u1[q * kU1 + (j & 3) * 32 + (j >> 2)] = v[u];
         }
     }
     __syncthreads();
     if (threadIdx.x < kB) {
         const int q = threadIdx.x;
-        rinv[q] = __frcp_rn(u1[q * kLd + (q & 3) * 32 + (q >> 2)]);
+        rinv[q] = __frcp_rn(u1[q * kU1 + (q & 3) * 32 + (q >> 2)]);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -390,39 +420,28 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
             b1 = obs_keep_bits(w1, rinv + 4 * g, n_keep);
             own0 = b0;
             own1 = b1;
+            obs_group_solve(w0, e0, b0, u1, rinv, g);
+            obs_group_solve(w1, e1, b1, u1, rinv, g);
         }
         b0 = __shfl_sync(kFull, b0, g);
         b1 = __shfl_sync(kFull, b1, g);
+        float x0[4], x1[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const bool p0 = !((b0 >> k) & 1u), p1 = !((b1 >> k) & 1u);  // warp-uniform
-            if (!p0 && !p1) continue;
-            const int q = 4 * g + k;
-            float x0 = 0.0f, x1 = 0.0f;
-            if (lane == g) {
-                const float rq = rinv[q];
-                x0 = p0 ? w0[k] * rq : 0.0f;
-                x1 = p1 ? w1[k] * rq : 0.0f;
-                e0[k] = x0;
-                e1[k] = x1;
-            }
-            x0 = __shfl_sync(kFull, x0, g);
-            x1 = __shfl_sync(kFull, x1, g);
-            const float* ur = u1 + q * kLd + lane;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                if (4 * lane + kk > q) {
-                    const float u = ur[kk * 32];
-                    w0[kk] = fmaf(-x0, u, w0[kk]);
-                    w1[kk] = fmaf(-x1, u, w1[kk]);
-                }
-            }
+            x0[k] = __shfl_sync(kFull, e0[k], g);
+            x1[k] = __shfl_sync(kFull, e1[k], g);
         }
-        if (lane == g) {
+        if (lane > g) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                if (!((b0 >> k) & 1u)) w0[k] = 0.0f;
-                if (!((b1 >> k) & 1u)) w1[k] = 0.0f;
+                if (((b0 & b1) >> k) & 1u) continue;  // kept in both rows: no error (warp-uniform)
+                const float* ur = u1 + (4 * g + k) * kU1 + lane;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float u = ur[kk * 32];
+                    w0[kk] = fmaf(-x0[k], u, w0[kk]);
+                    w1[kk] = fmaf(-x1[k], u, w1[kk]);
+                }
             }
         }
     }
@@ -449,6 +468,8 @@ struct Work {
     float *A, *A_hi, *A_lo, *V, *V_hi, *V_lo, *VT, *VT_hi, *VT_lo, *T_hi, *T_lo;
     int d;
     int* bad;
+    cudaStream_t side;  // stream of the triangular-inverse steps
+    cudaEvent_t ev;     // "this node's factor is complete", re-recorded per node
 };
 
 int gemm(const float* ah, const float* al, long long lda, const float* bh, const float* bl, long long ldb, int M, int N,
@@ -489,8 +510,16 @@ int trsm(Work& w, long long r0, int m, long long c0, int n, cudaStream_t st) {
     return trsm(w, r0, m, c0 + n1, n2, st);
 }
 
+int trtri_node(Work& w, int off, int n, cudaStream_t st);
+
 // Recursive Cholesky of A[off : off+n] (lower, in place, with split); the
-// 128 x 128 diagonal blocks also get their inverses in V / VT.
+// 128 x 128 diagonal blocks also get their inverses in V / VT.  Once a node's
+// factor is enqueued on st, its inverse step goes to w.side behind an event:
+// the inverse of finished sub-blocks then runs beside the rest of the
+// factorisation, whose chain of small dependent launches leaves most SMs idle.
+// Inverse steps only touch V's off-diagonal blocks and T, which the factor
+// side never reads, and on w.side they keep the recursion's order (both
+// halves of a node before the node).
 int chol(Work& w, int off, int n, cudaStream_t st) {
     const long long d = w.d;
     if (n == kB) {
@@ -514,23 +543,25 @@ int chol(Work& w, int off, int n, cudaStream_t st) {
                        n2, n1, o, st)))
             return rc;
     }
-    return chol(w, off + n1, n2, st);
+    if ((rc = chol(w, off + n1, n2, st))) return rc;
+    cudaError_t e = cudaEventRecord(w.ev, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(w.side, w.ev, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt stream fork");
+    return trtri_node(w, off, n, w.side);
 }
 
-// Recursive inverse V = L^-1 of the factor in A (diagonal 128-blocks already
-// inverted by the base kernel): V21 = -V22 (L21 V11), with V^T kept alongside.
-// Both products take a triangular left operand, so each output tile row runs
-// only over the K tiles inside the triangle (half the dense work); tiles
-// outside it are never read and need not be zero.
-int trtri(Work& w, int off, int n, cudaStream_t st) {
-    if (n == kB) return TB_OK;
+// Node step of the triangular inverse V = L^-1 for the node [off, off+n) once
+// V11 and V22 are complete (the diagonal 128-blocks come from the base kernel):
+// V21 = -V22 (L21 V11), with V^T kept alongside.  Both products take a
+// triangular left operand, so each output tile row runs only over the K tiles
+// inside the triangle (half the dense work); tiles outside it are never read
+// and need not be zero.
+int trtri_node(Work& w, int off, int n, cudaStream_t st) {
     const long long d = w.d;
     auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
     const long long o1 = off + n1;
-    int rc = trtri(w, off, n1, st);
-    if (!rc) rc = trtri(w, off + n1, n2, st);
-    if (rc) return rc;
+    int rc;
     {  // T^T = V11^T L21^T  (n1 x n2), split only
         umma::GemmOut o{};
         o.C_hi = w.T_hi; o.C_lo = w.T_lo; o.ld_split = n2;
@@ -620,36 +651,44 @@ struct Workspace {
     int dev = -1;
     float* ptr = nullptr;
     size_t floats = 0;
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev = nullptr, join = nullptr;
 };
 std::mutex g_ws_mu;
 std::vector<Workspace> g_ws;
 
-int workspace(size_t floats, float** out) {
+// Per-device workspace of at least `floats` floats, with the side stream and
+// events of the inverse steps (created once per device).
+int workspace(size_t floats, Workspace* out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     std::lock_guard<std::mutex> lk(g_ws_mu);
-    for (auto& w : g_ws)
-        if (w.dev == dev) {
-            if (w.floats < floats) {
-                cudaDeviceSynchronize();
-                cudaFree(w.ptr);
-                w.ptr = nullptr;
-                w.floats = 0;
-                e = cudaMalloc(reinterpret_cast<void**>(&w.ptr), floats * sizeof(float));
-                if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt workspace");
-                w.floats = floats;
-            }
-            *out = w.ptr;
-            return TB_OK;
+    Workspace* w = nullptr;
+    for (auto& x : g_ws)
+        if (x.dev == dev) w = &x;
+    if (!w) {
+        Workspace x;
+        x.dev = dev;
+        e = cudaStreamCreateWithFlags(&x.side, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.ev, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt stream/event setup");
+        g_ws.push_back(x);
+        w = &g_ws.back();
+    }
+    if (w->floats < floats) {
+        if (w->ptr) {
+            cudaDeviceSynchronize();
+            cudaFree(w->ptr);
         }
-    Workspace w;
-    w.dev = dev;
-    e = cudaMalloc(reinterpret_cast<void**>(&w.ptr), floats * sizeof(float));
-    if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt workspace");
-    w.floats = floats;
-    g_ws.push_back(w);
-    *out = w.ptr;
+        w->ptr = nullptr;
+        w->floats = 0;
+        e = cudaMalloc(reinterpret_cast<void**>(&w->ptr), floats * sizeof(float));
+        if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt workspace");
+        w->floats = floats;
+    }
+    *out = *w;
     return TB_OK;
 }
 
@@ -684,12 +723,15 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     // Workspace: 9 d x d FP32 matrices (A, V, V^T with their splits), the
     // trtri temporary T (at most d^2 / 4, with split), the error matrix E
     // (r x d, with split) and two scalars.
-    float* ws = nullptr;
+    Workspace wsp;
     const size_t ws_floats = 9 * dd + 2 * (dd / 4) + 2 * rd + 64;
-    if ((rc = workspace(ws_floats, &ws))) return rc;
+    if ((rc = workspace(ws_floats, &wsp))) return rc;
+    float* ws = wsp.ptr;
     cudaError_t e = cudaSuccess;
     Work w{};
     w.d = d;
+    w.side = wsp.side;
+    w.ev = wsp.ev;
     w.A = ws; w.A_hi = ws + dd; w.A_lo = ws + 2 * dd;
     w.V = ws + 3 * dd; w.V_hi = ws + 4 * dd; w.V_lo = ws + 5 * dd;
     w.VT = ws + 6 * dd; w.VT_hi = ws + 7 * dd; w.VT_lo = ws + 8 * dd;
@@ -710,7 +752,10 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
                        static_cast<const double*>(dsum), damp_frac, w.A, w.A_hi, w.A_lo);
     rc = e == cudaSuccess ? check_launch("hessian prep") : cuda_fail(e, "hessian prep launch");
     if (!rc) rc = chol(w, 0, d, st);
-    if (!rc) rc = trtri(w, 0, d, st);
+    // join: the inverse steps on the side stream finish before anything reads V
+    e = cudaEventRecord(wsp.join, w.side);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.join, 0);
+    if (e != cudaSuccess && !rc) rc = cuda_fail(e, "tb_obs_sparsegpt stream join");
     // Ut (lower) = (P V P)^T into A's buffers (A is no longer needed).
     float *Ut = w.A, *Ut_hi = w.A_hi, *Ut_lo = w.A_lo;
     if (!rc) {
