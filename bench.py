@@ -191,7 +191,7 @@ def run_ours(args):
             print(json.dumps({"gemm_probe": gemm_probe(torch, tb, dev, *args.gemm_probe)}), flush=True)
         return
     if args.obs_only:
-        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape)
+        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape, dist if world > 1 else None)
         if rank == 0:
             print(json.dumps({"metric": METRIC, "obs": obs, "n_gpus": world}), flush=True)
         if world > 1:
@@ -263,10 +263,10 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = run_e2e(torch, tb, dev, gen, args, world, rank, local)
 
-    # ---- configuration 4 (OBS on tensor cores), per rank -------------------
+    # ---- configuration 4 (OBS on tensor cores) -----------------------------
     obs = None
     if not args.no_obs:
-        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape)
+        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape, dist if world > 1 else None)
 
     # ---- CPU baseline (rank 0, single GPU only) ----------------------------
     cpu = None
@@ -404,42 +404,74 @@ def gemm_probe(torch, tb, dev, M, N, K, reps=5):
     return out
 
 
-def run_obs(torch, tb, dev, steps, shape=None):
+def sparsegpt_flops(d, r, n):
+    """FLOPs of the standard column-block OBS formulation (full X^T X, Cholesky
+    of H, explicit inverse, Cholesky of H^-1, lazy updates, in-block), the
+    count a route that forms H^-1 explicitly performs."""
+    return 2 * n * d * d + d ** 3 // 3 + 2 * d ** 3 // 3 + d ** 3 // 3 + r * d * d + r * d * 128
+
+
+def run_obs(torch, tb, dev, steps, shape=None, dist=None):
+    """Configuration 4 on tensor cores.  With several ranks the tokens are
+    split for X^T X (one NCCL all-reduce of H) and the rows of W for the sweep;
+    the factorisation of H is replicated on every rank.  Time per pass is the
+    maximum over ranks."""
+    import tbdist as td
     OBS_R, OBS_D, OBS_N = shape or (globals()["OBS_R"], globals()["OBS_D"], globals()["OBS_N"])
+    world = dist.get_world_size() if dist is not None else 1
+    rank = dist.get_rank() if dist is not None else 0
     gen = torch.Generator(device=dev).manual_seed(4)
     X = torch.randn(OBS_N, OBS_D, device=dev, generator=gen)
     hot = torch.randperm(OBS_D, device=dev, generator=gen)[: OBS_D // 100]
     X[:, hot] *= 20
-    xt = X.t().contiguous().to(torch.bfloat16)
+    t0, t1 = td.token_shard(OBS_N, world, rank)
+    xt = X[t0:t1].t().contiguous().to(torch.bfloat16)
     del X
-    W0 = (torch.randn(OBS_R, OBS_D, device=dev, generator=gen) * 0.02).to(torch.bfloat16).float()
+    r0, r1 = td.obs_row_shard(OBS_R, world, rank)
+    W0 = (torch.randn(OBS_R, OBS_D, device=dev, generator=gen) * 0.02).to(torch.bfloat16).float()[r0:r1].contiguous()
     W = torch.empty_like(W0)
     H = torch.zeros(OBS_D, OBS_D, device=dev)
-    mask = torch.empty(OBS_R * OBS_D // 4, dtype=torch.uint8, device=dev)
+    mask = torch.empty(max(1, (r1 - r0) * OBS_D // 4), dtype=torch.uint8, device=dev)
     L = tb.lib()
     sptr = torch.cuda.current_stream().cuda_stream
     ms = []
     for k in range(steps + 1):  # the first pass warms up (workspace, module load)
         W.copy_(W0)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        tb.check(L.tb_obs_hessian(xt.data_ptr(), OBS_D, OBS_N, H.data_ptr(), sptr))
-        tb.check(L.tb_obs_sparsegpt(W.data_ptr(), OBS_R, OBS_D, H.data_ptr(), 0.01, 2, 4, mask.data_ptr(), None, sptr))
+        if world > 1:
+            td.obs_hessian_token_split(dist, torch, xt, OBS_D, OBS_N, H)
+            td.prune_obs_row_split(dist, torch, W, H, mask)
+        else:
+            tb.check(L.tb_obs_hessian(xt.data_ptr(), OBS_D, OBS_N, H.data_ptr(), sptr))
+            tb.check(L.tb_obs_sparsegpt(W.data_ptr(), OBS_R, OBS_D, H.data_ptr(), 0.01, 2, 4, mask.data_ptr(),
+                                        None, sptr))
         e1.record()
         torch.cuda.synchronize()
         if k:
             ms.append(e0.elapsed_time(e1))
     pop = sum(((mask >> b) & 1).int() for b in range(4))
-    assert bool((pop == 2).all()), "OBS mask is not 2:4"
+    assert r1 == r0 or bool((pop == 2).all()), "OBS mask is not 2:4"
+    t = torch.tensor([sum(ms) / len(ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t = float(t.item())
     f = obs_flops(OBS_D, OBS_R, OBS_N)
-    t = sum(ms) / len(ms)
+    fs = sparsegpt_flops(OBS_D, OBS_R, OBS_N)
     bf16_peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
     tflops = f / (t / 1e3) / 1e12
     return {"workload": f"cfg4: {OBS_R}x{OBS_D} down_proj (BF16 -> FP32), X {OBS_N}x{OBS_D} BF16 N(0,1) with 1% columns x20, "
                         "damp 0.01 mean(diag), 128-column blocks, 2:4",
             "ms_per_pass": round(t, 2), "passes": steps, "flops_per_pass": f, "tflops": round(tflops, 1),
-            "unit": "TFLOP/s", "flop_count": "algorithmic: d(d+1)n + 2d^3/3 + r d^2 (bench.obs_flops)",
+            "unit": "TFLOP/s", "flop_count": "algorithmic for this route: d(d+1)n + 2d^3/3 + r d^2 (bench.obs_flops)",
+            "sparsegpt_flops_per_pass": fs,
+            "tflops_sparsegpt_equivalent": round(fs / (t / 1e3) / 1e12, 1),
+            "parallelism": (f"{world} ranks: tokens split for X^T X + NCCL all-reduce of H, factorisation replicated, "
+                            f"rows split for the sweep" if world > 1 else "1 GPU"),
             "tensor_peak_bf16_tflops": bf16_peak,
             "frac_of_bf16_peak": round(tflops / bf16_peak, 4),
             "frac_of_3xtf32_ceiling": round(tflops / (bf16_peak / 2 / 3), 4)}

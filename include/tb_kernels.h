@@ -186,18 +186,26 @@ int tb_gemm_status(void* stream);
  * H = X^T X / n from X^T given as BF16 [d][n] (row-major, d % 128 == 0,
  * n % 64 == 0); only the 128x128 tiles on or below the diagonal are written. */
 int tb_obs_hessian(const void* xt_bf16, int d, int n, float* H, void* stream);
+/* H = scale * X^T X over the n tokens given (same layout and tiles as
+ * tb_obs_hessian).  With calibration tokens split across ranks, each rank
+ * passes its own tokens and scale = 1 / (total tokens); the ranks' results
+ * summed (one all-reduce) give the Hessian of all tokens.  No reference
+ * counterpart: the reference has no activation Hessian. */
+int tb_obs_hessian_scaled(const void* xt_bf16, int d, int n, float scale, float* H, void* stream);
 /* Prunes W [r][d] (FP32, in place; r, d multiples of 128) to N:4 against H
  * (lower tiles valid, e.g. from tb_obs_hessian): lambda = damp_frac *
  * mean(diag H) is added to the diagonal, U = chol_upper((H + lambda I)^-1) is
- * formed on tensor cores (3xTF32 tcgen05 GEMMs), and columns are processed in
+ * formed on tensor cores (3xTF32 tcgen05 GEMMs), and columns are swept in
  * blocks of 128: per group of 4 the 4 - n_keep smallest w^2 / U_qq^2 are
- * pruned, each column's error updates the rest of its block, and the block's
- * errors update the remaining columns through one tcgen05 GEMM.  mask gets
+ * pruned and each pruned column's error updates the later columns of its row
+ * (inside the block directly, beyond it through tcgen05 GEMMs over the errors
+ * of whole column ranges).  Rows are independent, so a row range of W may be
+ * pruned on its own (each rank of a row split passes its rows).  mask gets
  * r*d/4 bytes (bit k = keep column 4g+k, the .tb convention).  ut_out (d x d,
- * may be NULL) receives U^T.  A workspace of ~11 d^2 floats is allocated on
- * first use and kept per device for later calls (grow-only; ~9 GB at d = 14336).
- * Synchronises the stream.  TB_ERR_CONFIG if H + lambda I is
- * not positive definite in FP32. */
+ * may be NULL) receives U^T.  A workspace of 9.5 d^2 + 2 r d floats is
+ * allocated on first use and kept per device for later calls (grow-only;
+ * ~8.3 GB at d = 14336, r = 4096).  Synchronises the stream.  TB_ERR_CONFIG
+ * if H + lambda I is not positive definite in FP32. */
 int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float damp_frac, int n_keep, int m,
                      uint8_t* mask, float* ut_out, void* stream);
 

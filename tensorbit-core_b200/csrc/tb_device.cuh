@@ -81,25 +81,6 @@ __device__ __forceinline__ float ema_next(float F, float beta, float contrib, fl
     return __fadd_rn(__fmul_rn(beta, F), __fmul_rn(__fmul_rn(contrib, g), g));
 }
 
-// Two lanes of ema_next in packed FP32 (sm_100 mul/add.rn.f32x2): each lane
-// is rounded to nearest separately and nothing is fused, so the bits equal two
-// ema_next calls while the instruction count halves.  beta2 / c2 hold the
-// scalar in both halves (pack2).
-__device__ __forceinline__ uint64_t pack2(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void ema_next2(float& f0, float& f1, uint64_t beta2, uint64_t c2, float g0, float g1) {
-    asm("{\n\t.reg .b64 F, G, T, U;\n\t"
-        "mov.b64 F, {%0, %1};\n\tmov.b64 G, {%2, %3};\n\t"
-        "mul.rn.f32x2 T, %5, G;\n\tmul.rn.f32x2 T, T, G;\n\t"
-        "mul.rn.f32x2 U, %4, F;\n\tadd.rn.f32x2 F, U, T;\n\t"
-        "mov.b64 {%0, %1}, F;\n\t}"
-        : "+f"(f0), "+f"(f1)
-        : "f"(g0), "f"(g1), "l"(beta2), "l"(c2));
-}
-
 // compute_importance (ehap.hpp:260-282).  have_f == false is the "no Fisher
 // state" branch (s = w * w).
 __device__ __forceinline__ float importance(float w, float F, float damp, int mode, bool have_f) {

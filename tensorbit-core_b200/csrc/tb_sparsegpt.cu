@@ -698,13 +698,18 @@ int workspace(size_t floats, Workspace* out) {
 using namespace tb;
 
 extern "C" int tb_obs_hessian(const void* xt, int d, int n, float* H, void* stream) {
+    if (n <= 0) return fail(TB_ERR_SHAPE, "tb_obs_hessian: n must be positive");
+    return tb_obs_hessian_scaled(xt, d, n, 1.0f / static_cast<float>(n), H, stream);
+}
+
+extern "C" int tb_obs_hessian_scaled(const void* xt, int d, int n, float scale, float* H, void* stream) {
     if (d <= 0 || n <= 0 || d % kB || n % 64) return fail(TB_ERR_SHAPE, "tb_obs_hessian: d %% 128 and n %% 64 must be 0");
     if (!xt || !H) return fail(TB_ERR_ARG, "tb_obs_hessian: null pointer");
     int rc = require_device(nullptr);
     if (rc) return rc;
     umma::GemmOut o{};
     o.C = H; o.ldc = d;
-    o.alpha = 1.0f / static_cast<float>(n);
+    o.alpha = scale;
     o.beta = 0.0f;
     o.lower_only = 1;
     return umma::gemm_nt(umma::kBF16, {xt, nullptr, n}, {xt, nullptr, n}, d, d, n, o, static_cast<cudaStream_t>(stream));

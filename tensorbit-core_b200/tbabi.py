@@ -120,6 +120,7 @@ def lib() -> C.CDLL:
                                  vp, C.c_longlong, i32, vp], i32),
             "tb_gemm_status": ([vp], i32),
             "tb_obs_hessian": ([vp, i32, i32, vp, vp], i32),
+            "tb_obs_hessian_scaled": ([vp, i32, i32, f32, vp, vp], i32),
             "tb_obs_sparsegpt": ([vp, i32, i32, vp, f32, i32, i32, vp, vp, vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),

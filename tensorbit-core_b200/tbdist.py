@@ -17,6 +17,12 @@ docs prune shards in separate processes, docs/CLOUD.md:155-170):
   recurrence to FP32 rounding (the association differs), so masks can differ
   only in near-tie groups, which the pass counts.
 
+Column-block exact OBS of one layer (`obs_hessian_token_split`,
+`prune_obs_row_split`): the calibration tokens are split across ranks, each
+rank forms X_r^T X_r / n on tensor cores and one NCCL all-reduce of the d x d
+FP32 Hessian sums them; every rank then factors the same H (replicated, not
+scaled) and sweeps only its own rows of W, which are independent.
+
 Ranks read RANK / WORLD_SIZE / LOCAL_RANK from the environment like torchrun.
 """
 from __future__ import annotations
@@ -153,3 +159,51 @@ def prune_sample_split(dist, torch, w_dev, w_dtype: int, g_local_dev, g_dtype: i
                           near_ties=ties.data_ptr(), **cfg)
         _check(tb.score_mask_pack(a, stream))
     return {"e0": e0, "e1": e1, "near_ties": ties, "fisher": F}
+
+
+# ---- column-block exact OBS --------------------------------------------------
+OBS_ROW_UNIT = 128   # rows of W per unit (tb_obs_sparsegpt takes multiples of 128)
+OBS_TOKEN_UNIT = 64  # tokens per unit (tb_obs_hessian_scaled takes multiples of 64)
+
+
+def obs_row_shard(r: int, world: int, rank: int) -> tuple[int, int]:
+    """Row range [r0, r1) of W for `rank`: whole 128-row units, balanced."""
+    if r % OBS_ROW_UNIT:
+        raise ValueError(f"rows {r} not a multiple of {OBS_ROW_UNIT}")
+    units = r // OBS_ROW_UNIT
+    return units * rank // world * OBS_ROW_UNIT, units * (rank + 1) // world * OBS_ROW_UNIT
+
+
+def token_shard(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Token range [t0, t1) of `rank`: whole 64-token units, balanced."""
+    if n % OBS_TOKEN_UNIT:
+        raise ValueError(f"tokens {n} not a multiple of {OBS_TOKEN_UNIT}")
+    units = n // OBS_TOKEN_UNIT
+    return units * rank // world * OBS_TOKEN_UNIT, units * (rank + 1) // world * OBS_TOKEN_UNIT
+
+
+def obs_hessian_token_split(dist, torch, xt_local_dev, d: int, n_total: int, H) -> None:
+    """H = X^T X / n_total over all ranks' tokens.  xt_local_dev is this rank's
+    tokens as X^T (BF16 [d][n_local], n_local a multiple of 64, may be None
+    for no tokens); H is a d x d FP32 device tensor, overwritten.  The partial
+    is formed with scale 1/n_total, so the all-reduced sum needs no rescaling;
+    tiles above the diagonal stay zero on every rank and sum to zero."""
+    stream = torch.cuda.current_stream().cuda_stream
+    H.zero_()
+    n_local = xt_local_dev.shape[1] if xt_local_dev is not None else 0
+    if n_local:
+        _check(tb.lib().tb_obs_hessian_scaled(xt_local_dev.data_ptr(), d, n_local, 1.0 / n_total, H.data_ptr(),
+                                              stream))
+    dist.all_reduce(H)
+
+
+def prune_obs_row_split(dist, torch, W_local, H, mask_local, *, damp_frac=0.01, n_keep=2, m=4) -> None:
+    """Prunes this rank's rows of W (FP32 device [rows][d], in place) against
+    the all-reduced H; mask_local gets rows * d / 4 bytes.  The Cholesky factor
+    of H^-1 is computed on every rank (it is the same on all of them)."""
+    rows, d = W_local.shape
+    if rows == 0:
+        return
+    stream = torch.cuda.current_stream().cuda_stream
+    _check(tb.lib().tb_obs_sparsegpt(W_local.data_ptr(), rows, d, H.data_ptr(), damp_frac, n_keep, m,
+                                     mask_local.data_ptr(), None, stream))

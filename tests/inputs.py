@@ -93,3 +93,13 @@ MOCK_RUNS = {
     "oneshot_4of8": ["--mock-size", "8192", "--sparsity", "4:8"],
     "damping_10000": ["--mock-size", "10000", "--sparsity", "2:4", "--damping", "0.05"],
 }
+
+
+def activations(n, d, seed, frac=0.01, scale=20.0):
+    """Calibration activations X [n][d] ~ N(0, 1) with a fraction of columns
+    scaled (heavy-tail channels), rounded to BF16 and returned as FP32."""
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((n, d), dtype=np.float32)
+    hot = rng.choice(d, max(1, int(d * frac)), replace=False)
+    X[:, hot] *= np.float32(scale)
+    return bf16_bits_to_f32(to_bf16_bits(X)).reshape(n, d)

@@ -101,3 +101,44 @@ def test_two_gloo_ranks(port, tmp_path):
     w, gg = inputs.cfg1()
     rc, wp, mk, *_ = port.pipeline(w, gg, strategy="optimal", redist="proportional")
     assert open(tmp_path / "sharded.tb", "rb").read() == port.tb_bytes(wp, mk, 2, 4)
+
+
+@pytest.mark.parametrize("r,n", [(4096, 2048), (256, 64), (640, 1344)])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_obs_row_and_token_shards(r, n, world):
+    rows = [tbdist.obs_row_shard(r, world, k) for k in range(world)]
+    toks = [tbdist.token_shard(n, world, k) for k in range(world)]
+    for ranges, unit, total in ((rows, 128, r), (toks, 64, n)):
+        assert ranges[0][0] == 0 and ranges[-1][1] == total
+        for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+            assert a1 == b0
+        assert all(a % unit == 0 and b % unit == 0 and a <= b for a, b in ranges)
+
+
+def _obs_worker(rank, world, port_no, tmpdir):
+    sys.path[:0] = [os.path.join(ROOT, "tensorbit-core_b200"), HERE]
+    import torch
+    import torch.distributed as dist
+    import tbdist as td
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    n, d = 320, 96
+    X = np.random.default_rng(11).standard_normal((n, d))
+    t0, t1 = td.token_shard(n, world, rank)
+    # the partial each rank forms (scale 1/n_total), summed by the all-reduce
+    H = torch.from_numpy(X[t0:t1].T @ X[t0:t1] / n)
+    dist.all_reduce(H)
+    np.save(os.path.join(tmpdir, f"H{rank}.npy"), H.numpy())
+    dist.destroy_process_group()
+
+
+def test_obs_token_split_sum_is_the_full_hessian(tmp_path):
+    """Two gloo ranks: partials over the token shards with the global 1/n scale
+    all-reduce to X^T X / n of all tokens, identically on both ranks."""
+    mp.start_processes(_obs_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    X = np.random.default_rng(11).standard_normal((320, 96))
+    H0, H1 = np.load(tmp_path / "H0.npy"), np.load(tmp_path / "H1.npy")
+    assert np.array_equal(H0, H1)
+    np.testing.assert_allclose(H0, X.T @ X / 320, rtol=1e-12, atol=1e-12)

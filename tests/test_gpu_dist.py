@@ -93,3 +93,66 @@ def test_two_rank_group_shard_and_sample_split(cuda, tblib, port, tmp_path):
     assert not (differ & ~near).any(), "a mask differs outside the near-tie groups"
     same = np.repeat(~differ, 4)
     assert np.array_equal(wgot[same], wo[same])
+
+
+def _obs_worker(rank, world, port_no, tmpdir):
+    sys.path[:0] = [os.path.join(ROOT, "tensorbit-core_b200"), HERE]
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    import inputs as inp
+    import tbdist as td
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    r, d, n = OBS_SHAPE
+    X = inp.activations(n, d, 17)
+    W = inp.normal(r * d, 0.02, 18).reshape(r, d)
+    t0, t1 = td.token_shard(n, world, rank)
+    xt = torch.from_numpy(np.ascontiguousarray(X[t0:t1].T)).cuda().to(torch.bfloat16).contiguous()
+    H = torch.empty(d, d, device="cuda")
+    td.obs_hessian_token_split(dist, torch, xt, d, n, H)
+    r0, r1 = td.obs_row_shard(r, world, rank)
+    Wl = torch.from_numpy(np.ascontiguousarray(W[r0:r1])).cuda()
+    ml = torch.zeros((r1 - r0) * d // 4, dtype=torch.uint8, device="cuda")
+    td.prune_obs_row_split(dist, torch, Wl, H, ml)
+    torch.cuda.synchronize()
+    np.save(os.path.join(tmpdir, f"obs_H{rank}.npy"), H.cpu().numpy())
+    np.save(os.path.join(tmpdir, f"obs_W{rank}.npy"), Wl.cpu().numpy())
+    np.save(os.path.join(tmpdir, f"obs_m{rank}.npy"), ml.cpu().numpy().reshape(r1 - r0, d // 4))
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+
+
+OBS_SHAPE = (256, 512, 1024)
+
+
+def test_two_rank_obs_token_and_row_split(cuda, tblib, tmp_path):
+    import sparsegpt_ref as ref
+    import torch.multiprocessing as mp
+    world = 2
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_obs_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    r, d, n = OBS_SHAPE
+    X = inputs.activations(n, d, 17)
+    W = inputs.normal(r * d, 0.02, 18).reshape(r, d)
+    H0 = np.load(tmp_path / "obs_H0.npy")
+    assert np.array_equal(H0, np.load(tmp_path / "obs_H1.npy"))
+    Hd = X.astype(np.float64).T @ X.astype(np.float64) / n
+    low = np.tril(np.ones((d // 128, d // 128), bool)).repeat(128, 0).repeat(128, 1)
+    assert np.abs(H0 - Hd)[low].max() <= 1e-5 * np.abs(Hd).max()
+    Wg = np.concatenate([np.load(tmp_path / f"obs_W{k}.npy") for k in range(world)])
+    mg = np.concatenate([np.load(tmp_path / f"obs_m{k}.npy") for k in range(world)])
+    Wr, mr, U, gap = ref.sparsegpt(W, X, 0.01, 2, 4, 128)
+    differ = mg != mr
+    assert differ.mean() <= 1e-3
+    first = np.argmax(differ, axis=1)
+    rows = np.nonzero(differ.any(1))[0]
+    assert (gap[rows, first[rows]] < 1e-2).all()
+    lg, lr = ref.layer_loss(W, Wg, X), ref.layer_loss(W, Wr, X)
+    assert abs(lg - lr) <= 0.01 * lr, (lg, lr)

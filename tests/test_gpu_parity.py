@@ -160,6 +160,18 @@ def test_nm_patterns(cuda, tblib, port, n, m, strategy):
 
 
 @pytest.mark.parametrize("n,m", [(2, 4), (1, 4), (2, 8), (4, 8)])
+def test_70b_sweep_settings(cuda, tblib, port, n, m):
+    """The 70B sweep's settings on a 256 x 8192 slice of a hidden-8192
+    projection: BF16 weights, 32 BF16 gradient samples, OBS scores, iterative
+    swap-refine with 4 passes, each of the sweep's patterns; bit-exact."""
+    N = 256 * 8192
+    w = inputs.normal(N, 0.02, 90 + m)
+    g = inputs.normal((32, N), 1e-3, 91 + n)
+    r = run_fused(cuda, tblib, w, g, wdt="bf16", gdt="bf16", n=n, m=m, strategy="iterative", mode="obs", rounds=4)
+    check_against_oracle(port, r, n=n, m=m, strategy="iterative", mode="obs", rounds=4)
+
+
+@pytest.mark.parametrize("n,m", [(2, 4), (1, 4), (2, 8), (4, 8)])
 @pytest.mark.parametrize("strategy", ["topn", "iterative", "optimal"])
 @pytest.mark.parametrize("permute", [False, True])
 def test_tie_heavy_inputs(cuda, tblib, port, n, m, strategy, permute):

@@ -13,14 +13,6 @@ import sparsegpt_ref as ref
 pytestmark = pytest.mark.gpu
 
 
-def activations(n, d, seed, frac=0.01, scale=20.0):
-    rng = np.random.default_rng(seed)
-    X = rng.standard_normal((n, d), dtype=np.float32)
-    hot = rng.choice(d, max(1, int(d * frac)), replace=False)
-    X[:, hot] *= np.float32(scale)
-    return inputs.bf16_bits_to_f32(inputs.to_bf16_bits(X)).reshape(n, d)
-
-
 def run(torch, tb, W, X, n_keep=2, damp=0.01):
     r, d = W.shape
     n = X.shape[0]
@@ -41,7 +33,7 @@ def run(torch, tb, W, X, n_keep=2, damp=0.01):
 def test_sparsegpt_against_float64(cuda, tblib, r, d, n, n_keep):
     """Includes fewer tokens than features (n < d): H is rank-deficient plus
     lambda I, the ill-conditioned regime of the 4096 x 14336 layer."""
-    X = activations(n, d, d + n)
+    X = inputs.activations(n, d, d + n)
     W = inputs.normal(r * d, 0.02, r + d).reshape(r, d)
     Wg, mg, ut = run(cuda, tblib, W, X, n_keep)
     Wr, mr, U, gap = ref.sparsegpt(W, X, 0.01, n_keep, 4, 128)
