@@ -140,13 +140,14 @@ __device__ __forceinline__ uint64_t groups16(const FusedParams& p, const float (
 // Vector kernel: 16 elements per thread, all pointers 16-byte aligned and
 // g_stride * sizeof(G) a multiple of 16 (checked on the host).  Three 256-thread
 // CTAs per SM (<= 85 registers) keep more loads in flight than two.  The
-// sample recurrence stays in scalar round-to-nearest FP32 operations: the
-// packed f32x2 forms were measured to differ from the reference's results by
-// up to 6 ulp after 8 samples, so they are not used here.
+// sample recurrence issues its products as packed f32x2 (ema_next2, exact);
+// at the power-capped clock the pass is partly issue-bound, so fewer FP32
+// instructions per element show up as bandwidth.
 template <int WDT, int GDT, int M>
 __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParams p) {
     constexpr int GW = Vec16<GDT>::kWords;
     constexpr int U = (GW == 2) ? 4 : 2;  // samples in flight per thread
+    const uint64_t beta2 = pack2(p.beta, p.beta), c2 = pack2(p.contrib, p.contrib);
     const size_t nchunks = p.N / kEpt;
     const size_t gstride_b = p.gstride * Dtype<GDT>::kBytes;
     int ties = 0;
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
                 float x[kEpt];
                 Vec16<GDT>::decode(b[u], x);
 #pragma unroll
-                for (int i = 0; i < kEpt; ++i) F[i] = ema_next(F[i], p.beta, p.contrib, x[i]);
+                for (int i = 0; i < kEpt; i += 2) ema_next2(F[i], F[i + 1], beta2, c2, x[i], x[i + 1]);
             }
         }
         for (; s < p.S; ++s) {
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
             float x[kEpt];
             Vec16<GDT>::decode(b, x);
 #pragma unroll
-            for (int i = 0; i < kEpt; ++i) F[i] = ema_next(F[i], p.beta, p.contrib, x[i]);
+            for (int i = 0; i < kEpt; i += 2) ema_next2(F[i], F[i + 1], beta2, c2, x[i], x[i + 1]);
         }
         // ---- importance ----
         float w[kEpt], sc[kEpt];
