@@ -105,16 +105,48 @@ constexpr int kP = kB + 4;           // shared-memory pitch of the 128 x 128 blo
 constexpr int kBaseThreads = 512;
 constexpr int kSP = 36;              // pitch of the 32 x 32 scratch blocks
 
-// Cholesky factor and inverse of one 32 x 32 diagonal block by one warp.
-// Lane i keeps row i in registers relative to the current column j
-// (a[k] = D[i][j+k]) and shifts the row by one after each column, so the
-// column loop stays rolled with constant register indices: the kernel runs
-// once per launch, and compact code matters more than unrolling here.
-// D (pitch kP) holds the Schur-updated block on and below the diagonal; on
-// return it holds L_kk with zeros above; Q gets L_kk^-1 (zeros above) and QT
-// its transpose (zeros below), both pitch kP.  Pivots <= 0 set *bad (and
-// continue with 1).
-__device__ __noinline__ void diag32(float* D, float* Q, float* QT, int lane, int* bad) {
+// ---- 32 x 32 diagonal step of the base kernel, three roles in parallel ----
+// Warp 0 factors the diagonal block column by column, lane i holding row i in
+// registers relative to a base column (a[k] = D[i][jb+k], shifted by four every
+// four columns, so the loop stays rolled with constant register indices).
+// After column j it publishes the column (Lc[j][k] = L[j+k][j]) and 1/L_jj in
+// shared memory and bumps a counter.  Warp 1 builds L_kk^-1 and warps 2.. solve
+// the panel rows below (x L_kk^T = a) by forward substitution, each consuming
+// the published columns one step behind, so neither sits on the critical path.
+// Columns are read back as eight 128-bit broadcast loads instead of 31 shuffles.
+// Waits are bounded: on expiry *bad gets 2 and the warp carries on (the host
+// reports a timeout).
+constexpr int kSpinLimit = 1 << 22;
+
+__device__ __forceinline__ void wait_columns(const volatile int* ready, int target, int* bad) {
+    int spins = 0;
+    while (*ready < target) {
+        if (++spins > kSpinLimit) {
+            atomicExch(bad, 2);
+            break;
+        }
+    }
+    __threadfence_block();
+}
+
+__device__ __forceinline__ void load_column(const float* Lc, int j, float (&lc)[32]) {
+    const float4* p = reinterpret_cast<const float4*>(Lc + j * 32);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 v = p[q];
+        lc[4 * q] = v.x; lc[4 * q + 1] = v.y; lc[4 * q + 2] = v.z; lc[4 * q + 3] = v.w;
+    }
+}
+
+__device__ __forceinline__ void shift4(float (&a)[32]) {
+#pragma unroll
+    for (int k = 0; k < 28; ++k) a[k] = a[k + 4];
+    a[28] = a[29] = a[30] = a[31] = 0.0f;
+}
+
+// Warp 0: factor D (pitch kP, Schur-updated, lower part valid) in place.
+__device__ __noinline__ void diag_factor(float* D, float* Lc, float* rinv, volatile int* ready, int count0, int lane,
+                                         int* bad) {
     float a[32];
 #pragma unroll
     for (int k = 0; k < 32; k += 4) {
@@ -124,46 +156,87 @@ __device__ __noinline__ void diag32(float* D, float* Q, float* QT, int lane, int
         a[k + 2] = (k + 2 <= lane) ? v.z : 0.0f;
         a[k + 3] = (k + 3 <= lane) ? v.w : 0.0f;
     }
-    float my_rinv = 1.0f;
     bool all_ok = true;
 #pragma unroll 1
-    for (int j = 0; j < 32; ++j) {
-        const float djj = __shfl_sync(kFull, a[0], j);
-        const bool ok = djj > 0.0f;
-        all_ok = all_ok && ok;
-        const float rj = ok ? rsqrtf(djj) : 1.0f;
-        // lanes above j hold a[0] = 0 (upper triangle)
-        const float l = (lane == j) ? (ok ? djj * rj : 1.0f) : a[0] * rj;
-        if (lane == j) my_rinv = rj;
-        D[lane * kP + j] = l;
+    for (int jb = 0; jb < 32; jb += 4) {
 #pragma unroll
-        for (int k = 1; k < 32; ++k) {  // branch-free: the shuffles issue back to back
-            const float lk = __shfl_sync(kFull, l, (j + k) & 31);
-            if (lane >= j + k) a[k] = fmaf(-l, lk, a[k]);
+        for (int jj = 0; jj < 4; ++jj) {
+            const int j = jb + jj;
+            const float djj = __shfl_sync(kFull, a[jj], j);
+            const bool ok = djj > 0.0f;
+            all_ok = all_ok && ok;
+            const float rj = ok ? rsqrtf(djj) : 1.0f;
+            // lanes above j hold a[jj] = 0 (upper triangle)
+            const float l = (lane == j) ? (ok ? djj * rj : 1.0f) : a[jj] * rj;
+            a[jj] = l;
+            D[lane * kP + j] = l;
+            if (lane >= j) Lc[j * 32 + (lane - j)] = l;
+            if (lane == j) rinv[j] = rj;
+            __syncwarp();
+            float lc[32];
+            load_column(Lc, j, lc);
+#pragma unroll
+            for (int k = 1; k < 32 - jj; ++k)
+                if (lane >= j + k) a[jj + k] = fmaf(-l, lc[k], a[jj + k]);
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) *ready = count0 + j + 1;
         }
-#pragma unroll
-        for (int k = 0; k < 31; ++k) a[k] = a[k + 1];
-        a[31] = 0.0f;
+        shift4(a);
     }
     if (!all_ok && lane == 0) atomicExch(bad, 1);
-    __syncwarp();
-    // column c = lane of L^-1 by forward elimination of L x = e_c; x[k] is row j+k
+}
+
+// Warp 1: column c = lane of L_kk^-1 by forward elimination of L x = e_c,
+// written to Q (rows) and QT (transposed), both pitch kP.
+__device__ __noinline__ void diag_inverse(const float* Lc, const float* rinv, const volatile int* ready, int count0,
+                                          float* Q, float* QT, int lane, int* bad) {
     float x[32];
 #pragma unroll
     for (int k = 0; k < 32; ++k) x[k] = (k == lane) ? 1.0f : 0.0f;
 #pragma unroll 1
-    for (int j = 0; j < 32; ++j) {
-        const float xj = x[0] * __shfl_sync(kFull, my_rinv, j);
-        Q[j * kP + lane] = xj;
-        QT[lane * kP + j] = xj;
+    for (int jb = 0; jb < 32; jb += 4) {
 #pragma unroll
-        for (int k = 1; k < 32; ++k)  // slots past row 31 hold values that are never stored
-            x[k] = fmaf(-xj, D[min(j + k, 31) * kP + j], x[k]);
+        for (int jj = 0; jj < 4; ++jj) {
+            const int j = jb + jj;
+            wait_columns(ready, count0 + j + 1, bad);
+            const float xj = x[jj] * rinv[j];
+            Q[j * kP + lane] = xj;
+            QT[lane * kP + j] = xj;
+            float lc[32];
+            load_column(Lc, j, lc);
 #pragma unroll
-        for (int k = 0; k < 31; ++k) x[k] = x[k + 1];
-        x[31] = 0.0f;
+            for (int k = 1; k < 32 - jj; ++k) x[jj + k] = fmaf(-xj, lc[k], x[jj + k]);
+        }
+        shift4(x);
     }
-    __syncwarp();
+}
+
+// Warps 2..: one panel row per lane, x L_kk^T = a by forward substitution, in
+// place in the row (pitch kP, 16-byte aligned).
+__device__ __noinline__ void diag_panel(float* row, const float* Lc, const float* rinv, const volatile int* ready,
+                                        int count0, int* bad) {
+    float a[32];
+#pragma unroll
+    for (int k = 0; k < 32; k += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(row + k);
+        a[k] = v.x; a[k + 1] = v.y; a[k + 2] = v.z; a[k + 3] = v.w;
+    }
+#pragma unroll 1
+    for (int jb = 0; jb < 32; jb += 4) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int j = jb + jj;
+            wait_columns(ready, count0 + j + 1, bad);
+            const float x = a[jj] * rinv[j];
+            row[j] = x;
+            float lc[32];
+            load_column(Lc, j, lc);
+#pragma unroll
+            for (int k = 1; k < 32 - jj; ++k) a[jj + k] = fmaf(-x, lc[k], a[jj + k]);
+        }
+        shift4(a);
+    }
 }
 
 // Four rows by one column of a row-by-row product: acc[r] = sum_{k<K}
@@ -207,10 +280,14 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
     float* sV = sA + kB * kP;       // 128 x kP: V = L^-1
     float* sVT = sV + kB * kP;      // 128 x kP: V^T
     float* sST = sVT + kB * kP;     // 3 x 32 x kSP: S^T blocks
+    float* sLc = sST + 3 * 32 * kSP;  // 32 x 32: published columns of the current diagonal block
+    float* sRinv = sLc + 32 * 32;     // 32: 1 / L_jj
+    int* sReady = reinterpret_cast<int*>(sRinv + 32);  // columns published so far (all steps)
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const size_t base = static_cast<size_t>(off) * ld + off;
     pdl_wait();
     pdl_trigger();
+    if (t == 0) *sReady = 0;
 #pragma unroll 4
     for (int e = t; e < kB * kB; e += kBaseThreads) {
         const int i = e >> 7, j = e & 127;
@@ -222,20 +299,17 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
 #pragma unroll 1
     for (int kb = 0; kb < 4; ++kb) {
         const int o = 32 * kb;
-        if (warp == 0) diag32(sA + o * kP + o, sV + o * kP + o, sVT + o * kP + o, lane, bad);
-        __syncthreads();
-        const int prow = kB - o - 32;
-        if (prow == 0) break;
-        // panel, in place (a warp owns its four rows): L[i][o+c] = sum_k A[i][o+k] V_kk[c][k]
-#pragma unroll 1
-        for (int g = warp; g < prow / 4; g += 16) {
-            const int i = o + 32 + 4 * g;
-            float acc[4];
-            dot4x1(sA + i * kP + o, kP, sV + (o + lane) * kP + o, 32, acc);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) sA[(i + r) * kP + o + lane] = acc[r];
+        const int prow = kB - o - 32;  // panel rows below the diagonal block
+        volatile int* ready = sReady;
+        if (warp == 0) {
+            diag_factor(sA + o * kP + o, sLc, sRinv, ready, 32 * kb, lane, bad);
+        } else if (warp == 1) {
+            diag_inverse(sLc, sRinv, ready, 32 * kb, sV + o * kP + o, sVT + o * kP + o, lane, bad);
+        } else if (warp - 2 < prow / 32) {
+            diag_panel(sA + (o + 32 + 32 * (warp - 2) + lane) * kP + o, sLc, sRinv, ready, 32 * kb, bad);
         }
         __syncthreads();
+        if (prow == 0) break;
         // trailing lower blocks: A[i][j] -= sum_k L[i][o+k] L[j][o+k]
         const int nbt = prow / 32;
         const int ntask = nbt * (nbt + 1) / 2 * 8;  // (block pair, four-row group)
@@ -294,7 +368,7 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
         VT_lo[g] = vt - ht;
     }
 }
-constexpr size_t kBaseSmem = (3 * kB * kP + 3 * 32 * kSP) * sizeof(float);
+constexpr size_t kBaseSmem = (3 * kB * kP + 3 * 32 * kSP + 32 * 32 + 32 + 4) * sizeof(float);
 
 // Ut = (P V P)^T on the lower triangle: Ut[i][j] = V[d-1-j][d-1-i], with split.
 __global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, float* __restrict__ Ut,
@@ -783,6 +857,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
         const int ge = umma::gemm_take_error(st);
         if (ge) rc = fail(TB_ERR_TIMEOUT, "a tcgen05 GEMM pipeline wait expired");
     }
-    if (!rc && bad) rc = fail(TB_ERR_CONFIG, "H + lambda I is not positive definite in FP32 (a Cholesky pivot <= 0)");
+    if (!rc && bad == 2) rc = fail(TB_ERR_TIMEOUT, "a wait inside the 128-block factorisation expired");
+    if (!rc && bad == 1) rc = fail(TB_ERR_CONFIG, "H + lambda I is not positive definite in FP32 (a Cholesky pivot <= 0)");
     return rc;
 }
