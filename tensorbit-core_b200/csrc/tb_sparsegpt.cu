@@ -145,6 +145,9 @@ __device__ __forceinline__ void shift4(float (&a)[32]) {
 }
 
 // Warp 0: factor D (pitch kP, Schur-updated, lower part valid) in place.
+// Columns are published four at a time (one fence and one counter update per
+// group); the column each lane needs for the next pivot comes from its own
+// register, so the shared-memory round trip feeds only the other updates.
 __device__ __noinline__ void diag_factor(float* D, float* Lc, float* rinv, volatile int* ready, int count0, int lane,
                                          int* bad) {
     float a[32];
@@ -157,6 +160,7 @@ __device__ __noinline__ void diag_factor(float* D, float* Lc, float* rinv, volat
         a[k + 3] = (k + 3 <= lane) ? v.w : 0.0f;
     }
     bool all_ok = true;
+    float my_r = 1.0f;
 #pragma unroll 1
     for (int jb = 0; jb < 32; jb += 4) {
 #pragma unroll
@@ -169,19 +173,22 @@ __device__ __noinline__ void diag_factor(float* D, float* Lc, float* rinv, volat
             // lanes above j hold a[jj] = 0 (upper triangle)
             const float l = (lane == j) ? (ok ? djj * rj : 1.0f) : a[jj] * rj;
             a[jj] = l;
-            D[lane * kP + j] = l;
+            if (lane == j) my_r = rj;
+            if (lane == j + 1) a[jj + 1] = fmaf(-l, l, a[jj + 1]);  // next pivot first
             if (lane >= j) Lc[j * 32 + (lane - j)] = l;
-            if (lane == j) rinv[j] = rj;
             __syncwarp();
             float lc[32];
             load_column(Lc, j, lc);
 #pragma unroll
             for (int k = 1; k < 32 - jj; ++k)
-                if (lane >= j + k) a[jj + k] = fmaf(-l, lc[k], a[jj + k]);
-            __threadfence_block();
-            __syncwarp();
-            if (lane == 0) *ready = count0 + j + 1;
+                if (lane >= j + k && !(k == 1 && lane == j + 1)) a[jj + k] = fmaf(-l, lc[k], a[jj + k]);
         }
+        // columns jb..jb+3 are final: L into D (zeros above), 1/L_jj, then publish
+        *reinterpret_cast<float4*>(D + lane * kP + jb) = make_float4(a[0], a[1], a[2], a[3]);
+        if (lane >= jb && lane < jb + 4) rinv[lane] = my_r;
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) *ready = count0 + jb + 4;
         shift4(a);
     }
     if (!all_ok && lane == 0) atomicExch(bad, 1);
@@ -199,7 +206,7 @@ __device__ __noinline__ void diag_inverse(const float* Lc, const float* rinv, co
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int j = jb + jj;
-            wait_columns(ready, count0 + j + 1, bad);
+            if (jj == 0) wait_columns(ready, count0 + jb + 4, bad);
             const float xj = x[jj] * rinv[j];
             Q[j * kP + lane] = xj;
             QT[lane * kP + j] = xj;
@@ -227,7 +234,7 @@ __device__ __noinline__ void diag_panel(float* row, const float* Lc, const float
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int j = jb + jj;
-            wait_columns(ready, count0 + j + 1, bad);
+            if (jj == 0) wait_columns(ready, count0 + jb + 4, bad);
             const float x = a[jj] * rinv[j];
             row[j] = x;
             float lc[32];
