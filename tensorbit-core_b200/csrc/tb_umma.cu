@@ -24,7 +24,9 @@ namespace umma {
 namespace {
 
 constexpr int kTile = 128;              // rows of A / B per tile, M = N = 128
-constexpr int kTileBytes = kTile * 128; // one 128-row x 128-byte operand slice
+// Operand K-slices are 128 rows x SW bytes, loaded by TMA with the SW-byte
+// swizzle (SW = 128 or 64): the canonical K-major layouts whose 8-row atoms
+// sit 8 * SW bytes apart.
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
 
 __device__ int g_umma_error;
@@ -65,8 +67,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+template <int SW>
+__device__ __forceinline__ uint64_t sw_desc(uint32_t addr) {
+    constexpr uint64_t kLayout = (SW == 128) ? 2ull : 4ull;  // 128-byte / 64-byte swizzle
+    constexpr uint64_t kSbo = (8ull * SW) >> 4;              // 8-row atom stride
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (1ull << 16) | (kSbo << 32) | (1ull << 46) | (kLayout << 61);
 }
 template <int KIND>
 __device__ __forceinline__ void mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
@@ -111,14 +116,75 @@ __device__ __forceinline__ float tf32_hi(float x) {
 // Warps 0-3 accumulate and store the tile (warp w owns TMEM lanes / rows
 // 32w..32w+31), warp 4 lane 0 issues TMA, warp 5 lane 0 issues tcgen05.mma.
 // The tensor core's FP32 accumulation truncates, so the K loop is cut into
-// groups of kGroup 128-byte slices: each group accumulates in one of two TMEM
+// groups of 128 K elements: each group accumulates in one of two TMEM
 // buffers, and warps 0-3 add the finished buffer into FP32 registers (round to
 // nearest) while the next group runs in the other buffer.
-constexpr int kGroup = 4;
 constexpr int kThreadsGemm = 192;
 constexpr int kStagePitch = kTile + 4;  // epilogue staging pitch (floats): float4 rows without bank conflicts
 
-template <int KIND, int STAGES>
+// Epilogue of one warp: acc holds row `row0 + lane` of a 128-column output
+// tile starting at column col0.  The 32 x 128 block is staged in shared memory
+// (sbuf, pitch kStagePitch) and handled one output row per step with lane l on
+// columns 4l..4l+3, so every global load and store is a coalesced 512-byte row.
+__device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc)[kTile], float* sbuf,
+                                           long long row0, long long col0, int lane) {
+#pragma unroll
+    for (int c = 0; c < kTile / 4; ++c)
+        *reinterpret_cast<float4*>(sbuf + lane * kStagePitch + 4 * c) =
+            make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+    __syncwarp();
+    const long long gcol = col0 + 4 * lane;
+    constexpr int kBatch = 8;  // rows whose Cin loads are in flight together
+    for (int rb = 0; rb < 32; rb += kBatch) {
+        float4 cin[kBatch];
+        if (out.beta != 0.0f) {
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u)
+                cin[u] = *reinterpret_cast<const float4*>(out.Cin + (row0 + rb + u) * out.ldcin + gcol);
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const long long grow = row0 + rb + u;
+            float4* sp = reinterpret_cast<float4*>(sbuf + (rb + u) * kStagePitch + 4 * lane);
+            const float4 a = *sp;
+            float o[4] = {out.alpha * a.x, out.alpha * a.y, out.alpha * a.z, out.alpha * a.w};
+            if (out.beta != 0.0f) {
+                o[0] += out.beta * cin[u].x;
+                o[1] += out.beta * cin[u].y;
+                o[2] += out.beta * cin[u].z;
+                o[3] += out.beta * cin[u].w;
+            }
+            const float4 ov = make_float4(o[0], o[1], o[2], o[3]);
+            if (out.C) *reinterpret_cast<float4*>(out.C + grow * out.ldc + gcol) = ov;
+            if (out.C_hi) {
+                float h[4], l[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    h[e] = tf32_hi(o[e]);
+                    l[e] = o[e] - h[e];
+                }
+                *reinterpret_cast<float4*>(out.C_hi + grow * out.ld_split + gcol) = make_float4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<float4*>(out.C_lo + grow * out.ld_split + gcol) = make_float4(l[0], l[1], l[2], l[3]);
+            }
+            if (out.Ct) *sp = ov;  // final values back for the transposed copy
+        }
+    }
+    if (out.Ct) {  // Ct[col][row]: lane = row again, 32 consecutive rows per store
+        __syncwarp();
+#pragma unroll 4
+        for (int c = 0; c < kTile / 4; ++c) {
+            const float4 x = *reinterpret_cast<const float4*>(sbuf + lane * kStagePitch + 4 * c);
+            const long long col = col0 + 4 * c;
+            const long long row = row0 + lane;
+            out.Ct[(col + 0) * out.ldct + row] = x.x;
+            out.Ct[(col + 1) * out.ldct + row] = x.y;
+            out.Ct[(col + 2) * out.ldct + row] = x.z;
+            out.Ct[(col + 3) * out.ldct + row] = x.w;
+        }
+    }
+}
+
+template <int KIND, int STAGES, int SW>
 __global__ void __launch_bounds__(kThreadsGemm, 1)
 gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
                const __grid_constant__ CUtensorMap tB0, const __grid_constant__ CUtensorMap tB1, const int nk,
@@ -126,7 +192,10 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
     const int tm = blockIdx.y, tn = blockIdx.x;
     if (out.lower_only && tn > tm) return;
     constexpr int kOps = (KIND == kTF32x3) ? 4 : 2;
-    constexpr int kElems = (KIND == kTF32x3) ? 32 : 64;  // K elements per 128-byte slice
+    constexpr int kElems = SW / ((KIND == kTF32x3) ? 4 : 2);  // K elements per slice
+    constexpr int kTileBytes = kTile * SW;                   // one operand slice
+    constexpr int kSteps = SW / 32;                          // 32-byte MMA K steps per slice
+    constexpr int kGroup = 128 / kElems * ((KIND == kTF32x3) ? 1 : 2);  // slices per promotion group
     constexpr uint32_t kFmt = (KIND == kTF32x3) ? 2u : 1u;
     constexpr uint32_t kIdesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((kTile >> 3) << 17) | ((kTile >> 4) << 24);
     extern __shared__ uint8_t smem_raw[];
@@ -221,13 +290,13 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
                     const int s = kc % STAGES;
                     if (*abort_flag || !mbar_wait(smem_u32(&full[s]), (kc / STAGES) & 1)) { ok = false; break; }
                     fence_after();
-                    const uint64_t a0 = sw128_desc(tile(s, 0)), b0 = sw128_desc(tile(s, 1));
+                    const uint64_t a0 = sw_desc<SW>(tile(s, 0)), b0 = sw_desc<SW>(tile(s, 1));
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
+                    for (int kk = 0; kk < kSteps; ++kk) {
                         const uint64_t adv = static_cast<uint64_t>(kk * 2);  // +32 bytes along K
                         const uint32_t acc = (kc != g * kGroup || kk) ? 1u : 0u;
                         if constexpr (KIND == kTF32x3) {
-                            const uint64_t a1 = sw128_desc(tile(s, 2)), b1 = sw128_desc(tile(s, 3));
+                            const uint64_t a1 = sw_desc<SW>(tile(s, 2)), b1 = sw_desc<SW>(tile(s, 3));
                             mma<KIND>(acc_t, a0 + adv, b1 + adv, kIdesc, acc);
                             mma<KIND>(acc_t, a1 + adv, b0 + adv, kIdesc, 1u);
                             mma<KIND>(acc_t, a0 + adv, b0 + adv, kIdesc, 1u);
@@ -272,66 +341,10 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
         if (!ok) {
             if (lane == 0) atomicExch(&g_umma_error, 1);
         } else {
-            // All MMAs have completed, so the operand ring is free: stage this
-            // warp's 32 x 128 block (row = lane) with a 132-float pitch, then
-            // handle one output row per step with lane l on columns 4l..4l+3.
+            // All MMAs have completed, so the operand ring is free for staging.
             static_assert(4 * 32 * kStagePitch * 4 <= STAGES * kOps * kTileBytes, "epilogue staging exceeds the ring");
-            float* sbuf = reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch;
-#pragma unroll
-            for (int c = 0; c < kTile / 4; ++c)
-                *reinterpret_cast<float4*>(sbuf + lane * kStagePitch + 4 * c) =
-                    make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
-            __syncwarp();
-            const long long grow0 = static_cast<long long>(tm) * kTile + warp * 32;
-            const long long gcol = static_cast<long long>(tn) * kTile + 4 * lane;
-            constexpr int kBatch = 8;  // rows whose Cin loads are in flight together
-            for (int rb = 0; rb < 32; rb += kBatch) {
-                float4 cin[kBatch];
-                if (out.beta != 0.0f) {
-#pragma unroll
-                    for (int u = 0; u < kBatch; ++u)
-                        cin[u] = *reinterpret_cast<const float4*>(out.Cin + (grow0 + rb + u) * out.ldcin + gcol);
-                }
-#pragma unroll
-                for (int u = 0; u < kBatch; ++u) {
-                    const long long grow = grow0 + rb + u;
-                    float4* sp = reinterpret_cast<float4*>(sbuf + (rb + u) * kStagePitch + 4 * lane);
-                    const float4 a = *sp;
-                    float o[4] = {out.alpha * a.x, out.alpha * a.y, out.alpha * a.z, out.alpha * a.w};
-                    if (out.beta != 0.0f) {
-                        o[0] += out.beta * cin[u].x;
-                        o[1] += out.beta * cin[u].y;
-                        o[2] += out.beta * cin[u].z;
-                        o[3] += out.beta * cin[u].w;
-                    }
-                    const float4 ov = make_float4(o[0], o[1], o[2], o[3]);
-                    if (out.C) *reinterpret_cast<float4*>(out.C + grow * out.ldc + gcol) = ov;
-                    if (out.C_hi) {
-                        float h[4], l[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            h[e] = tf32_hi(o[e]);
-                            l[e] = o[e] - h[e];
-                        }
-                        *reinterpret_cast<float4*>(out.C_hi + grow * out.ld_split + gcol) = make_float4(h[0], h[1], h[2], h[3]);
-                        *reinterpret_cast<float4*>(out.C_lo + grow * out.ld_split + gcol) = make_float4(l[0], l[1], l[2], l[3]);
-                    }
-                    if (out.Ct) *sp = ov;  // final values back for the transposed copy
-                }
-            }
-            if (out.Ct) {  // Ct[col][row]: lane = row again, 32 consecutive rows per store
-                __syncwarp();
-#pragma unroll 4
-                for (int c = 0; c < kTile / 4; ++c) {
-                    const float4 x = *reinterpret_cast<const float4*>(sbuf + lane * kStagePitch + 4 * c);
-                    const long long col = static_cast<long long>(tn) * kTile + 4 * c;
-                    const long long row = grow0 + lane;
-                    out.Ct[(col + 0) * out.ldct + row] = x.x;
-                    out.Ct[(col + 1) * out.ldct + row] = x.y;
-                    out.Ct[(col + 2) * out.ldct + row] = x.z;
-                    out.Ct[(col + 3) * out.ldct + row] = x.w;
-                }
-            }
+            store_rows(out, acc, reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch,
+                       static_cast<long long>(tm) * kTile + warp * 32, static_cast<long long>(tn) * kTile, lane);
         }
     }
     fence_before();
@@ -339,6 +352,224 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
     if (warp == 0) {
         fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTile));
+    }
+}
+
+// ---- CTA-pair variant (cta_group::2) for large FP32-accurate products --------
+// Two CTAs of a cluster compute a 256 x NB tile (NB = 128 or 256) with one
+// tcgen05.mma stream: each CTA holds its 128 rows of A and NB/2 of the NB B
+// rows in its own shared memory, and its 128 x NB slice of the accumulator in
+// its own TMEM.  Wider MMAs pay off: the per-instruction cost is measured at
+// ~1.46x for N = 64 versus N = 128 (not 2x), so N = 256 per instruction does
+// the same work in fewer, longer MMAs.  The even CTA (rank 0) issues the MMAs
+// and owns the full and accumulator-empty barriers: both CTAs' TMA loads
+// complete on its full barrier, its commits arrive on both CTAs' barriers,
+// and both CTAs' epilogue warps arrive on its accumulator-empty barrier.
+// Operand loads carry no multicast.  All waits are bounded; a CTA that gives
+// up records the error and both CTAs still meet at the closing cluster barrier.
+constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // shared address of the even CTA's copy
+constexpr int kPairA = kTile * 128;           // 128 rows x 128 B
+
+template <int NB> struct Pair {
+    static constexpr int kB = (NB / 2) * 128;              // NB/2 rows x 128 B per CTA
+    static constexpr int kStage = 2 * kPairA + 2 * kB;      // A hi/lo, B hi/lo
+    static constexpr int kStages = (NB == 256) ? 3 : 4;
+    static constexpr int kEpiWarps = NB / 32;               // 4 warps per 128 columns
+    static constexpr int kThreads = 32 * (kEpiWarps + 2);   // + TMA warp + MMA warp
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStage + 1024 + 256;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t even_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(even_bar)
+        : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+        ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u));
+}
+__device__ __forceinline__ void commit_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        ::"r"(bar), "h"(static_cast<uint16_t>(3))
+        : "memory");
+}
+
+template <int NB>
+__global__ void __launch_bounds__(Pair<NB>::kThreads, 1)
+gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
+                    const __grid_constant__ CUtensorMap tB0, const __grid_constant__ CUtensorMap tB1, const int nk,
+                    const GemmOut out) {
+    using P = Pair<NB>;
+    constexpr int kStages = P::kStages;
+    constexpr int kEpi = P::kEpiWarps;
+    const uint32_t rank = cluster_rank();
+    const int tn = blockIdx.x >> 1, tm2 = blockIdx.y;  // NB-column tile, 256-row tile
+    constexpr int kSub = NB / kTile;                    // 128-column sub-tiles per tile
+    // lower_only: the pair skips together when every 128 x 128 sub-tile lies above the diagonal
+    if (out.lower_only && tn * kSub > 2 * tm2 + 1) return;
+    constexpr int kElems = 32;  // TF32 elements per 128-byte slice
+    constexpr int kGroup = 4;   // slices per promotion group (128 K elements)
+    constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((NB >> 3) << 17) | ((2 * kTile >> 4) << 24);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * P::kStage);
+    uint64_t* empty = full + kStages;
+    uint64_t* accfull = empty + kStages;
+    uint64_t* accempty = accfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ngroups = (nk + kGroup - 1) / kGroup;
+
+    if (threadIdx.x == 32 * kEpi) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tB0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA1)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tB1)) : "memory");
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&accfull[b]), 1);
+            mbar_init(smem_u32(&accempty[b]), 2 * kEpi);  // the epilogue warps of both CTAs
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(2 * NB));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    fence_before();
+    cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
+    auto a_tile = [&](int s, int lo) { return smem_u32(smem + s * P::kStage + lo * kPairA); };
+    auto b_tile = [&](int s, int lo) { return smem_u32(smem + s * P::kStage + 2 * kPairA + lo * P::kB); };
+
+    if (warp == kEpi) {
+        if (lane == 0) {  // TMA producer, both CTAs
+            const int arow = tm2 * 2 * kTile + static_cast<int>(rank) * kTile;
+            const int brow = tn * NB + static_cast<int>(rank) * (NB / 2);
+            int issued = 0;
+            for (int kc = 0; kc < nk; ++kc) {
+                const int s = kc % kStages;
+                if (kc >= kStages && !mbar_wait(smem_u32(&empty[s]), ((kc / kStages) - 1) & 1)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                if (*abort_flag) break;
+                const uint32_t even_full = smem_u32(&full[s]) & kPeerMask;
+                if (rank == 0) mbar_expect_tx(smem_u32(&full[s]), 2 * P::kStage);
+                const int x = kc * kElems;
+                tma_load_2d_pair(a_tile(s, 0), &tA0, x, arow, even_full);
+                tma_load_2d_pair(a_tile(s, 1), &tA1, x, arow, even_full);
+                tma_load_2d_pair(b_tile(s, 0), &tB0, x, brow, even_full);
+                tma_load_2d_pair(b_tile(s, 1), &tB1, x, brow, even_full);
+                issued = kc + 1;
+            }
+            // Bounded drain after an abort: the even CTA's full barrier counts both CTAs' loads.
+            if (*abort_flag && rank == 0)
+                for (int kc = std::max(0, issued - kStages); kc < issued; ++kc)
+                    mbar_wait(smem_u32(&full[kc % kStages]), (kc / kStages) & 1);
+        }
+        __syncwarp();
+    } else if (warp == kEpi + 1) {
+        if (lane == 0 && rank == 0) {  // MMA issuer, even CTA only
+            bool ok = true;
+            for (int g = 0; g < ngroups && ok; ++g) {
+                const int b = g & 1;
+                if (g >= 2 && !mbar_wait(smem_u32(&accempty[b]), ((g >> 1) - 1) & 1)) { ok = false; break; }
+                fence_after();
+                const uint32_t acc_t = tmem + static_cast<uint32_t>(b * NB);
+                const int k_end = std::min(nk, (g + 1) * kGroup);
+                for (int kc = g * kGroup; kc < k_end; ++kc) {
+                    const int s = kc % kStages;
+                    if (*abort_flag || !mbar_wait(smem_u32(&full[s]), (kc / kStages) & 1)) { ok = false; break; }
+                    fence_after();
+                    const uint64_t a0 = sw_desc<128>(a_tile(s, 0)), a1 = sw_desc<128>(a_tile(s, 1));
+                    const uint64_t b0 = sw_desc<128>(b_tile(s, 0)), b1 = sw_desc<128>(b_tile(s, 1));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t adv = static_cast<uint64_t>(kk * 2);  // +32 bytes along K
+                        const uint32_t acc = (kc != g * kGroup || kk) ? 1u : 0u;
+                        mma_pair(acc_t, a0 + adv, b1 + adv, kIdesc, acc);
+                        mma_pair(acc_t, a1 + adv, b0 + adv, kIdesc, 1u);
+                        mma_pair(acc_t, a0 + adv, b0 + adv, kIdesc, 1u);
+                    }
+                    commit_pair(smem_u32(&empty[s]));  // frees stage s in both CTAs
+                }
+                commit_pair(smem_u32(&accfull[b]));
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                commit_pair(smem_u32(&accfull[0]));
+                commit_pair(smem_u32(&accfull[1]));
+            }
+        }
+        __syncwarp();
+    } else {
+        // Epilogue warps of both CTAs: warp e reads TMEM lanes 32 (e % 4).. and
+        // the 128 accumulator columns 128 (e / 4)..; promotes each finished group.
+        const int quad = warp & 3, half = warp >> 2;
+        float acc[kTile];
+#pragma unroll
+        for (int j = 0; j < kTile; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        for (int g = 0; g < ngroups; ++g) {
+            const int b = g & 1;
+            if (!mbar_wait(smem_u32(&accfull[b]), (g >> 1) & 1) || *abort_flag) { ok = false; break; }
+            fence_after();
+            const uint32_t base = tmem + (static_cast<uint32_t>(quad * 32) << 16) +
+                                  static_cast<uint32_t>(b * NB + half * kTile);
+#pragma unroll
+            for (int c = 0; c < kTile / 32; ++c) {
+                float v[32];
+                tmem_ld32(base + static_cast<uint32_t>(c * 32), v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], v[j]);
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(smem_u32(&accempty[b]) & kPeerMask)
+                             : "memory");
+        }
+        const int sub_col = tn * kSub + half;                    // 128-column sub-tile of this warp
+        const int sub_row = 2 * tm2 + static_cast<int>(rank);    // 128-row tile of this CTA
+        if (!ok) {
+            if (lane == 0) atomicExch(&g_umma_error, 1);
+        } else if (!(out.lower_only && sub_col > sub_row)) {
+            static_assert(kEpi * 32 * kStagePitch * 4 <= kStages * P::kStage, "epilogue staging exceeds the ring");
+            store_rows(out, acc, reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch,
+                       static_cast<long long>(sub_row) * kTile + quad * 32, static_cast<long long>(sub_col) * kTile,
+                       lane);
+        }
+    }
+    fence_before();
+    cluster_sync_all();  // every MMA of the pair is complete and both epilogues are done
+    if (warp == 0) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NB));
     }
 }
 
@@ -358,40 +589,73 @@ EncodeFn encode_fn() {
     return fn;
 }
 
-// Row-major [rows, k] operand, 128-row x 128-byte boxes with the 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* base, bool bf16, long long rows, long long k, long long ld) {
+// Row-major [rows, k] operand, 128-row x sw-byte boxes with the sw-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, bool bf16, long long rows, long long k, long long ld, int sw,
+             int box_rows = kTile) {
     EncodeFn enc = encode_fn();
     if (!enc) return fail(TB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const int esize = bf16 ? 2 : 4;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(kTile)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(sw / esize), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                      const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     sw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(TB_ERR_ARG, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return TB_OK;
 }
 
-template <int KIND, int STAGES>
+template <int KIND, int STAGES, int SW>
 int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0, const CUtensorMap& b1, int M, int N,
            int nk, const GemmOut& out, cudaStream_t st) {
     constexpr int kOps = (KIND == kTF32x3) ? 4 : 2;
-    const size_t smem = static_cast<size_t>(STAGES) * kOps * kTileBytes + 1024 + 256;
+    const size_t smem = static_cast<size_t>(STAGES) * kOps * kTile * SW + 1024 + 256;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [&] {
-        attr = cudaFuncSetAttribute(gemm_nt_kernel<KIND, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr = cudaFuncSetAttribute(gemm_nt_kernel<KIND, STAGES, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem));
     });
     if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute(gemm_nt_kernel)");
-    const cudaError_t e = launch_pdl(gemm_nt_kernel<KIND, STAGES>, dim3(N / kTile, M / kTile), dim3(kThreadsGemm),
+    const cudaError_t e = launch_pdl(gemm_nt_kernel<KIND, STAGES, SW>, dim3(N / kTile, M / kTile), dim3(kThreadsGemm),
                                      smem, st, a0, a1, b0, b1, nk, out);
     return e == cudaSuccess ? check_launch("gemm_nt_kernel") : cuda_fail(e, "gemm_nt_kernel launch");
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launches the CTA-pair kernel: clusters of two along x, programmatic
+// serialization as for the single-CTA kernel.
+template <int NB>
+int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0, const CUtensorMap& b1, int M,
+                int N, int nk, const GemmOut& out, cudaStream_t st) {
+    using P = Pair<NB>;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [&] {
+        attr = cudaFuncSetAttribute(gemm_nt_pair_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(P::kSmem));
+    });
+    if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute(gemm_nt_pair_kernel)");
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (N / NB), M / (2 * kTile));
+    cfg.blockDim = dim3(P::kThreads);
+    cfg.dynamicSmemBytes = P::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_nt_pair_kernel<NB>, a0, a1, b0, b1, nk, out);
+    return e == cudaSuccess ? check_launch("gemm_nt_pair_kernel") : cuda_fail(e, "gemm_nt_pair_kernel launch");
+}
 
 }  // namespace
 
@@ -414,15 +678,31 @@ int gemm_nt(Kind kind, const Operand& A, const Operand& B, int M, int N, int K, 
         return fail(TB_ERR_ARG, "gemm_nt: a triangular A must be square (M == K)");
     const bool bf16 = kind == kBF16;
     CUtensorMap a0{}, a1{}, b0{}, b1{};
-    int rc = make_map(&a0, A.hi, bf16, M, K, A.ld);
-    if (!rc) rc = make_map(&b0, B.hi, bf16, N, K, B.ld);
-    if (!rc && !bf16) rc = make_map(&a1, A.lo, false, M, K, A.ld);
-    if (!rc && !bf16) rc = make_map(&b1, B.lo, false, N, K, B.ld);
+    // 128-byte slices: three stages for TF32x3, four for BF16.  (64-byte slices
+    // with six stages were measured slower: 176 vs 211 TFLOP/s at 4096^3.)
+    const int sw = 128;
+    // Large FP32-accurate products on CTA pairs (256-row tiles); a triangular A
+    // stays on single CTAs, whose K ranges follow each 128-row tile.
+    if (!bf16 && M % (2 * kTile) == 0 && K >= 512 && out.tri_a == 0) {
+        CUtensorMap pa0{}, pa1{}, pb0{}, pb1{};
+        int rc = make_map(&pa0, A.hi, false, M, K, A.ld, sw);
+        if (!rc) rc = make_map(&pa1, A.lo, false, M, K, A.ld, sw);
+        const int nb = (N % 256 == 0) ? 256 : 128;  // 256-wide MMAs where N allows
+        if (!rc) rc = make_map(&pb0, B.hi, false, N, K, B.ld, sw, nb / 2);
+        if (!rc) rc = make_map(&pb1, B.lo, false, N, K, B.ld, sw, nb / 2);
+        if (rc) return rc;
+        return nb == 256 ? launch_pair<256>(pa0, pa1, pb0, pb1, M, N, K / 32, out, stream)
+                         : launch_pair<128>(pa0, pa1, pb0, pb1, M, N, K / 32, out, stream);
+    }
+    int rc = make_map(&a0, A.hi, bf16, M, K, A.ld, sw);
+    if (!rc) rc = make_map(&b0, B.hi, bf16, N, K, B.ld, sw);
+    if (!rc && !bf16) rc = make_map(&a1, A.lo, false, M, K, A.ld, sw);
+    if (!rc && !bf16) rc = make_map(&b1, B.lo, false, N, K, B.ld, sw);
     if (rc) return rc;
     if (bf16) { a1 = a0; b1 = b0; }
-    const int nk = K / kstep;
-    return bf16 ? launch<kBF16, 4>(a0, a1, b0, b1, M, N, nk, out, stream)
-                : launch<kTF32x3, 3>(a0, a1, b0, b1, M, N, nk, out, stream);
+    const int nk = K / (sw / (bf16 ? 2 : 4));
+    return bf16 ? launch<kBF16, 4, 128>(a0, a1, b0, b1, M, N, nk, out, stream)
+                : launch<kTF32x3, 3, 128>(a0, a1, b0, b1, M, N, nk, out, stream);
 }
 
 int gemm_take_error(cudaStream_t stream) {

@@ -1,5 +1,7 @@
 """GPU: the tcgen05 NT GEMM (3xTF32 and BF16) against float64, with the error
-bar of an FP32 (non-TF32) cuBLAS product of the same operands."""
+bar of an FP32 (non-TF32) cuBLAS product of the same operands.  3xTF32 shapes
+with M a multiple of 256 and K >= 512 run on CTA pairs (cta_group::2), the
+others on single CTAs; both paths appear below, with and without lower_only."""
 import ctypes as C
 
 import pytest
@@ -16,6 +18,7 @@ def split(torch, tb, x):
 @pytest.mark.parametrize("M,N,K,alpha,beta,lower,kind", [
     (128, 128, 32, 1.0, 0.0, 0, "x3"), (256, 384, 96, 1.0, 0.0, 0, "x3"), (1024, 1024, 1024, 1.0, 0.0, 0, "x3"),
     (512, 256, 4096, 1.0, 0.0, 0, "x3"), (384, 384, 256, -1.0, 1.0, 1, "x3"), (2048, 1024, 512, 0.5, 2.0, 0, "x3"),
+    (768, 768, 512, -1.0, 1.0, 1, "x3"), (640, 384, 1024, 1.0, 0.0, 0, "x3"), (256, 128, 8192, 1.0, 0.0, 0, "x3"),
     (128, 128, 64, 1.0, 0.0, 0, "bf16"), (1024, 512, 2048, 0.5, 1.0, 0, "bf16"), (768, 768, 128, 1.0, 0.0, 1, "bf16")])
 def test_gemm_nt_matches_float64(cuda, tblib, M, N, K, alpha, beta, lower, kind):
     torch = cuda
