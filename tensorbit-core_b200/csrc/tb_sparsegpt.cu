@@ -373,6 +373,15 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
         VT[g] = vt;
         VT_hi[g] = ht;
         VT_lo[g] = vt - ht;
+        // Zero the neighbouring off-diagonal blocks no other step writes: V's block
+        // to the right (above the diagonal) and V^T's block below.  The inverse
+        // steps' CTA-pair products read one 128-block past the triangle there.
+        if (off + kB < ld) {
+            const size_t gr = base + static_cast<size_t>(i) * ld + kB + j;         // V[off+i][off+128+j]
+            const size_t gb = base + static_cast<size_t>(kB + i) * ld + j;         // V^T[off+128+i][off+j]
+            V[gr] = 0.0f; V_hi[gr] = 0.0f; V_lo[gr] = 0.0f;
+            VT[gb] = 0.0f; VT_hi[gb] = 0.0f; VT_lo[gb] = 0.0f;
+        }
     }
 }
 constexpr size_t kBaseSmem = (3 * kB * kP + 3 * 32 * kSP + 32 * 32 + 32 + 4) * sizeof(float);

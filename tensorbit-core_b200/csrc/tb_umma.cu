@@ -432,7 +432,14 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ngroups = (nk + kGroup - 1) / kGroup;
+    // K slices [kc0, kc0 + nkr): a triangular A restricts them to the union of the
+    // pair's two 128-row tiles (the extra 128-block is a zero block next to the
+    // triangle, written by the producer of A)
+    int kc0 = 0, kc1 = nk;
+    if (out.tri_a == 1) kc0 = min(nk, 2 * tm2 * (kTile / kElems));
+    else if (out.tri_a == 2) kc1 = min(nk, (2 * tm2 + 2) * (kTile / kElems));
+    const int nkr = max(0, kc1 - kc0);
+    const int ngroups = (nkr + kGroup - 1) / kGroup;
 
     if (threadIdx.x == 32 * kEpi) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA0)) : "memory");
@@ -471,7 +478,7 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
             const int arow = tm2 * 2 * kTile + static_cast<int>(rank) * kTile;
             const int brow = tn * NB + static_cast<int>(rank) * (NB / 2);
             int issued = 0;
-            for (int kc = 0; kc < nk; ++kc) {
+            for (int kc = 0; kc < nkr; ++kc) {
                 const int s = kc % kStages;
                 if (kc >= kStages && !mbar_wait(smem_u32(&empty[s]), ((kc / kStages) - 1) & 1)) {
                     *abort_flag = 1;
@@ -480,7 +487,7 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
                 if (*abort_flag) break;
                 const uint32_t even_full = smem_u32(&full[s]) & kPeerMask;
                 if (rank == 0) mbar_expect_tx(smem_u32(&full[s]), 2 * P::kStage);
-                const int x = kc * kElems;
+                const int x = (kc0 + kc) * kElems;
                 tma_load_2d_pair(a_tile(s, 0), &tA0, x, arow, even_full);
                 tma_load_2d_pair(a_tile(s, 1), &tA1, x, arow, even_full);
                 tma_load_2d_pair(b_tile(s, 0), &tB0, x, brow, even_full);
@@ -501,7 +508,7 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
                 if (g >= 2 && !mbar_wait(smem_u32(&accempty[b]), ((g >> 1) - 1) & 1)) { ok = false; break; }
                 fence_after();
                 const uint32_t acc_t = tmem + static_cast<uint32_t>(b * NB);
-                const int k_end = std::min(nk, (g + 1) * kGroup);
+                const int k_end = std::min(nkr, (g + 1) * kGroup);
                 for (int kc = g * kGroup; kc < k_end; ++kc) {
                     const int s = kc % kStages;
                     if (*abort_flag || !mbar_wait(smem_u32(&full[s]), (kc / kStages) & 1)) { ok = false; break; }
@@ -681,9 +688,10 @@ int gemm_nt(Kind kind, const Operand& A, const Operand& B, int M, int N, int K, 
     // 128-byte slices: three stages for TF32x3, four for BF16.  (64-byte slices
     // with six stages were measured slower: 176 vs 211 TFLOP/s at 4096^3.)
     const int sw = 128;
-    // Large FP32-accurate products on CTA pairs (256-row tiles); a triangular A
-    // stays on single CTAs, whose K ranges follow each 128-row tile.
-    if (!bf16 && M % (2 * kTile) == 0 && K >= 512 && out.tri_a == 0) {
+    // Large FP32-accurate products on CTA pairs (256-row tiles).  With a
+    // triangular A the pair runs over the union of its two row tiles' K ranges,
+    // one 128-block past the triangle, which the caller keeps zero.
+    if (!bf16 && M % (2 * kTile) == 0 && K >= 512) {
         CUtensorMap pa0{}, pa1{}, pb0{}, pb1{};
         int rc = make_map(&pa0, A.hi, false, M, K, A.ld, sw);
         if (!rc) rc = make_map(&pa1, A.lo, false, M, K, A.ld, sw);

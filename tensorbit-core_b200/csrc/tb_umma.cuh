@@ -44,7 +44,11 @@ struct GemmOut {
     float alpha, beta;
     int lower_only;      // compute only tiles with tile_row >= tile_col
     int tri_a;           // A is square and triangular (M == K): 1 = upper, so output tile row
-                         // t runs over K tiles t.. only; 2 = lower, K tiles ..t only; 0 = dense
+                         // t runs over K tiles t.. only; 2 = lower, K tiles ..t only; 0 = dense.
+                         // Products on CTA pairs (M % 256 == 0, K >= 512) run a pair of row
+                         // tiles over the union of their ranges, so the 128-block next to
+                         // the triangle's diagonal blocks (below for upper, right for lower)
+                         // must be zero.
 };
 
 // Operand view for the host wrapper: row-major [rows, K] with leading dimension ld (elements).
