@@ -370,10 +370,11 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
 constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // shared address of the even CTA's copy
 constexpr int kPairA = kTile * 128;           // 128 rows x 128 B
 
-template <int NB> struct Pair {
+template <int KIND, int NB> struct Pair {
+    static constexpr int kParts = (KIND == kTF32x3) ? 2 : 1; // hi/lo or the BF16 operand alone
     static constexpr int kB = (NB / 2) * 128;              // NB/2 rows x 128 B per CTA
-    static constexpr int kStage = 2 * kPairA + 2 * kB;      // A hi/lo, B hi/lo
-    static constexpr int kStages = (NB == 256) ? 3 : 4;
+    static constexpr int kStage = kParts * (kPairA + kB);
+    static constexpr int kStages = (192 * 1024) / kStage;   // 3 or 4 (TF32x3), 6 or 8 (BF16)
     static constexpr int kEpiWarps = NB / 32;               // 4 warps per 128 columns
     static constexpr int kThreads = 32 * (kEpiWarps + 2);   // + TMA warp + MMA warp
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStage + 1024 + 256;
@@ -394,11 +395,19 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(even_bar)
         : "memory");
 }
+template <int KIND>
 __device__ __forceinline__ void mma_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
-        ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u));
+    if constexpr (KIND == kTF32x3) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+            ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+            ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u));
+    }
 }
 __device__ __forceinline__ void commit_pair(uint32_t bar) {
     asm volatile(
@@ -407,12 +416,12 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
         : "memory");
 }
 
-template <int NB>
-__global__ void __launch_bounds__(Pair<NB>::kThreads, 1)
+template <int KIND, int NB>
+__global__ void __launch_bounds__(Pair<KIND, NB>::kThreads, 1)
 gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
                     const __grid_constant__ CUtensorMap tB0, const __grid_constant__ CUtensorMap tB1, const int nk,
                     const GemmOut out) {
-    using P = Pair<NB>;
+    using P = Pair<KIND, NB>;
     constexpr int kStages = P::kStages;
     constexpr int kEpi = P::kEpiWarps;
     const uint32_t rank = cluster_rank();
@@ -420,9 +429,10 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
     constexpr int kSub = NB / kTile;                    // 128-column sub-tiles per tile
     // lower_only: the pair skips together when every 128 x 128 sub-tile lies above the diagonal
     if (out.lower_only && tn * kSub > 2 * tm2 + 1) return;
-    constexpr int kElems = 32;  // TF32 elements per 128-byte slice
-    constexpr int kGroup = 4;   // slices per promotion group (128 K elements)
-    constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((NB >> 3) << 17) | ((2 * kTile >> 4) << 24);
+    constexpr int kElems = (KIND == kTF32x3) ? 32 : 64;  // K elements per 128-byte slice
+    constexpr int kGroup = 4;  // slices per promotion group (128 K elements TF32, 256 BF16)
+    constexpr uint32_t kFmt = (KIND == kTF32x3) ? 2u : 1u;
+    constexpr uint32_t kIdesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((NB >> 3) << 17) | ((2 * kTile >> 4) << 24);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * P::kStage);
@@ -444,8 +454,10 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
     if (threadIdx.x == 32 * kEpi) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA0)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tB0)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA1)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tB1)) : "memory");
+        if constexpr (KIND == kTF32x3) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tA1)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tB1)) : "memory");
+        }
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -471,7 +483,7 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
     pdl_wait();
     pdl_trigger();
     auto a_tile = [&](int s, int lo) { return smem_u32(smem + s * P::kStage + lo * kPairA); };
-    auto b_tile = [&](int s, int lo) { return smem_u32(smem + s * P::kStage + 2 * kPairA + lo * P::kB); };
+    auto b_tile = [&](int s, int lo) { return smem_u32(smem + s * P::kStage + P::kParts * kPairA + lo * P::kB); };
 
     if (warp == kEpi) {
         if (lane == 0) {  // TMA producer, both CTAs
@@ -489,9 +501,11 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
                 if (rank == 0) mbar_expect_tx(smem_u32(&full[s]), 2 * P::kStage);
                 const int x = (kc0 + kc) * kElems;
                 tma_load_2d_pair(a_tile(s, 0), &tA0, x, arow, even_full);
-                tma_load_2d_pair(a_tile(s, 1), &tA1, x, arow, even_full);
                 tma_load_2d_pair(b_tile(s, 0), &tB0, x, brow, even_full);
-                tma_load_2d_pair(b_tile(s, 1), &tB1, x, brow, even_full);
+                if constexpr (KIND == kTF32x3) {
+                    tma_load_2d_pair(a_tile(s, 1), &tA1, x, arow, even_full);
+                    tma_load_2d_pair(b_tile(s, 1), &tB1, x, brow, even_full);
+                }
                 issued = kc + 1;
             }
             // Bounded drain after an abort: the even CTA's full barrier counts both CTAs' loads.
@@ -513,15 +527,19 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
                     const int s = kc % kStages;
                     if (*abort_flag || !mbar_wait(smem_u32(&full[s]), (kc / kStages) & 1)) { ok = false; break; }
                     fence_after();
-                    const uint64_t a0 = sw_desc<128>(a_tile(s, 0)), a1 = sw_desc<128>(a_tile(s, 1));
-                    const uint64_t b0 = sw_desc<128>(b_tile(s, 0)), b1 = sw_desc<128>(b_tile(s, 1));
+                    const uint64_t a0 = sw_desc<128>(a_tile(s, 0)), b0 = sw_desc<128>(b_tile(s, 0));
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t adv = static_cast<uint64_t>(kk * 2);  // +32 bytes along K
                         const uint32_t acc = (kc != g * kGroup || kk) ? 1u : 0u;
-                        mma_pair(acc_t, a0 + adv, b1 + adv, kIdesc, acc);
-                        mma_pair(acc_t, a1 + adv, b0 + adv, kIdesc, 1u);
-                        mma_pair(acc_t, a0 + adv, b0 + adv, kIdesc, 1u);
+                        if constexpr (KIND == kTF32x3) {
+                            const uint64_t a1 = sw_desc<128>(a_tile(s, 1)), b1 = sw_desc<128>(b_tile(s, 1));
+                            mma_pair<KIND>(acc_t, a0 + adv, b1 + adv, kIdesc, acc);
+                            mma_pair<KIND>(acc_t, a1 + adv, b0 + adv, kIdesc, 1u);
+                            mma_pair<KIND>(acc_t, a0 + adv, b0 + adv, kIdesc, 1u);
+                        } else {
+                            mma_pair<KIND>(acc_t, a0 + adv, b0 + adv, kIdesc, acc);
+                        }
                     }
                     commit_pair(smem_u32(&empty[s]));  // frees stage s in both CTAs
                 }
@@ -635,14 +653,14 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Launches the CTA-pair kernel: clusters of two along x, programmatic
 // serialization as for the single-CTA kernel.
-template <int NB>
+template <int KIND, int NB>
 int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0, const CUtensorMap& b1, int M,
                 int N, int nk, const GemmOut& out, cudaStream_t st) {
-    using P = Pair<NB>;
+    using P = Pair<KIND, NB>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [&] {
-        attr = cudaFuncSetAttribute(gemm_nt_pair_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr = cudaFuncSetAttribute(gemm_nt_pair_kernel<KIND, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(P::kSmem));
     });
     if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute(gemm_nt_pair_kernel)");
@@ -660,7 +678,7 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_nt_pair_kernel<NB>, a0, a1, b0, b1, nk, out);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_nt_pair_kernel<KIND, NB>, a0, a1, b0, b1, nk, out);
     return e == cudaSuccess ? check_launch("gemm_nt_pair_kernel") : cuda_fail(e, "gemm_nt_pair_kernel launch");
 }
 
@@ -688,19 +706,24 @@ int gemm_nt(Kind kind, const Operand& A, const Operand& B, int M, int N, int K, 
     // 128-byte slices: three stages for TF32x3, four for BF16.  (64-byte slices
     // with six stages were measured slower: 176 vs 211 TFLOP/s at 4096^3.)
     const int sw = 128;
-    // Large FP32-accurate products on CTA pairs (256-row tiles).  With a
+    // Large products on CTA pairs (256-row tiles).  With a
     // triangular A the pair runs over the union of its two row tiles' K ranges,
     // one 128-block past the triangle, which the caller keeps zero.
-    if (!bf16 && M % (2 * kTile) == 0 && K >= 512) {
+    if (M % (2 * kTile) == 0 && K >= 512) {
         CUtensorMap pa0{}, pa1{}, pb0{}, pb1{};
-        int rc = make_map(&pa0, A.hi, false, M, K, A.ld, sw);
-        if (!rc) rc = make_map(&pa1, A.lo, false, M, K, A.ld, sw);
         const int nb = (N % 256 == 0) ? 256 : 128;  // 256-wide MMAs where N allows
-        if (!rc) rc = make_map(&pb0, B.hi, false, N, K, B.ld, sw, nb / 2);
-        if (!rc) rc = make_map(&pb1, B.lo, false, N, K, B.ld, sw, nb / 2);
+        int rc = make_map(&pa0, A.hi, bf16, M, K, A.ld, sw);
+        if (!rc) rc = make_map(&pb0, B.hi, bf16, N, K, B.ld, sw, nb / 2);
+        if (!rc && !bf16) rc = make_map(&pa1, A.lo, false, M, K, A.ld, sw);
+        if (!rc && !bf16) rc = make_map(&pb1, B.lo, false, N, K, B.ld, sw, nb / 2);
         if (rc) return rc;
-        return nb == 256 ? launch_pair<256>(pa0, pa1, pb0, pb1, M, N, K / 32, out, stream)
-                         : launch_pair<128>(pa0, pa1, pb0, pb1, M, N, K / 32, out, stream);
+        if (bf16) { pa1 = pa0; pb1 = pb0; }
+        const int nk2 = K / (bf16 ? 64 : 32);
+        if (bf16)
+            return nb == 256 ? launch_pair<kBF16, 256>(pa0, pa1, pb0, pb1, M, N, nk2, out, stream)
+                             : launch_pair<kBF16, 128>(pa0, pa1, pb0, pb1, M, N, nk2, out, stream);
+        return nb == 256 ? launch_pair<kTF32x3, 256>(pa0, pa1, pb0, pb1, M, N, nk2, out, stream)
+                         : launch_pair<kTF32x3, 128>(pa0, pa1, pb0, pb1, M, N, nk2, out, stream);
     }
     int rc = make_map(&a0, A.hi, bf16, M, K, A.ld, sw);
     if (!rc) rc = make_map(&b0, B.hi, bf16, N, K, B.ld, sw);
