@@ -19,6 +19,7 @@ def split(torch, tb, x):
     (128, 128, 32, 1.0, 0.0, 0, "x3"), (256, 384, 96, 1.0, 0.0, 0, "x3"), (1024, 1024, 1024, 1.0, 0.0, 0, "x3"),
     (512, 256, 4096, 1.0, 0.0, 0, "x3"), (384, 384, 256, -1.0, 1.0, 1, "x3"), (2048, 1024, 512, 0.5, 2.0, 0, "x3"),
     (768, 768, 512, -1.0, 1.0, 1, "x3"), (640, 384, 1024, 1.0, 0.0, 0, "x3"), (256, 128, 8192, 1.0, 0.0, 0, "x3"),
+    (512, 384, 512, -1.0, 1.0, 1, "x3"),
     (128, 128, 64, 1.0, 0.0, 0, "bf16"), (1024, 512, 2048, 0.5, 1.0, 0, "bf16"), (768, 768, 128, 1.0, 0.0, 1, "bf16"),
     (768, 768, 1024, 1.0, 0.0, 1, "bf16"), (512, 384, 2048, 1.0, 0.5, 0, "bf16")])
 def test_gemm_nt_matches_float64(cuda, tblib, M, N, K, alpha, beta, lower, kind):
