@@ -358,11 +358,14 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
         }
         __syncthreads();
     }
+    // Write-out: V in FP32 (the final transpose reads it) with its split, and
+    // the split of V^T.  The factor of this block is not written back: after
+    // its diagonal block is factored nothing reads it (the triangular solves
+    // use V_cc, the inverse steps only off-diagonal blocks of L).
 #pragma unroll 2
     for (int e = t; e < kB * kB; e += kBaseThreads) {
         const int i = e >> 7, j = e & 127;
         const size_t g = base + static_cast<size_t>(i) * ld + j;
-        if (j <= i) A[g] = sA[i * kP + j];
         const float v = sV[i * kP + j];
         const float h = tf32_round(v);
         V[g] = v;
@@ -370,18 +373,28 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
         V_lo[g] = v - h;
         const float vt = sVT[i * kP + j];
         const float ht = tf32_round(vt);
-        VT[g] = vt;
         VT_hi[g] = ht;
         VT_lo[g] = vt - ht;
-        // Zero the neighbouring off-diagonal blocks no other step writes: V's block
-        // to the right (above the diagonal) and V^T's block below.  The inverse
-        // steps' CTA-pair products read one 128-block past the triangle there.
-        if (off + kB < ld) {
-            const size_t gr = base + static_cast<size_t>(i) * ld + kB + j;         // V[off+i][off+128+j]
-            const size_t gb = base + static_cast<size_t>(kB + i) * ld + j;         // V^T[off+128+i][off+j]
-            V[gr] = 0.0f; V_hi[gr] = 0.0f; V_lo[gr] = 0.0f;
-            VT[gb] = 0.0f; VT_hi[gb] = 0.0f; VT_lo[gb] = 0.0f;
-        }
+    }
+}
+
+// Zeroes the 128-blocks next to the diagonal that no other step writes: V's
+// block right of each diagonal block and V^T's block below it (with their
+// splits).  The inverse steps' CTA-pair products read one 128-block past the
+// triangle there.  One CTA per (block, row) pair, off the critical path.
+__global__ void __launch_bounds__(256) zero_adjacent_kernel(float* __restrict__ V, float* __restrict__ V_hi,
+                                                            float* __restrict__ V_lo, float* __restrict__ VT_hi,
+                                                            float* __restrict__ VT_lo, int d) {
+    pdl_wait();
+    pdl_trigger();
+    const int blk = blockIdx.y;  // diagonal block index, 0 .. d/128 - 2
+    const size_t off = static_cast<size_t>(blk) * kB;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < kB * kB; e += gridDim.x * blockDim.x) {
+        const int i = e >> 7, j = e & 127;
+        const size_t gr = (off + i) * d + off + kB + j;  // V[off+i][off+128+j]
+        const size_t gb = (off + kB + i) * d + off + j;  // V^T[off+128+i][off+j]
+        V[gr] = 0.0f; V_hi[gr] = 0.0f; V_lo[gr] = 0.0f;
+        VT_hi[gb] = 0.0f; VT_lo[gb] = 0.0f;
     }
 }
 constexpr size_t kBaseSmem = (3 * kB * kP + 3 * 32 * kSP + 32 * 32 + 32 + 4) * sizeof(float);
@@ -422,8 +435,8 @@ __global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, flo
 // of the later groups.  Errors go to E (row pitch ldE) at the block's own
 // columns, with their tf32 split.
 constexpr int kU1 = kB + 1;  // pitch of the in-block copy of U
-constexpr int kIbThreads = 512;
-constexpr int kIbRows = 2 * (kIbThreads / 32);
+constexpr int kIbThreads = 448;                     // 14 warps, two rows each: 28 rows per CTA,
+constexpr int kIbRows = 2 * (kIbThreads / 32);      // so 4096 rows fill all 148 SMs
 constexpr size_t kIbSmem = (kB * kU1 + kB) * sizeof(float);
 
 __device__ __forceinline__ uint32_t obs_keep_bits(const float (&w)[4], const float* rv, int n_keep) {
@@ -462,7 +475,7 @@ __device__ __forceinline__ void obs_group_solve(float (&w)[4], float (&e)[4], ui
     }
 }
 
-__global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, int d, int i1,
+__global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, int r, int d, int i1,
                                                              const float* __restrict__ Ut, int n_keep,
                                                              uint8_t* __restrict__ mask, float* __restrict__ E_hi,
                                                              float* __restrict__ E_lo, long long ldE) {
@@ -476,12 +489,12 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
             const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
-            v[u] = (j >= q) ? Ut[static_cast<size_t>(i1 + j) * d + i1 + q] : 0.0f;
+            v[u] = (e < kB * kB && j >= q) ? Ut[static_cast<size_t>(i1 + j) * d + i1 + q] : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
             const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
-            u1[q * kU1 + (j & 3) * 32 + (j >> 2)] = v[u];
+            if (e < kB * kB) u1[q * kU1 + (j & 3) * 32 + (j >> 2)] = v[u];
         }
     }
     __syncthreads();
@@ -492,6 +505,7 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t row0 = static_cast<size_t>(blockIdx.x) * kIbRows + 2 * warp;
+    if (row0 >= static_cast<size_t>(r)) return;  // r is even: both rows of the warp exist
     float* wr0 = W + row0 * d + i1;
     float* wr1 = wr0 + d;
     float w0[4], w1[4];
@@ -691,7 +705,8 @@ struct Sweep {
 int sweep(const Sweep& s, int a, int n, cudaStream_t st) {
     const long long d = s.d;
     if (n == kB) {
-        const cudaError_t e = launch_pdl(inblock_kernel, dim3(s.r / kIbRows), dim3(kIbThreads), kIbSmem, st, s.W, s.d,
+        const cudaError_t e = launch_pdl(inblock_kernel, dim3((s.r + kIbRows - 1) / kIbRows), dim3(kIbThreads), kIbSmem,
+                                         st, s.W, s.r, s.d,
                                          a, s.Ut, s.n_keep, s.mask, s.E_hi, s.E_lo, d);
         return e == cudaSuccess ? check_launch("inblock_kernel") : cuda_fail(e, "inblock_kernel launch");
     }
@@ -846,6 +861,11 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
         e = launch_pdl(reverse_damp_kernel, dim3(d / 32, d / 32), dim3(32, 8), 0, st, H, d,
                        static_cast<const double*>(dsum), damp_frac, w.A, w.A_hi, w.A_lo);
     rc = e == cudaSuccess ? check_launch("hessian prep") : cuda_fail(e, "hessian prep launch");
+    if (!rc && d > kB) {  // on the side stream, ahead of every inverse step there
+        e = launch_pdl(zero_adjacent_kernel, dim3(16, d / kB - 1), dim3(256), 0, w.side, w.V, w.V_hi, w.V_lo,
+                       w.VT_hi, w.VT_lo, d);
+        rc = e == cudaSuccess ? check_launch("zero_adjacent_kernel") : cuda_fail(e, "zero_adjacent_kernel launch");
+    }
     if (!rc) rc = chol(w, 0, d, st);
     // join: the inverse steps on the side stream finish before anything reads V
     e = cudaEventRecord(wsp.join, w.side);
