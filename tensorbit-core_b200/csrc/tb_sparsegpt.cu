@@ -568,12 +568,25 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
     reinterpret_cast<float4*>(E_lo + (row0 + 1) * ldE + i1)[lane] = l;
 }
 
+constexpr int kMaxDepth = 16;
+constexpr int kLookAhead = 1024;  // split the Schur update of nodes whose A22 is at least this wide
+
 struct Work {
     float *A, *A_hi, *A_lo, *V, *V_hi, *V_lo, *VT, *VT_hi, *VT_lo, *T_hi, *T_lo;
     int d;
     int* bad;
     cudaStream_t side;  // stream of the triangular-inverse steps
     cudaEvent_t ev;     // "this node's factor is complete", re-recorded per node
+    cudaStream_t ahead;              // stream of the look-ahead Schur updates
+    cudaEvent_t evl;                 // "this node's L21 is complete"
+    cudaEvent_t ev21[kMaxDepth], ev22[kMaxDepth];  // look-ahead updates done, per recursion depth
+};
+
+// Regions of a node's matrix that its parent's look-ahead update is still
+// writing on the look-ahead stream: rows n1.. x cols ..n1 (ev21) and rows
+// n1.. x cols n1.. (ev22), n1 = half_blocks(n); null when already complete.
+struct Pending {
+    cudaEvent_t ev21 = nullptr, ev22 = nullptr;
 };
 
 int gemm(const float* ah, const float* al, long long lda, const float* bh, const float* bl, long long ldb, int M, int N,
@@ -591,9 +604,9 @@ int trsm(Work& w, long long r0, int m, long long c0, int n, cudaStream_t st) {
     const long long d = w.d;
     auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
     int rc;
-    if (n == kB) {  // B <- B V_cc^T, in place (one 128-column output tile per row block)
+    if (n == kB) {  // B <- B V_cc^T, in place; only the split is read later (solved blocks
+                    // are operands from then on, never a Cin)
         umma::GemmOut o{};
-        o.C = at(w.A, r0, c0); o.ldc = d;
         o.C_hi = at(w.A_hi, r0, c0); o.C_lo = at(w.A_lo, r0, c0); o.ld_split = d;
         o.alpha = 1.0f; o.beta = 0.0f;
         return gemm(at(w.A_hi, r0, c0), at(w.A_lo, r0, c0), d, at(w.V_hi, c0, c0), at(w.V_lo, c0, c0), d, m, kB, kB,
@@ -616,41 +629,71 @@ int trsm(Work& w, long long r0, int m, long long c0, int n, cudaStream_t st) {
 
 int trtri_node(Work& w, int off, int n, cudaStream_t st);
 
-// Recursive Cholesky of A[off : off+n] (lower, in place, with split); the
-// 128 x 128 diagonal blocks also get their inverses in V / VT.  Once a node's
-// factor is enqueued on st, its inverse step goes to w.side behind an event:
-// the inverse of finished sub-blocks then runs beside the rest of the
-// factorisation, whose chain of small dependent launches leaves most SMs idle.
-// Inverse steps only touch V's off-diagonal blocks and T, which the factor
-// side never reads, and on w.side they keep the recursion's order (both
-// halves of a node before the node).
-int chol(Work& w, int off, int n, cudaStream_t st) {
+// Schur update A[r0.., c0..] -= L[r0.., lc..] L[c0.., lc..]^T over an (m x nn)
+// region with inner size k, with split; lower_only for diagonal regions.
+int schur(Work& w, long long r0, long long c0, int m, int nn, long long lc, int k, int lower, cudaStream_t st) {
     const long long d = w.d;
+    auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
+    umma::GemmOut o{};
+    o.C = at(w.A, r0, c0); o.ldc = d;
+    o.Cin = at(w.A, r0, c0); o.ldcin = d;
+    o.C_hi = at(w.A_hi, r0, c0); o.C_lo = at(w.A_lo, r0, c0); o.ld_split = d;
+    o.alpha = -1.0f; o.beta = 1.0f; o.lower_only = lower;
+    return gemm(at(w.A_hi, r0, lc), at(w.A_lo, r0, lc), d, at(w.A_hi, c0, lc), at(w.A_lo, c0, lc), d, m, nn, k, o, st);
+}
+
+int wait_on(cudaStream_t st, cudaEvent_t ev) {
+    if (!ev) return TB_OK;
+    const cudaError_t e = cudaStreamWaitEvent(st, ev, 0);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "tb_obs_sparsegpt stream wait");
+}
+int record_on(cudaEvent_t ev, cudaStream_t st) {
+    const cudaError_t e = cudaEventRecord(ev, st);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "tb_obs_sparsegpt event record");
+}
+
+// Recursive Cholesky of A[off : off+n] (lower, in place, with split); the
+// 128 x 128 diagonal blocks also get their inverses in V / VT.
+//  * Inverse steps: once a node's factor is enqueued on st, its inverse step
+//    goes to w.side behind an event, beside the rest of the factorisation,
+//    whose chain of small dependent launches leaves most SMs idle.  Inverse
+//    steps only touch V's off-diagonal blocks and T, which the factor side
+//    never reads, and on w.side they keep the recursion's order.
+//  * Look-ahead: of the Schur update A22 -= L21 L21^T only the top-left
+//    triangle (what the child factors first) runs on st; the lower-left block
+//    and the lower-right triangle go to w.ahead, and the child waits for them
+//    just before its own solve and update touch those regions.
+int chol(Work& w, int off, int n, cudaStream_t st, int depth, Pending pend) {
     if (n == kB) {
         const cudaError_t e = launch_pdl(base_chol_inv_kernel, dim3(1), dim3(kBaseThreads), kBaseSmem, st, w.A, w.V,
                                          w.V_hi, w.V_lo, w.VT, w.VT_hi, w.VT_lo, w.d, off, w.bad);
         return e == cudaSuccess ? check_launch("base_chol_inv_kernel") : cuda_fail(e, "base_chol_inv_kernel launch");
     }
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
-    int rc = chol(w, off, n1, st);
-    if (rc) return rc;
     const long long o1 = off + n1;
-    if ((rc = trsm(w, o1, n2, off, n1, st))) return rc;  // L21 = A21 L11^-T
-    auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
-    {  // A22 -= L21 L21^T on the lower tiles, with split
-        umma::GemmOut o{};
-        o.C = at(w.A, o1, o1); o.ldc = d;
-        o.Cin = at(w.A, o1, o1); o.ldcin = d;
-        o.C_hi = at(w.A_hi, o1, o1); o.C_lo = at(w.A_lo, o1, o1); o.ld_split = d;
-        o.alpha = -1.0f; o.beta = 1.0f; o.lower_only = 1;
-        if ((rc = gemm(at(w.A_hi, o1, off), at(w.A_lo, o1, off), d, at(w.A_hi, o1, off), at(w.A_lo, o1, off), d, n2,
-                       n2, n1, o, st)))
-            return rc;
+    int rc = chol(w, off, n1, st, depth + 1, Pending{});
+    if (!rc) rc = wait_on(st, pend.ev21);                 // A21 fully updated by the parent
+    if (!rc) rc = trsm(w, o1, n2, off, n1, st);          // L21 = A21 L11^-T
+    if (!rc) rc = wait_on(st, pend.ev22);                 // A22 fully updated by the parent
+    if (rc) return rc;
+    Pending child{};
+    if (n2 >= kLookAhead && depth < kMaxDepth) {
+        const int h1 = static_cast<int>(half_blocks(n2)), h2 = n2 - h1;
+        if ((rc = record_on(w.evl, st))) return rc;
+        if ((rc = wait_on(w.ahead, w.evl))) return rc;
+        if ((rc = schur(w, o1 + h1, o1, h2, h1, off, n1, 0, w.ahead))) return rc;        // lower-left block
+        if ((rc = record_on(w.ev21[depth], w.ahead))) return rc;
+        if ((rc = schur(w, o1 + h1, o1 + h1, h2, h2, off, n1, 1, w.ahead))) return rc;   // lower-right triangle
+        if ((rc = record_on(w.ev22[depth], w.ahead))) return rc;
+        if ((rc = schur(w, o1, o1, h1, h1, off, n1, 1, st))) return rc;                 // top-left triangle
+        child.ev21 = w.ev21[depth];
+        child.ev22 = w.ev22[depth];
+    } else if ((rc = schur(w, o1, o1, n2, n2, off, n1, 1, st))) {
+        return rc;
     }
-    if ((rc = chol(w, off + n1, n2, st))) return rc;
-    cudaError_t e = cudaEventRecord(w.ev, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(w.side, w.ev, 0);
-    if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt stream fork");
+    if ((rc = chol(w, off + n1, n2, st, depth + 1, child))) return rc;
+    if ((rc = record_on(w.ev, st))) return rc;
+    if ((rc = wait_on(w.side, w.ev))) return rc;
     return trtri_node(w, off, n, w.side);
 }
 
@@ -756,8 +799,9 @@ struct Workspace {
     int dev = -1;
     float* ptr = nullptr;
     size_t floats = 0;
-    cudaStream_t side = nullptr;
-    cudaEvent_t ev = nullptr, join = nullptr;
+    cudaStream_t side = nullptr, ahead = nullptr;
+    cudaEvent_t ev = nullptr, join = nullptr, evl = nullptr, join_ahead = nullptr;
+    cudaEvent_t ev21[kMaxDepth] = {}, ev22[kMaxDepth] = {};
 };
 std::mutex g_ws_mu;
 std::vector<Workspace> g_ws;
@@ -776,8 +820,14 @@ int workspace(size_t floats, Workspace* out) {
         Workspace x;
         x.dev = dev;
         e = cudaStreamCreateWithFlags(&x.side, cudaStreamNonBlocking);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.ev, cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&x.ahead, cudaStreamNonBlocking);
+        cudaEvent_t* evs[] = {&x.ev, &x.join, &x.evl, &x.join_ahead};
+        for (cudaEvent_t* p : evs)
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(p, cudaEventDisableTiming);
+        for (int k = 0; k < kMaxDepth && e == cudaSuccess; ++k) {
+            e = cudaEventCreateWithFlags(&x.ev21[k], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.ev22[k], cudaEventDisableTiming);
+        }
         if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt stream/event setup");
         g_ws.push_back(x);
         w = &g_ws.back();
@@ -842,6 +892,12 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     w.d = d;
     w.side = wsp.side;
     w.ev = wsp.ev;
+    w.ahead = wsp.ahead;
+    w.evl = wsp.evl;
+    for (int k = 0; k < kMaxDepth; ++k) {
+        w.ev21[k] = wsp.ev21[k];
+        w.ev22[k] = wsp.ev22[k];
+    }
     w.A = ws; w.A_hi = ws + dd; w.A_lo = ws + 2 * dd;
     w.V = ws + 3 * dd; w.V_hi = ws + 4 * dd; w.V_lo = ws + 5 * dd;
     w.VT = ws + 6 * dd; w.VT_hi = ws + 7 * dd; w.VT_lo = ws + 8 * dd;
@@ -866,10 +922,13 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
                        w.VT_hi, w.VT_lo, d);
         rc = e == cudaSuccess ? check_launch("zero_adjacent_kernel") : cuda_fail(e, "zero_adjacent_kernel launch");
     }
-    if (!rc) rc = chol(w, 0, d, st);
-    // join: the inverse steps on the side stream finish before anything reads V
+    if (!rc) rc = chol(w, 0, d, st, 0, Pending{});
+    // join: the inverse steps (side) and look-ahead updates (ahead) finish
+    // before anything reads V or the next call reuses the workspace
     e = cudaEventRecord(wsp.join, w.side);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.join, 0);
+    if (e == cudaSuccess) e = cudaEventRecord(wsp.join_ahead, w.ahead);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.join_ahead, 0);
     if (e != cudaSuccess && !rc) rc = cuda_fail(e, "tb_obs_sparsegpt stream join");
     // Ut (lower) = (P V P)^T into A's buffers (A is no longer needed).
     float *Ut = w.A, *Ut_hi = w.A_hi, *Ut_lo = w.A_lo;
