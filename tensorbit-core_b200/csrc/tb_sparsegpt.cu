@@ -736,6 +736,9 @@ struct Sweep {
     const float *Ut, *Ut_hi, *Ut_lo;
     uint8_t* mask;
     float *E_hi, *E_lo;  // r x d, pitch d
+    cudaStream_t ahead;              // look-ahead updates
+    cudaEvent_t evl;                 // "the left half's errors are complete"
+    const cudaEvent_t* ev;           // [kMaxDepth] look-ahead update done, per depth
 };
 
 // Column sweep of [a, a+n): recursive on the columns, like the triangular
@@ -745,7 +748,21 @@ struct Sweep {
 // therefore sees all earlier errors before its own sweep, as in the
 // block-by-block lazy update, but W is read and written once per level
 // instead of once per block, and the products have K up to d/2.
-int sweep(const Sweep& s, int a, int n, cudaStream_t st) {
+// W[:, a+c0 : a+c0+nc] -= E[:, a : a+k] U[a : a+k, a+c0 : ...] (the errors of
+// columns [a, a+k) applied to nc later columns starting c0 after a).
+int sweep_update(const Sweep& s, int a, int k, int c0, int nc, cudaStream_t st) {
+    const long long d = s.d;
+    umma::GemmOut o{};
+    o.C = s.W + a + c0; o.ldc = d;
+    o.Cin = s.W + a + c0; o.ldcin = d;
+    o.alpha = -1.0f; o.beta = 1.0f;
+    return umma::gemm_nt(umma::kTF32x3, {s.E_hi + a, s.E_lo + a, d},
+                         {s.Ut_hi + (a + c0) * d + a, s.Ut_lo + (a + c0) * d + a, d}, s.r, nc, k, o, st);
+}
+
+// pend: the parent's look-ahead update of this range's right half (columns
+// a + half_blocks(n) ..) is still running on s.ahead; null when complete.
+int sweep(const Sweep& s, int a, int n, cudaStream_t st, int depth, cudaEvent_t pend) {
     const long long d = s.d;
     if (n == kB) {
         const cudaError_t e = launch_pdl(inblock_kernel, dim3((s.r + kIbRows - 1) / kIbRows), dim3(kIbThreads), kIbSmem,
@@ -754,16 +771,23 @@ int sweep(const Sweep& s, int a, int n, cudaStream_t st) {
         return e == cudaSuccess ? check_launch("inblock_kernel") : cuda_fail(e, "inblock_kernel launch");
     }
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
-    int rc = sweep(s, a, n1, st);
+    int rc = sweep(s, a, n1, st, depth + 1, nullptr);
+    if (!rc) rc = wait_on(st, pend);  // the right half has all earlier errors applied
     if (rc) return rc;
-    umma::GemmOut o{};
-    o.C = s.W + a + n1; o.ldc = d;
-    o.Cin = s.W + a + n1; o.ldcin = d;
-    o.alpha = -1.0f; o.beta = 1.0f;
-    if ((rc = umma::gemm_nt(umma::kTF32x3, {s.E_hi + a, s.E_lo + a, d},
-                            {s.Ut_hi + (a + n1) * d + a, s.Ut_lo + (a + n1) * d + a, d}, s.r, n2, n1, o, st)))
-        return rc;
-    return sweep(s, a + n1, n2, st);
+    if (n2 >= kLookAhead && depth < kMaxDepth) {
+        // Look-ahead: the part of the right half that the child sweeps first is
+        // updated on st, the rest on s.ahead (ordered after the parent's piece
+        // there), and the child waits for it before its own update of it.
+        const int h1 = static_cast<int>(half_blocks(n2));
+        if ((rc = record_on(s.evl, st))) return rc;
+        if ((rc = wait_on(s.ahead, s.evl))) return rc;
+        if ((rc = sweep_update(s, a, n1, n1 + h1, n2 - h1, s.ahead))) return rc;
+        if ((rc = record_on(s.ev[depth], s.ahead))) return rc;
+        if ((rc = sweep_update(s, a, n1, n1, h1, st))) return rc;
+        return sweep(s, a + n1, n2, st, depth + 1, s.ev[depth]);
+    }
+    if ((rc = sweep_update(s, a, n1, n1, n2, st))) return rc;
+    return sweep(s, a + n1, n2, st, depth + 1, nullptr);
 }
 
 }  // namespace
@@ -937,7 +961,13 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
                        static_cast<const float*>(w.V), d, Ut, Ut_hi, Ut_lo);
         rc = e == cudaSuccess ? check_launch("reverse_transpose_kernel") : cuda_fail(e, "reverse_transpose launch");
     }
-    if (!rc) rc = sweep(Sweep{W, r, d, n_keep, Ut, Ut_hi, Ut_lo, mask, E_hi, E_lo}, 0, d, st);
+    if (!rc) rc = sweep(Sweep{W, r, d, n_keep, Ut, Ut_hi, Ut_lo, mask, E_hi, E_lo, w.ahead, w.evl, w.ev21}, 0, d, st, 0,
+                        nullptr);
+    if (!rc) {  // the look-ahead updates are all consumed by later steps; join anyway
+        e = cudaEventRecord(wsp.join_ahead, w.ahead);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.join_ahead, 0);
+        if (e != cudaSuccess) rc = cuda_fail(e, "tb_obs_sparsegpt stream join");
+    }
     int bad = 0;
     if (!rc && ut_out) {
         e = cudaMemcpyAsync(ut_out, Ut, dd * sizeof(float), cudaMemcpyDeviceToDevice, st);
