@@ -165,9 +165,12 @@ int tb_block_obs(float* weights, const float* fisher, const float* const* hist, 
 int tb_split_tf32(const float* x, float* hi, float* lo, size_t n, void* stream);
 /* C[M,N] = alpha * A[M,K] * B[N,K]^T + beta * Cin, A and B row-major FP32 given
  * as hi/lo pairs (tb_split_tf32); products hi*hi + hi*lo + lo*hi on TF32 tensor
- * cores with FP32 accumulation in tensor memory.  M, N multiples of 128, K of 32;
- * 16-byte aligned operands with ld*4 % 16 == 0.  lower_only computes only the
- * 128x128 tiles on or below the diagonal. */
+ * cores, accumulated in tensor memory in groups of 128 K and summed in FP32
+ * registers (round to nearest).  M, N multiples of 128, K of 32; 16-byte
+ * aligned operands with ld*4 % 16 == 0.  lower_only writes only the 128x128
+ * tiles on or below the diagonal.  M % 256 == 0 and K >= 512 run on CTA pairs
+ * (tcgen05 cta_group::2, 256x256 tiles where N % 256 == 0), the rest on
+ * single CTAs (128x128 tiles). */
 int tb_gemm_nt_tf32x3(const float* a_hi, const float* a_lo, long long lda, const float* b_hi,
                       const float* b_lo, long long ldb, int M, int N, int K, float alpha, float beta,
                       const float* c_in, long long ldcin, float* c, long long ldc, int lower_only,
@@ -204,8 +207,11 @@ int tb_obs_hessian_scaled(const void* xt_bf16, int d, int n, float scale, float*
  * r*d/4 bytes (bit k = keep column 4g+k, the .tb convention).  ut_out (d x d,
  * may be NULL) receives U^T.  A workspace of 9.5 d^2 + 2 r d floats is
  * allocated on first use and kept per device for later calls (grow-only;
- * ~8.3 GB at d = 14336, r = 4096).  Synchronises the stream.  TB_ERR_CONFIG
- * if H + lambda I is not positive definite in FP32. */
+ * ~8.3 GB at d = 14336, r = 4096), so calls on one device must not overlap;
+ * two internal streams per device carry the parts of the factorisation and
+ * the sweep that run beside the caller's stream.  Synchronises the stream.
+ * TB_ERR_CONFIG if H + lambda I is not positive definite in FP32;
+ * TB_ERR_TIMEOUT if an internal bounded wait expired. */
 int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float damp_frac, int n_keep, int m,
                      uint8_t* mask, float* ut_out, void* stream);
 
