@@ -122,22 +122,41 @@ __device__ __forceinline__ float tf32_hi(float x) {
 constexpr int kThreadsGemm = 192;
 constexpr int kStagePitch = kTile + 4;  // epilogue staging pitch (floats): float4 rows without bank conflicts
 
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
 // Epilogue of one warp: acc holds row `row0 + lane` of a 128-column output
 // tile starting at column col0.  The 32 x 128 block is staged in shared memory
 // (sbuf, pitch kStagePitch) and handled one output row per step with lane l on
 // columns 4l..4l+3, so every global load and store is a coalesced 512-byte row.
-__device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc)[kTile], float* sbuf,
+// With cbuf (a second staging block), the warp's 32 Cin rows are fetched with
+// asynchronous copies while the accumulator is staged, one round trip in all;
+// without it they are loaded in batches of 8 rows.
+__device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc)[kTile], float* sbuf, float* cbuf,
                                            long long row0, long long col0, int lane) {
+    const long long gcol = col0 + 4 * lane;
+    const bool prefetch = cbuf != nullptr && out.beta != 0.0f;
+    if (prefetch) {
+#pragma unroll 8
+        for (int rr = 0; rr < 32; ++rr)
+            cp_async16(cbuf + rr * kStagePitch + 4 * lane, out.Cin + (row0 + rr) * out.ldcin + gcol);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
 #pragma unroll
     for (int c = 0; c < kTile / 4; ++c)
         *reinterpret_cast<float4*>(sbuf + lane * kStagePitch + 4 * c) =
             make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+    if (prefetch) asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncwarp();
-    const long long gcol = col0 + 4 * lane;
     constexpr int kBatch = 8;  // rows whose Cin loads are in flight together
     for (int rb = 0; rb < 32; rb += kBatch) {
         float4 cin[kBatch];
-        if (out.beta != 0.0f) {
+        if (prefetch) {
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u)
+                cin[u] = *reinterpret_cast<const float4*>(cbuf + (rb + u) * kStagePitch + 4 * lane);
+        } else if (out.beta != 0.0f) {
 #pragma unroll
             for (int u = 0; u < kBatch; ++u)
                 cin[u] = *reinterpret_cast<const float4*>(out.Cin + (row0 + rb + u) * out.ldcin + gcol);
@@ -343,7 +362,10 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
         } else {
             // All MMAs have completed, so the operand ring is free for staging.
             static_assert(4 * 32 * kStagePitch * 4 <= STAGES * kOps * kTileBytes, "epilogue staging exceeds the ring");
-            store_rows(out, acc, reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch,
+            // a second staging block for the Cin prefetch where the ring has room (3xTF32)
+            constexpr bool kCinBuf = 8 * 32 * kStagePitch * 4 <= STAGES * kOps * kTileBytes;
+            float* sb = reinterpret_cast<float*>(smem);
+            store_rows(out, acc, sb + warp * 32 * kStagePitch, kCinBuf ? sb + (4 + warp) * 32 * kStagePitch : nullptr,
                        static_cast<long long>(tm) * kTile + warp * 32, static_cast<long long>(tn) * kTile, lane);
         }
     }
@@ -585,7 +607,7 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
             if (lane == 0) atomicExch(&g_umma_error, 1);
         } else if (!(out.lower_only && sub_col > sub_row)) {
             static_assert(kEpi * 32 * kStagePitch * 4 <= kStages * P::kStage, "epilogue staging exceeds the ring");
-            store_rows(out, acc, reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch,
+            store_rows(out, acc, reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch, nullptr,
                        static_cast<long long>(sub_row) * kTile + quad * 32, static_cast<long long>(sub_col) * kTile,
                        lane);
         }
