@@ -572,7 +572,8 @@ constexpr int kMaxDepth = 16;
 constexpr int kLookAhead = 1024;  // split the Schur update of nodes whose A22 is at least this wide
 
 struct Work {
-    float *A, *A_hi, *A_lo, *V, *V_hi, *V_lo, *VT, *VT_hi, *VT_lo, *T_hi, *T_lo;
+    float *A, *A_hi, *A_lo, *V, *V_hi, *V_lo, *VT, *VT_hi, *VT_lo;
+    float *T_hi[kMaxDepth], *T_lo[kMaxDepth];  // the inverse step's temporary, one per recursion depth
     int d;
     int* bad;
     cudaStream_t side;  // stream of the triangular-inverse steps
@@ -627,7 +628,8 @@ int trsm(Work& w, long long r0, int m, long long c0, int n, cudaStream_t st) {
     return trsm(w, r0, m, c0 + n1, n2, st);
 }
 
-int trtri_node(Work& w, int off, int n, cudaStream_t st);
+int trtri_t(Work& w, int off, int n, int depth, cudaStream_t st);
+int trtri_v(Work& w, int off, int n, int depth, cudaStream_t st);
 
 // Schur update A[r0.., c0..] -= L[r0.., lc..] L[c0.., lc..]^T over an (m x nn)
 // region with inner size k, with split; lower_only for diagonal regions.
@@ -674,6 +676,9 @@ int chol(Work& w, int off, int n, cudaStream_t st, int depth, Pending pend) {
     int rc = chol(w, off, n1, st, depth + 1, Pending{});
     if (!rc) rc = wait_on(st, pend.ev21);                 // A21 fully updated by the parent
     if (!rc) rc = trsm(w, o1, n2, off, n1, st);          // L21 = A21 L11^-T
+    if (!rc) rc = record_on(w.ev, st);                    // L21 and V11 exist: T on the side stream
+    if (!rc) rc = wait_on(w.side, w.ev);
+    if (!rc) rc = trtri_t(w, off, n, depth, w.side);
     if (!rc) rc = wait_on(st, pend.ev22);                 // A22 fully updated by the parent
     if (rc) return rc;
     Pending child{};
@@ -694,40 +699,52 @@ int chol(Work& w, int off, int n, cudaStream_t st, int depth, Pending pend) {
     if ((rc = chol(w, off + n1, n2, st, depth + 1, child))) return rc;
     if ((rc = record_on(w.ev, st))) return rc;
     if ((rc = wait_on(w.side, w.ev))) return rc;
-    return trtri_node(w, off, n, w.side);
+    return trtri_v(w, off, n, depth, w.side);
 }
 
-// Node step of the triangular inverse V = L^-1 for the node [off, off+n) once
-// V11 and V22 are complete (the diagonal 128-blocks come from the base kernel):
-// V21 = -V22 (L21 V11), with V^T kept alongside.  Both products take a
-// triangular left operand, so each output tile row runs only over the K tiles
-// inside the triangle (half the dense work); tiles outside it are never read
-// and need not be zero.
-int trtri_node(Work& w, int off, int n, cudaStream_t st) {
+// Node steps of the triangular inverse V = L^-1 for the node [off, off+n):
+// V21 = -V22 (L21 V11), with V^T kept alongside.  trtri_t forms
+// T^T = V11^T L21^T as soon as L21 and V11 exist (long before the node's
+// lower half is factored); trtri_v then forms V21 = -V22 T once V22 exists.
+// T lives in a buffer of the node's recursion depth: between the two steps
+// only deeper nodes run theirs.  Both products take a triangular left operand,
+// so each output tile row runs only over the K tiles inside the triangle.
+int trtri_t(Work& w, int off, int n, int depth, cudaStream_t st) {
     const long long d = w.d;
     auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
     const long long o1 = off + n1;
-    int rc;
-    {  // T^T = V11^T L21^T  (n1 x n2), split only
-        umma::GemmOut o{};
-        o.C_hi = w.T_hi; o.C_lo = w.T_lo; o.ld_split = n2;
-        o.alpha = 1.0f; o.beta = 0.0f;
-        o.tri_a = 1;  // V11^T upper
-        if ((rc = gemm(at(w.VT_hi, off, off), at(w.VT_lo, off, off), d, at(w.A_hi, o1, off), at(w.A_lo, o1, off), d,
-                       n1, n2, n1, o, st)))
-            return rc;
-    }
-    {  // V21 = -V22 T, with split, and V21^T into VT12
-        umma::GemmOut o{};
-        o.C = at(w.V, o1, off); o.ldc = d;
-        o.C_hi = at(w.V_hi, o1, off); o.C_lo = at(w.V_lo, o1, off); o.ld_split = d;
-        o.Ct = at(w.VT, off, o1); o.ldct = d;
-        o.alpha = -1.0f; o.beta = 0.0f;
-        o.tri_a = 2;  // V22 lower
-        if ((rc = gemm(at(w.V_hi, o1, o1), at(w.V_lo, o1, o1), d, w.T_hi, w.T_lo, n2, n2, n1, n2, o, st))) return rc;
-    }
+    umma::GemmOut o{};
+    o.C_hi = w.T_hi[depth]; o.C_lo = w.T_lo[depth]; o.ld_split = n2;
+    o.alpha = 1.0f; o.beta = 0.0f;
+    o.tri_a = 1;  // V11^T upper
+    return gemm(at(w.VT_hi, off, off), at(w.VT_lo, off, off), d, at(w.A_hi, o1, off), at(w.A_lo, o1, off), d, n1, n2,
+                n1, o, st);
+}
+
+int trtri_v(Work& w, int off, int n, int depth, cudaStream_t st) {
+    const long long d = w.d;
+    auto at = [&](float* p, long long r, long long c) { return p + r * d + c; };
+    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
+    const long long o1 = off + n1;
+    umma::GemmOut o{};
+    o.C = at(w.V, o1, off); o.ldc = d;
+    o.C_hi = at(w.V_hi, o1, off); o.C_lo = at(w.V_lo, o1, off); o.ld_split = d;
+    o.Ct = at(w.VT, off, o1); o.ldct = d;
+    o.alpha = -1.0f; o.beta = 0.0f;
+    o.tri_a = 2;  // V22 lower
+    int rc = gemm(at(w.V_hi, o1, o1), at(w.V_lo, o1, o1), d, w.T_hi[depth], w.T_lo[depth], n2, n2, n1, n2, o, st);
+    if (rc) return rc;
     return tb_split_tf32_2d(at(w.VT, off, o1), at(w.VT_hi, off, o1), at(w.VT_lo, off, o1), n1, n2, d, st);
+}
+
+// Largest n1 x n2 of the inverse steps at each recursion depth (T's size).
+void trtri_sizes(int n, int depth, size_t* need) {
+    if (n == kB || depth >= kMaxDepth) return;
+    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
+    need[depth] = std::max(need[depth], static_cast<size_t>(n1) * n2);
+    trtri_sizes(n1, depth + 1, need);
+    trtri_sizes(n2, depth + 1, need);
 }
 
 struct Sweep {
@@ -823,8 +840,8 @@ struct Workspace {
     int dev = -1;
     float* ptr = nullptr;
     size_t floats = 0;
-    cudaStream_t side = nullptr, ahead = nullptr;
-    cudaEvent_t ev = nullptr, join = nullptr, evl = nullptr, join_ahead = nullptr;
+    cudaStream_t side = nullptr, ahead = nullptr, chain = nullptr;
+    cudaEvent_t ev = nullptr, join = nullptr, evl = nullptr, join_ahead = nullptr, fork = nullptr, done = nullptr;
     cudaEvent_t ev21[kMaxDepth] = {}, ev22[kMaxDepth] = {};
 };
 std::mutex g_ws_mu;
@@ -843,9 +860,15 @@ int workspace(size_t floats, Workspace* out) {
     if (!w) {
         Workspace x;
         x.dev = dev;
-        e = cudaStreamCreateWithFlags(&x.side, cudaStreamNonBlocking);
-        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&x.ahead, cudaStreamNonBlocking);
-        cudaEvent_t* evs[] = {&x.ev, &x.join, &x.evl, &x.join_ahead};
+        // The chain of dependent steps runs on a high-priority stream; the
+        // inverse steps and look-ahead updates beside it on low-priority ones,
+        // so freed SMs go to the chain first.
+        int least = 0, greatest = 0;
+        e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&x.chain, cudaStreamNonBlocking, greatest);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&x.side, cudaStreamNonBlocking, least);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&x.ahead, cudaStreamNonBlocking, least);
+        cudaEvent_t* evs[] = {&x.ev, &x.join, &x.evl, &x.join_ahead, &x.fork, &x.done};
         for (cudaEvent_t* p : evs)
             if (e == cudaSuccess) e = cudaEventCreateWithFlags(p, cudaEventDisableTiming);
         for (int k = 0; k < kMaxDepth && e == cudaSuccess; ++k) {
@@ -897,21 +920,32 @@ extern "C" int tb_obs_hessian_scaled(const void* xt, int d, int n, float scale, 
 extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float damp_frac, int n_keep, int m,
                                 uint8_t* mask, float* ut_out, void* stream) {
     if (r <= 0 || d <= 0 || r % kB || d % kB) return fail(TB_ERR_SHAPE, "tb_obs_sparsegpt: r and d must be multiples of 128");
+    if (d > (1 << 20)) return fail(TB_ERR_SHAPE, "tb_obs_sparsegpt: d above 2^20 (recursion depth)");
     if (m != 4 || n_keep <= 0 || n_keep >= m) return fail(TB_ERR_UNSUPPORTED, "tb_obs_sparsegpt: N:4 patterns only (N in 1..3)");
     if (!W || !H || !mask) return fail(TB_ERR_ARG, "tb_obs_sparsegpt: null pointer");
     int rc = require_device(nullptr);
     if (rc) return rc;
-    auto st = static_cast<cudaStream_t>(stream);
+    const auto user = static_cast<cudaStream_t>(stream);
     const size_t dd = static_cast<size_t>(d) * d;
     const size_t rd = static_cast<size_t>(r) * d;
     // Workspace: 9 d x d FP32 matrices (A, V, V^T with their splits), the
-    // trtri temporary T (at most d^2 / 4, with split), the error matrix E
-    // (r x d, with split) and two scalars.
+    // inverse steps' temporaries T (one per recursion depth, with split;
+    // about d^2/3 in all), the error matrix E (r x d, with split) and two scalars.
+    size_t tneed[kMaxDepth] = {};
+    trtri_sizes(d, 0, tneed);
+    size_t tsum = 0;
+    for (size_t x : tneed) tsum += (x + 63) / 64 * 64;  // keep each buffer 256-byte aligned
     Workspace wsp;
-    const size_t ws_floats = 9 * dd + 2 * (dd / 4) + 2 * rd + 64;
+    const size_t ws_floats = 9 * dd + 2 * tsum + 2 * rd + 64;
     if ((rc = workspace(ws_floats, &wsp))) return rc;
     float* ws = wsp.ptr;
     cudaError_t e = cudaSuccess;
+    // everything below runs on the internal chain stream, forked from and
+    // joined back into the caller's stream
+    const cudaStream_t st = wsp.chain;
+    e = cudaEventRecord(wsp.fork, user);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.fork, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt stream fork");
     Work w{};
     w.d = d;
     w.side = wsp.side;
@@ -925,8 +959,14 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     w.A = ws; w.A_hi = ws + dd; w.A_lo = ws + 2 * dd;
     w.V = ws + 3 * dd; w.V_hi = ws + 4 * dd; w.V_lo = ws + 5 * dd;
     w.VT = ws + 6 * dd; w.VT_hi = ws + 7 * dd; w.VT_lo = ws + 8 * dd;
-    w.T_hi = ws + 9 * dd; w.T_lo = w.T_hi + dd / 4;
-    float* E_hi = w.T_lo + dd / 4;
+    float* tp = ws + 9 * dd;
+    for (int k = 0; k < kMaxDepth; ++k) {
+        const size_t sz = (tneed[k] + 63) / 64 * 64;
+        w.T_hi[k] = tp;
+        w.T_lo[k] = tp + sz;
+        tp += 2 * sz;
+    }
+    float* E_hi = tp;
     float* E_lo = E_hi + rd;
     double* dsum = reinterpret_cast<double*>(E_lo + rd);
     w.bad = reinterpret_cast<int*>(dsum + 1);
@@ -973,13 +1013,17 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
         e = cudaMemcpyAsync(ut_out, Ut, dd * sizeof(float), cudaMemcpyDeviceToDevice, st);
         if (e != cudaSuccess) rc = cuda_fail(e, "tb_obs_sparsegpt Ut copy");
     }
+    // join the chain stream back into the caller's stream (also on errors)
+    e = cudaEventRecord(wsp.done, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(user, wsp.done, 0);
+    if (e != cudaSuccess && !rc) rc = cuda_fail(e, "tb_obs_sparsegpt stream join");
     if (!rc) {
-        e = cudaMemcpyAsync(&bad, w.bad, sizeof(int), cudaMemcpyDeviceToHost, st);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        e = cudaMemcpyAsync(&bad, w.bad, sizeof(int), cudaMemcpyDeviceToHost, user);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(user);
         if (e != cudaSuccess) rc = cuda_fail(e, "tb_obs_sparsegpt sync");
     }
     if (!rc) {
-        const int ge = umma::gemm_take_error(st);
+        const int ge = umma::gemm_take_error(user);
         if (ge) rc = fail(TB_ERR_TIMEOUT, "a tcgen05 GEMM pipeline wait expired");
     }
     if (!rc && bad == 2) rc = fail(TB_ERR_TIMEOUT, "a wait inside the 128-block factorisation expired");
