@@ -126,45 +126,51 @@ __device__ __forceinline__ void cp_async16(float* dst, const float* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
-// Epilogue of one warp: acc holds row `row0 + lane` of a 128-column output
-// tile starting at column col0.  The 32 x 128 block is staged in shared memory
-// (sbuf, pitch kStagePitch) and handled one output row per step with lane l on
-// columns 4l..4l+3, so every global load and store is a coalesced 512-byte row.
-// With cbuf (a second staging block), the warp's 32 Cin rows are fetched with
-// asynchronous copies while the accumulator is staged, one round trip in all;
-// without it they are loaded in batches of 8 rows.
-__device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc)[kTile], float* sbuf, float* cbuf,
+// Epilogue of one warp: acc holds row `row0 + lane` of a TN-column output
+// tile starting at column col0.  The 32 x TN block is staged in shared memory
+// (sbuf, pitch TN + 4) and handled 128/TN output rows per step with TN/4 lanes
+// per row, each on 4 columns, so every global load and store covers whole
+// rows.  With cbuf (a second staging block), the warp's 32 Cin rows are
+// fetched with asynchronous copies while the accumulator is staged, one round
+// trip in all; without it they are loaded in batches.
+template <int TN>
+__device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc)[TN], float* sbuf, float* cbuf,
                                            long long row0, long long col0, int lane) {
-    const long long gcol = col0 + 4 * lane;
+    constexpr int kPitch = TN + 4;
+    constexpr int kLanesRow = TN / 4;        // lanes per output row
+    constexpr int kRowsStep = 32 / kLanesRow; // rows per step
+    const int sub = lane / kLanesRow, cl = lane % kLanesRow;
+    const long long gcol = col0 + 4 * cl;
     const bool prefetch = cbuf != nullptr && out.beta != 0.0f;
     if (prefetch) {
 #pragma unroll 8
-        for (int rr = 0; rr < 32; ++rr)
-            cp_async16(cbuf + rr * kStagePitch + 4 * lane, out.Cin + (row0 + rr) * out.ldcin + gcol);
+        for (int rr = sub; rr < 32; rr += kRowsStep)
+            cp_async16(cbuf + rr * kPitch + 4 * cl, out.Cin + (row0 + rr) * out.ldcin + gcol);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
 #pragma unroll
-    for (int c = 0; c < kTile / 4; ++c)
-        *reinterpret_cast<float4*>(sbuf + lane * kStagePitch + 4 * c) =
+    for (int c = 0; c < TN / 4; ++c)
+        *reinterpret_cast<float4*>(sbuf + lane * kPitch + 4 * c) =
             make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
     if (prefetch) asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncwarp();
-    constexpr int kBatch = 8;  // rows whose Cin loads are in flight together
-    for (int rb = 0; rb < 32; rb += kBatch) {
+    constexpr int kBatch = 8;  // rows (per lane) whose Cin loads are in flight together
+    for (int rb = 0; rb < 32 / kRowsStep; rb += kBatch) {
         float4 cin[kBatch];
         if (prefetch) {
 #pragma unroll
             for (int u = 0; u < kBatch; ++u)
-                cin[u] = *reinterpret_cast<const float4*>(cbuf + (rb + u) * kStagePitch + 4 * lane);
+                cin[u] = *reinterpret_cast<const float4*>(cbuf + ((rb + u) * kRowsStep + sub) * kPitch + 4 * cl);
         } else if (out.beta != 0.0f) {
 #pragma unroll
             for (int u = 0; u < kBatch; ++u)
-                cin[u] = *reinterpret_cast<const float4*>(out.Cin + (row0 + rb + u) * out.ldcin + gcol);
+                cin[u] = *reinterpret_cast<const float4*>(out.Cin + (row0 + (rb + u) * kRowsStep + sub) * out.ldcin + gcol);
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-            const long long grow = row0 + rb + u;
-            float4* sp = reinterpret_cast<float4*>(sbuf + (rb + u) * kStagePitch + 4 * lane);
+            const int rr = (rb + u) * kRowsStep + sub;
+            const long long grow = row0 + rr;
+            float4* sp = reinterpret_cast<float4*>(sbuf + rr * kPitch + 4 * cl);
             const float4 a = *sp;
             float o[4] = {out.alpha * a.x, out.alpha * a.y, out.alpha * a.z, out.alpha * a.w};
             if (out.beta != 0.0f) {
@@ -191,8 +197,8 @@ __device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc
     if (out.Ct) {  // Ct[col][row]: lane = row again, 32 consecutive rows per store
         __syncwarp();
 #pragma unroll 4
-        for (int c = 0; c < kTile / 4; ++c) {
-            const float4 x = *reinterpret_cast<const float4*>(sbuf + lane * kStagePitch + 4 * c);
+        for (int c = 0; c < TN / 4; ++c) {
+            const float4 x = *reinterpret_cast<const float4*>(sbuf + lane * kPitch + 4 * c);
             const long long col = col0 + 4 * c;
             const long long row = row0 + lane;
             out.Ct[(col + 0) * out.ldct + row] = x.x;
@@ -203,23 +209,25 @@ __device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc
     }
 }
 
-template <int KIND, int STAGES, int SW>
+template <int KIND, int STAGES, int SW, int TN>
 __global__ void __launch_bounds__(kThreadsGemm, 1)
 gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
                const __grid_constant__ CUtensorMap tB0, const __grid_constant__ CUtensorMap tB1, const int nk,
                const GemmOut out) {
-    const int tm = blockIdx.y, tn = blockIdx.x;
-    if (out.lower_only && tn > tm) return;
+    const int tm = blockIdx.y, tn = blockIdx.x;  // 128-row tile, TN-column tile
+    if (out.lower_only && tn * TN / kTile > tm) return;  // 128 x 128 coverage of the lower triangle
     constexpr int kOps = (KIND == kTF32x3) ? 4 : 2;
     constexpr int kElems = SW / ((KIND == kTF32x3) ? 4 : 2);  // K elements per slice
-    constexpr int kTileBytes = kTile * SW;                   // one operand slice
+    constexpr int kABytes = kTile * SW;                      // A operand slice (128 rows)
+    constexpr int kBBytes = TN * SW;                         // B operand slice (TN rows)
+    constexpr int kStageBytes = (kOps / 2) * (kABytes + kBBytes);
     constexpr int kSteps = SW / 32;                          // 32-byte MMA K steps per slice
     constexpr int kGroup = 128 / kElems * ((KIND == kTF32x3) ? 1 : 2);  // slices per promotion group
     constexpr uint32_t kFmt = (KIND == kTF32x3) ? 2u : 1u;
-    constexpr uint32_t kIdesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((kTile >> 3) << 17) | ((kTile >> 4) << 24);
+    constexpr uint32_t kIdesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((TN >> 3) << 17) | ((kTile >> 4) << 24);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kOps * kTileBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* accfull = empty + STAGES;   // [2] group finished in TMEM buffer b
     uint64_t* accempty = accfull + 2;     // [2] buffer b drained by warps 0-3
@@ -256,7 +264,7 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(smem_u32(tmem_slot)), "r"(2 * kTile));
+                     ::"r"(smem_u32(tmem_slot)), "r"(2 * TN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     fence_before();
@@ -267,7 +275,10 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
     // belong to the kernel before this one in the stream.
     pdl_wait();
     pdl_trigger();
-    auto tile = [&](int s, int op) { return smem_u32(smem + (s * kOps + op) * kTileBytes); };
+    // stage layout: A hi, B hi, A lo, B lo (op 0..3)
+    auto tile = [&](int s, int op) {
+        return smem_u32(smem + s * kStageBytes + (op >> 1) * (kABytes + kBBytes) + (op & 1) * kABytes);
+    };
 
     if (warp == 4) {
         if (lane == 0) {  // TMA producer
@@ -280,13 +291,13 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
                 }
                 if (*abort_flag) break;
                 const uint32_t bar = smem_u32(&full[s]);
-                mbar_expect_tx(bar, kOps * kTileBytes);
+                mbar_expect_tx(bar, kStageBytes);
                 const int x = (kc0 + kc) * kElems;
                 tma_load_2d(tile(s, 0), &tA0, x, tm * kTile, bar);
-                tma_load_2d(tile(s, 1), &tB0, x, tn * kTile, bar);
+                tma_load_2d(tile(s, 1), &tB0, x, tn * TN, bar);
                 if constexpr (KIND == kTF32x3) {
                     tma_load_2d(tile(s, 2), &tA1, x, tm * kTile, bar);
-                    tma_load_2d(tile(s, 3), &tB1, x, tn * kTile, bar);
+                    tma_load_2d(tile(s, 3), &tB1, x, tn * TN, bar);
                 }
                 issued = kc + 1;
             }
@@ -303,7 +314,7 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
                 const int b = g & 1;
                 if (g >= 2 && !mbar_wait(smem_u32(&accempty[b]), ((g >> 1) - 1) & 1)) { ok = false; break; }
                 fence_after();
-                const uint32_t acc_t = tmem + static_cast<uint32_t>(b * kTile);
+                const uint32_t acc_t = tmem + static_cast<uint32_t>(b * TN);
                 const int k_end = std::min(nkr, (g + 1) * kGroup);
                 for (int kc = g * kGroup; kc < k_end; ++kc) {
                     const int s = kc % STAGES;
@@ -337,17 +348,17 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
         __syncwarp();
     } else {
         // Warps 0-3: promote each finished group into FP32 registers, then store.
-        float acc[kTile];
+        float acc[TN];
 #pragma unroll
-        for (int j = 0; j < kTile; ++j) acc[j] = 0.0f;
+        for (int j = 0; j < TN; ++j) acc[j] = 0.0f;
         bool ok = true;
         for (int g = 0; g < ngroups; ++g) {
             const int b = g & 1;
             if (!mbar_wait(smem_u32(&accfull[b]), (g >> 1) & 1) || *abort_flag) { ok = false; break; }
             fence_after();
-            const uint32_t base = tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(b * kTile);
+            const uint32_t base = tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(b * TN);
 #pragma unroll
-            for (int c = 0; c < kTile / 32; ++c) {
+            for (int c = 0; c < TN / 32; ++c) {
                 float v[32];
                 tmem_ld32(base + static_cast<uint32_t>(c * 32), v);
 #pragma unroll
@@ -361,19 +372,20 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
             if (lane == 0) atomicExch(&g_umma_error, 1);
         } else {
             // All MMAs have completed, so the operand ring is free for staging.
-            static_assert(4 * 32 * kStagePitch * 4 <= STAGES * kOps * kTileBytes, "epilogue staging exceeds the ring");
-            // a second staging block for the Cin prefetch where the ring has room (3xTF32)
-            constexpr bool kCinBuf = 8 * 32 * kStagePitch * 4 <= STAGES * kOps * kTileBytes;
+            constexpr int kBlk = 32 * (TN + 4);  // one warp's staging block (floats)
+            static_assert(4 * kBlk * 4 <= STAGES * kStageBytes, "epilogue staging exceeds the ring");
+            // a second staging block for the Cin prefetch where the ring has room
+            constexpr bool kCinBuf = 8 * kBlk * 4 <= STAGES * kStageBytes;
             float* sb = reinterpret_cast<float*>(smem);
-            store_rows(out, acc, sb + warp * 32 * kStagePitch, kCinBuf ? sb + (4 + warp) * 32 * kStagePitch : nullptr,
-                       static_cast<long long>(tm) * kTile + warp * 32, static_cast<long long>(tn) * kTile, lane);
+            store_rows<TN>(out, acc, sb + warp * kBlk, kCinBuf ? sb + (4 + warp) * kBlk : nullptr,
+                           static_cast<long long>(tm) * kTile + warp * 32, static_cast<long long>(tn) * TN, lane);
         }
     }
     fence_before();
     __syncthreads();
     if (warp == 0) {
         fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTile));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TN));
     }
 }
 
@@ -607,7 +619,7 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
             if (lane == 0) atomicExch(&g_umma_error, 1);
         } else if (!(out.lower_only && sub_col > sub_row)) {
             static_assert(kEpi * 32 * kStagePitch * 4 <= kStages * P::kStage, "epilogue staging exceeds the ring");
-            store_rows(out, acc, reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch, nullptr,
+            store_rows<kTile>(out, acc, reinterpret_cast<float*>(smem) + warp * 32 * kStagePitch, nullptr,
                        static_cast<long long>(sub_row) * kTile + quad * 32, static_cast<long long>(sub_col) * kTile,
                        lane);
         }
@@ -654,20 +666,20 @@ int make_map(CUtensorMap* map, const void* base, bool bf16, long long rows, long
     return TB_OK;
 }
 
-template <int KIND, int STAGES, int SW>
+template <int KIND, int STAGES, int SW, int TN>
 int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0, const CUtensorMap& b1, int M, int N,
            int nk, const GemmOut& out, cudaStream_t st) {
     constexpr int kOps = (KIND == kTF32x3) ? 4 : 2;
-    const size_t smem = static_cast<size_t>(STAGES) * kOps * kTile * SW + 1024 + 256;
+    const size_t smem = static_cast<size_t>(STAGES) * (kOps / 2) * (kTile + TN) * SW + 1024 + 256;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [&] {
-        attr = cudaFuncSetAttribute(gemm_nt_kernel<KIND, STAGES, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr = cudaFuncSetAttribute(gemm_nt_kernel<KIND, STAGES, SW, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem));
     });
     if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute(gemm_nt_kernel)");
-    const cudaError_t e = launch_pdl(gemm_nt_kernel<KIND, STAGES, SW>, dim3(N / kTile, M / kTile), dim3(kThreadsGemm),
-                                     smem, st, a0, a1, b0, b1, nk, out);
+    const cudaError_t e = launch_pdl(gemm_nt_kernel<KIND, STAGES, SW, TN>, dim3(N / TN, M / kTile),
+                                     dim3(kThreadsGemm), smem, st, a0, a1, b0, b1, nk, out);
     return e == cudaSuccess ? check_launch("gemm_nt_kernel") : cuda_fail(e, "gemm_nt_kernel launch");
 }
 
@@ -747,15 +759,21 @@ int gemm_nt(Kind kind, const Operand& A, const Operand& B, int M, int N, int K, 
         return nb == 256 ? launch_pair<kTF32x3, 256>(pa0, pa1, pb0, pb1, M, N, nk2, out, stream)
                          : launch_pair<kTF32x3, 128>(pa0, pa1, pb0, pb1, M, N, nk2, out, stream);
     }
+    // Products that fill less than one wave of 128 x 128 tiles are latency-bound
+    // (one SM writes a whole tile): 128 x 64 tiles halve each CTA's output and
+    // hold four K-slices in flight.
+    const bool narrow = !bf16 && (static_cast<long long>(M / kTile) * (N / kTile) < 148);
+    const int tn_rows = narrow ? kTile / 2 : kTile;
     int rc = make_map(&a0, A.hi, bf16, M, K, A.ld, sw);
-    if (!rc) rc = make_map(&b0, B.hi, bf16, N, K, B.ld, sw);
+    if (!rc) rc = make_map(&b0, B.hi, bf16, N, K, B.ld, sw, tn_rows);
     if (!rc && !bf16) rc = make_map(&a1, A.lo, false, M, K, A.ld, sw);
-    if (!rc && !bf16) rc = make_map(&b1, B.lo, false, N, K, B.ld, sw);
+    if (!rc && !bf16) rc = make_map(&b1, B.lo, false, N, K, B.ld, sw, tn_rows);
     if (rc) return rc;
     if (bf16) { a1 = a0; b1 = b0; }
     const int nk = K / (sw / (bf16 ? 2 : 4));
-    return bf16 ? launch<kBF16, 4, 128>(a0, a1, b0, b1, M, N, nk, out, stream)
-                : launch<kTF32x3, 3, 128>(a0, a1, b0, b1, M, N, nk, out, stream);
+    if (bf16) return launch<kBF16, 4, 128, 128>(a0, a1, b0, b1, M, N, nk, out, stream);
+    return narrow ? launch<kTF32x3, 4, 128, 64>(a0, a1, b0, b1, M, N, nk, out, stream)
+                  : launch<kTF32x3, 3, 128, 128>(a0, a1, b0, b1, M, N, nk, out, stream);
 }
 
 int gemm_take_error(cudaStream_t stream) {

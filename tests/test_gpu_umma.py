@@ -1,7 +1,9 @@
 """GPU: the tcgen05 NT GEMM (3xTF32 and BF16) against float64, with the error
 bar of an FP32 (non-TF32) cuBLAS product of the same operands.  3xTF32 shapes
 with M a multiple of 256 and K >= 512 run on CTA pairs (cta_group::2), the
-others on single CTAs; both paths appear below, with and without lower_only."""
+others on single CTAs with 128 x 128 tiles, or 128 x 64 tiles when fewer than
+148 tiles of 128 x 128 cover the output; every path appears below, with and
+without lower_only."""
 import ctypes as C
 
 import pytest
@@ -19,7 +21,7 @@ def split(torch, tb, x):
     (128, 128, 32, 1.0, 0.0, 0, "x3"), (256, 384, 96, 1.0, 0.0, 0, "x3"), (1024, 1024, 1024, 1.0, 0.0, 0, "x3"),
     (512, 256, 4096, 1.0, 0.0, 0, "x3"), (384, 384, 256, -1.0, 1.0, 1, "x3"), (2048, 1024, 512, 0.5, 2.0, 0, "x3"),
     (768, 768, 512, -1.0, 1.0, 1, "x3"), (640, 384, 1024, 1.0, 0.0, 0, "x3"), (256, 128, 8192, 1.0, 0.0, 0, "x3"),
-    (512, 384, 512, -1.0, 1.0, 1, "x3"),
+    (512, 384, 512, -1.0, 1.0, 1, "x3"), (1152, 2432, 256, 0.5, 1.0, 0, "x3"), (1152, 1152, 384, -1.0, 1.0, 1, "x3"),
     (128, 128, 64, 1.0, 0.0, 0, "bf16"), (1024, 512, 2048, 0.5, 1.0, 0, "bf16"), (768, 768, 128, 1.0, 0.0, 1, "bf16"),
     (768, 768, 1024, 1.0, 0.0, 1, "bf16"), (512, 384, 2048, 1.0, 0.5, 0, "bf16")])
 def test_gemm_nt_matches_float64(cuda, tblib, M, N, K, alpha, beta, lower, kind):
