@@ -266,11 +266,44 @@ __device__ __forceinline__ void dot4x1(const float* X, int px, const float* Y, i
     }
 }
 
+constexpr int kBaseWarps = kBaseThreads / 32;
+constexpr int kIdle0 = 5;  // first warp free during a diagonal step (0: factor, 1: inverse, 2-4: panel)
+
+// Block row ib of V = L^-1 is V_ij = -V_ii S_j with S_j = sum_{m=j}^{i-1} L_im V_mj
+// (j < i), in 32-blocks.  v_row_s forms S_j^T (from L's row block ib and V^T's
+// rows of the final block rows < ib) into sST; v_row_finish forms V_ij and its
+// transpose once V_ii exists.  Work is split over nw warps, four rows each.
+__device__ __forceinline__ void v_row_s(const float* sA, const float* sVT, float* sST, int ib, int iw, int nw,
+                                        int lane) {
+#pragma unroll 1
+    for (int task = iw; task < ib * 8; task += nw) {
+        const int jb = task >> 3, i = 4 * (task & 7);
+        float acc[4];
+        dot4x1(sA + (32 * ib + i) * kP + 32 * jb, kP, sVT + (32 * jb + lane) * kP + 32 * jb, 32 * (ib - jb), acc);
+        *reinterpret_cast<float4*>(sST + (jb * 32 + lane) * kSP + i) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+}
+__device__ __forceinline__ void v_row_finish(float* sV, float* sVT, const float* sST, int ib, int iw, int nw,
+                                             int lane) {
+#pragma unroll 1
+    for (int task = iw; task < ib * 8; task += nw) {
+        const int jb = task >> 3, i = 4 * (task & 7);
+        float acc[4];
+        dot4x1(sV + (32 * ib + i) * kP + 32 * ib, kP, sST + (jb * 32 + lane) * kSP, 32, acc);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sV[(32 * ib + i + r) * kP + 32 * jb + lane] = -acc[r];
+        *reinterpret_cast<float4*>(sVT + (32 * jb + lane) * kP + 32 * ib + i) =
+            make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
+    }
+}
+
 // Cholesky and inverse of one 128 x 128 diagonal block in shared memory,
 // blocked by 32: per 32-column step, the diagonal block is factored and
 // inverted by one warp (diag32), the panel below is L_ik = A_ik L_kk^-T and
 // the trailing lower blocks take the Schur update; then the off-diagonal
-// blocks of V = L^-1 are V_ij = -V_ii sum_{k=j}^{i-1} L_ik V_kj.  Every
+// blocks of V = L^-1 are V_ij = -V_ii sum_{k=j}^{i-1} L_ik V_kj, formed by
+// the warps a diagonal step leaves idle (block row i's sum during step i, its
+// product with V_ii during step i+1; the last row after the loop).  Every
 // product is written as rows times rows (V^T and S^T are kept for that), each
 // thread computing four rows of one column.
 // Writes L (lower part of A), V with its split (zeros above the diagonal) and
@@ -314,6 +347,14 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
             diag_inverse(sLc, sRinv, ready, 32 * kb, sV + o * kP + o, sVT + o * kP + o, lane, bad);
         } else if (warp - 2 < prow / 32) {
             diag_panel(sA + (o + 32 + 32 * (warp - 2) + lane) * kP + o, sLc, sRinv, ready, 32 * kb, bad);
+        } else if (warp >= kIdle0) {
+            // Warps 5..15 are otherwise idle during the diagonal step: they finish
+            // block row kb-1 of V (its diagonal inverse came from the previous
+            // step) and then form S for block row kb (rows < kb of V are final).
+            const int iw = warp - kIdle0;
+            if (kb >= 2) v_row_finish(sV, sVT, sST, kb - 1, iw, kBaseWarps - kIdle0, lane);
+            asm volatile("bar.sync 1, %0;" ::"r"(32 * (kBaseWarps - kIdle0)) : "memory");
+            if (kb >= 1) v_row_s(sA, sVT, sST, kb, iw, kBaseWarps - kIdle0, lane);
         }
         __syncthreads();
         if (prow == 0) break;
@@ -333,31 +374,9 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
         }
         __syncthreads();
     }
-    // off-diagonal blocks of V, block row by block row
-#pragma unroll 1
-    for (int ib = 1; ib < 4; ++ib) {
-        // S_j^T[c][i] = sum_{m=32jb}^{32ib-1} L[32ib+i][m] V^T[32jb+c][m]
-#pragma unroll 1
-        for (int task = warp; task < ib * 8; task += 16) {
-            const int jb = task >> 3, i = 4 * (task & 7);
-            float acc[4];
-            dot4x1(sA + (32 * ib + i) * kP + 32 * jb, kP, sVT + (32 * jb + lane) * kP + 32 * jb, 32 * (ib - jb), acc);
-            *reinterpret_cast<float4*>(sST + (jb * 32 + lane) * kSP + i) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        }
-        __syncthreads();
-        // V[32ib+i][32jb+c] = -sum_m V[32ib+i][32ib+m] S_j^T[c][m], and its transpose
-#pragma unroll 1
-        for (int task = warp; task < ib * 8; task += 16) {
-            const int jb = task >> 3, i = 4 * (task & 7);
-            float acc[4];
-            dot4x1(sV + (32 * ib + i) * kP + 32 * ib, kP, sST + (jb * 32 + lane) * kSP, 32, acc);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) sV[(32 * ib + i + r) * kP + 32 * jb + lane] = -acc[r];
-            *reinterpret_cast<float4*>(sVT + (32 * jb + lane) * kP + 32 * ib + i) =
-                make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
-        }
-        __syncthreads();
-    }
+    // the last block row of V (its S was formed during the last diagonal step)
+    v_row_finish(sV, sVT, sST, 3, warp, kBaseWarps, lane);
+    __syncthreads();
     // Write-out: V in FP32 (the final transpose reads it) with its split, and
     // the split of V^T.  The factor of this block is not written back: after
     // its diagonal block is factored nothing reads it (the triangular solves
