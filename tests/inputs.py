@@ -103,3 +103,65 @@ def activations(n, d, seed, frac=0.01, scale=20.0):
     hot = rng.choice(d, max(1, int(d * frac)), replace=False)
     X[:, hot] *= np.float32(scale)
     return bf16_bits_to_f32(to_bf16_bits(X)).reshape(n, d)
+
+
+def _tb_file(path, nm_n, nm_m, n_weights, mask_bytes, precision, seed, magic=0x31304254, payload=None):
+    """A .tb file: the 4096-byte header, then `payload` bytes (default: FP32
+    weights, or FP64 for precision 3, then the mask bytes)."""
+    import struct
+    rng = np.random.default_rng(seed)
+    head = bytearray(4096)
+    elem = 8 if precision == 3 else 4
+    struct.pack_into("<IIIIQQQQB", head, 0, magic, 1, nm_n, nm_m, n_weights, mask_bytes,
+                     4096, 4096 + elem * n_weights, precision)
+    if payload is None:
+        w = rng.standard_normal(n_weights).astype(np.float64 if elem == 8 else np.float32)
+        payload = w.tobytes() + rng.integers(0, 256, mask_bytes, dtype=np.uint8).tobytes()
+    with open(path, "wb") as f:
+        f.write(bytes(head) + payload)
+
+
+def merge_tree(root):
+    """Two shard directories of .tb files for the .tbm merge, with the cases the
+    merge has to get right: hidden names, suffixes inside names, duplicates
+    (including a name reserved by a file whose header is bad), a truncated
+    header, a wrong magic, an FP64 tensor and a short payload (offsets follow the
+    headers, not the file sizes), quotes, backslashes and non-ASCII names, and
+    files that are not .tb."""
+    import os
+    s1, s2 = os.path.join(root, "shard1"), os.path.join(root, "shard2")
+    os.makedirs(s1)
+    os.makedirs(s2)
+    _tb_file(os.path.join(s1, "model.layers.0.self_attn.q_proj.weight.tb"), 2, 4, 96, 24, 0, 1)
+    _tb_file(os.path.join(s1, "model.layers.0.mlp.down_proj.weight.tb"), 2, 8, 128, 16, 0, 2)
+    _tb_file(os.path.join(s1, "lm_head.weight.tb"), 2, 4, 32, 8, 3, 3)
+    _tb_file(os.path.join(s1, ".hidden.tb"), 1, 4, 16, 4, 1, 4)
+    _tb_file(os.path.join(s1, "dup.tb"), 2, 4, 8, 2, 0, 5)
+    _tb_file(os.path.join(s1, "bad_magic.tb"), 2, 4, 8, 2, 0, 6, magic=0x12345678)
+    with open(os.path.join(s1, "zz_truncated.tb"), "wb") as f:
+        f.write(bytes(range(100)))
+    with open(os.path.join(s1, "model.tbm"), "wb") as f:
+        f.write(b"not a container")
+    with open(os.path.join(s1, "notes.txt"), "w") as f:
+        f.write("ignored\n")
+    _tb_file(os.path.join(s2, "model.layers.1.self_attn.q_proj.weight.tb"), 2, 4, 64, 16, 2, 7)
+    _tb_file(os.path.join(s2, "dup.tb"), 2, 4, 8, 2, 0, 8)
+    _tb_file(os.path.join(s2, "bad_magic.tb"), 2, 4, 8, 2, 0, 9)
+    _tb_file(os.path.join(s2, 'we"ird\\name ü.tb'), 2, 4, 8, 2, 0, 10)
+    _tb_file(os.path.join(s2, "emoji\U0001F600.tb"), 4, 8, 16, 2, 0, 11)
+    _tb_file(os.path.join(s2, "x.tbm.tb"), 2, 4, 8, 2, 0, 12)
+    _tb_file(os.path.join(s2, "a.tb.tb"), 2, 4, 8, 2, 0, 13)
+    _tb_file(os.path.join(s2, "Upper.tb"), 2, 4, 8, 2, 0, 14)
+    _tb_file(os.path.join(s2, "short_payload.tb"), 2, 4, 1000, 250, 0, 15, payload=bytes(40))
+    os.makedirs(os.path.join(root, "empty"))
+    return s1, s2
+
+
+# tb-merge / merge_tbm.py runs over merge_tree(): (key, arguments, run from)
+MERGE_RUNS = {
+    "shards": (["--input", "./shard1/", "shard2", "missing_dir", "--output", "out/full/model.tbm"], "."),
+    "reversed_arch": (["--input", "shard2", "shard1", "--output", "r.tbm",
+                       "--architecture", 'mistral "7b" ü\\\U0001F600'], "."),
+    "dot_input": (["--input", ".", "--output", "../dot/model.tbm"], "shard1"),
+    "empty": (["--input", "empty", "--output", "e.tbm"], "."),
+}
