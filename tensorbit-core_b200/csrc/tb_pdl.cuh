@@ -1,21 +1,54 @@
 // Programmatic dependent launch for chains of small dependent kernels (the
 // recursive factorisation issues ~1300 of them per OBS pass).  A kernel
-// launched by launch_pdl() may be scheduled while its predecessor in the
-// stream is still running: it does its setup that touches no global memory
-// (barrier init, TMEM allocation, tensor-map prefetch), then pdl_wait() blocks
-// until the predecessor grid has completed and its writes are visible, and
-// only then reads or writes global memory.  pdl_trigger() lets the kernel's
-// own successor be scheduled; it is issued right after pdl_wait(), so at most
-// one launch ahead is resident early.  A kernel launched without the attribute
-// returns from pdl_wait() at once.
+// launched by launch_pdl() is handed to the GPU before its predecessor in the
+// stream has finished, so that it starts the moment the predecessor exits
+// instead of a launch latency later.  It does its setup that touches no global
+// memory (barrier init, TMEM allocation, tensor-map prefetch), then pdl_wait()
+// blocks until the predecessor grid has completed and its writes are visible,
+// and only then reads or writes global memory.  A kernel launched without the
+// attribute returns from pdl_wait() at once.
+//
+// No kernel issues griddepcontrol.launch_dependents: its successor is released
+// only when it exits.  With the trigger issued right after pdl_wait() in every
+// kernel (successors resident early), the exact-OBS chain of a 14336-wide
+// layer gave results that differed from run to run on B200, some with a failed
+// Cholesky pivot, although every ordering of the schedule checks out; without
+// the early trigger it is bit-reproducible and barely slower.
 #pragma once
 
 #include <cuda_runtime.h>
 
+#include <vector>
+
 namespace tb {
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Streams whose next launch must be an ordinary one: the first launch behind a
+// cudaStreamWaitEvent takes no attribute, so that nothing rests on how a
+// programmatic launch combines the predecessor kernel with the awaited event.
+// Every cross-stream wait marks its stream with pdl_fence(); pdl_allowed()
+// reads and clears the mark.  The marks are per host thread; a stream is
+// driven from one thread at a time.
+inline thread_local std::vector<cudaStream_t> g_pdl_fences;
+
+inline void pdl_fence(cudaStream_t st) {
+    for (cudaStream_t x : g_pdl_fences)
+        if (x == st) return;
+    g_pdl_fences.push_back(st);
+}
+
+// True if the next launch on st may be programmatic; clears st's mark.
+inline bool pdl_allowed(cudaStream_t st) {
+    auto& f = g_pdl_fences;
+    for (size_t i = 0; i < f.size(); ++i)
+        if (f[i] == st) {
+            f[i] = f.back();
+            f.pop_back();
+            return false;
+        }
+    return true;
+}
 
 template <typename... Params, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
@@ -27,7 +60,7 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_allowed(st) ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);

@@ -52,7 +52,6 @@ __device__ __forceinline__ float tf32_round(float x) {
 __global__ void diag_sum_kernel(const float* __restrict__ H, int d, double* __restrict__ out) {
     __shared__ double part[1024];
     pdl_wait();
-    pdl_trigger();
     double s = 0.0;
     for (int i = threadIdx.x; i < d; i += blockDim.x) s += static_cast<double>(H[static_cast<size_t>(i) * d + i]);
     part[threadIdx.x] = s;
@@ -76,7 +75,6 @@ __global__ void __launch_bounds__(256) reverse_damp_kernel(const float* __restri
     __shared__ float tile[32][33];
     const int I = blockIdx.y, J = blockIdx.x;  // output tile: rows 32I.., columns 32J..
     pdl_wait();
-    pdl_trigger();
     if (J > I && (J >> 2) != (I >> 2)) return;
     const float lambda = static_cast<float>(frac * (*diag_sum / d));
     const int tx = threadIdx.x, ty = threadIdx.y;
@@ -326,7 +324,6 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const size_t base = static_cast<size_t>(off) * ld + off;
     pdl_wait();
-    pdl_trigger();
     if (t == 0) *sReady = 0;
 #pragma unroll 4
     for (int e = t; e < kB * kB; e += kBaseThreads) {
@@ -405,7 +402,6 @@ __global__ void __launch_bounds__(256) zero_adjacent_kernel(float* __restrict__ 
                                                             float* __restrict__ V_lo, float* __restrict__ VT_hi,
                                                             float* __restrict__ VT_lo, int d) {
     pdl_wait();
-    pdl_trigger();
     const int blk = blockIdx.y;  // diagonal block index, 0 .. d/128 - 2
     const size_t off = static_cast<size_t>(blk) * kB;
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < kB * kB; e += gridDim.x * blockDim.x) {
@@ -418,13 +414,12 @@ __global__ void __launch_bounds__(256) zero_adjacent_kernel(float* __restrict__ 
 }
 constexpr size_t kBaseSmem = (3 * kB * kP + 3 * 32 * kSP + 32 * 32 + 32 + 4) * sizeof(float);
 
-// Ut = (P V P)^T on the lower triangle: Ut[i][j] = V[d-1-j][d-1-i], with split.
-__global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, float* __restrict__ Ut,
-                                         float* __restrict__ Ut_hi, float* __restrict__ Ut_lo) {
+// Ut = (P V P)^T on the lower triangle: Ut[i][j] = V[d-1-j][d-1-i] (the
+// factor U = chol(H^-1) transposed, for callers that ask for it).
+__global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, float* __restrict__ Ut) {
     __shared__ float tile[32][33];
     const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // output tile (rows by.., cols bx..)
     pdl_wait();
-    pdl_trigger();
     // source rows d-1-(bx+..), cols d-1-(by+..)
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
         const int sr = d - 1 - (bx + k), sc = d - 1 - (by + threadIdx.x);
@@ -434,17 +429,18 @@ __global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, flo
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
         const int i = by + k, j = bx + threadIdx.x;
         const float v = (j <= i) ? tile[threadIdx.x][k] : 0.0f;
-        const size_t g = static_cast<size_t>(i) * d + j;
-        const float h = tf32_round(v);
-        Ut[g] = v;
-        Ut_hi[g] = h;
-        Ut_lo[g] = v - h;
+        Ut[static_cast<size_t>(i) * d + j] = v;
     }
 }
 
 // In-block OBS sweep of columns [i1, i1+128) for every row: one warp per two
 // rows (two independent dependency chains per warp), lane l holding columns
-// 4l..4l+3 of both rows.  M must be 4 here (the lane's four columns are one
+// 4l..4l+3 of both rows.  The sweep keeps W and the errors in reversed column
+// order (Wr[:, c] = W[:, d-1-c], likewise E), so that the later columns' updates
+// are plain products with V = L^-1 of the reversed Hessian; this kernel reads
+// its block from Wr, writes the block's final weights to W in natural order
+// (no later step touches them), and its errors to E reversed.  Its block of U
+// is U[i1+q][i1+j] = V[o+127-q][o+127-j], o = d-i1-128.  M must be 4 here (the lane's four columns are one
 // group); N:4 with N in {1, 2, 3}.  The block of U sits in shared memory with
 // column j of row q at q*kU1 + (j%4)*32 + j/4, so that the four values a lane
 // needs are bank-conflict free; 1/U_qq follows it.  Only pruned columns carry
@@ -494,25 +490,27 @@ __device__ __forceinline__ void obs_group_solve(float (&w)[4], float (&e)[4], ui
     }
 }
 
-__global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, int r, int d, int i1,
-                                                             const float* __restrict__ Ut, int n_keep,
-                                                             uint8_t* __restrict__ mask, float* __restrict__ E_hi,
-                                                             float* __restrict__ E_lo, long long ldE) {
+__global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, const float* __restrict__ Wr,
+                                                             int r, int d, int i1, const float* __restrict__ V,
+                                                             int n_keep, uint8_t* __restrict__ mask,
+                                                             float* __restrict__ E_hi, float* __restrict__ E_lo,
+                                                             long long ldE) {
     extern __shared__ float u1[];
     float* rinv = u1 + kB * kU1;
+    const int o = d - i1 - kB;  // the block's first column in reversed order
     pdl_wait();
-    pdl_trigger();
-    // U[i1+q][i1+j] = Ut[i1+j][i1+q] (j >= q), sixteen loads in flight per thread
+    // U[q][j] = V[o+vr][o+vc] with q = 127-vr, j = 127-vc (j >= q, i.e. vc <= vr),
+    // read along V's rows, sixteen loads in flight per thread
     for (int b = threadIdx.x; b < kB * kB; b += kIbThreads * 16) {
         float v[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-            const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
-            v[u] = (e < kB * kB && j >= q) ? Ut[static_cast<size_t>(i1 + j) * d + i1 + q] : 0.0f;
+            const int e = b + u * kIbThreads, vc = e & 127, vr = e >> 7;
+            v[u] = (e < kB * kB && vc <= vr) ? V[static_cast<size_t>(o + vr) * d + o + vc] : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-            const int e = b + u * kIbThreads, q = e & 127, j = e >> 7;
+            const int e = b + u * kIbThreads, j = 127 - (e & 127), q = 127 - (e >> 7);
             if (e < kB * kB) u1[q * kU1 + (j & 3) * 32 + (j >> 2)] = v[u];
         }
     }
@@ -528,11 +526,12 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
     float* wr0 = W + row0 * d + i1;
     float* wr1 = wr0 + d;
     float w0[4], w1[4];
-    {
-        const float4 x = reinterpret_cast<const float4*>(wr0)[lane];
-        const float4 y = reinterpret_cast<const float4*>(wr1)[lane];
-        w0[0] = x.x; w0[1] = x.y; w0[2] = x.z; w0[3] = x.w;
-        w1[0] = y.x; w1[1] = y.y; w1[2] = y.z; w1[3] = y.w;
+    {  // columns 4l..4l+3 sit reversed in Wr's float4 31-l of the block
+        const float* rr0 = Wr + row0 * d + o;
+        const float4 x = reinterpret_cast<const float4*>(rr0)[31 - lane];
+        const float4 y = reinterpret_cast<const float4*>(rr0 + d)[31 - lane];
+        w0[0] = x.w; w0[1] = x.z; w0[2] = x.y; w0[3] = x.x;
+        w1[0] = y.w; w1[1] = y.z; w1[2] = y.y; w1[3] = y.x;
     }
     float e0[4] = {0, 0, 0, 0}, e1[4] = {0, 0, 0, 0};
     uint32_t own0 = 0, own1 = 0;
@@ -572,19 +571,30 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
     reinterpret_cast<float4*>(wr1)[lane] = make_float4(w1[0], w1[1], w1[2], w1[3]);
     mask[(row0 * d + i1) / 4 + lane] = static_cast<uint8_t>(own0);
     mask[((row0 + 1) * d + i1) / 4 + lane] = static_cast<uint8_t>(own1);
-    float4 h, l;
-    h.x = tf32_round(e0[0]); l.x = e0[0] - h.x;
-    h.y = tf32_round(e0[1]); l.y = e0[1] - h.y;
-    h.z = tf32_round(e0[2]); l.z = e0[2] - h.z;
-    h.w = tf32_round(e0[3]); l.w = e0[3] - h.w;
-    reinterpret_cast<float4*>(E_hi + row0 * ldE + i1)[lane] = h;
-    reinterpret_cast<float4*>(E_lo + row0 * ldE + i1)[lane] = l;
-    h.x = tf32_round(e1[0]); l.x = e1[0] - h.x;
-    h.y = tf32_round(e1[1]); l.y = e1[1] - h.y;
-    h.z = tf32_round(e1[2]); l.z = e1[2] - h.z;
-    h.w = tf32_round(e1[3]); l.w = e1[3] - h.w;
-    reinterpret_cast<float4*>(E_hi + (row0 + 1) * ldE + i1)[lane] = h;
-    reinterpret_cast<float4*>(E_lo + (row0 + 1) * ldE + i1)[lane] = l;
+    float4 h, l;  // errors reversed, like Wr
+    h.x = tf32_round(e0[3]); l.x = e0[3] - h.x;
+    h.y = tf32_round(e0[2]); l.y = e0[2] - h.y;
+    h.z = tf32_round(e0[1]); l.z = e0[1] - h.z;
+    h.w = tf32_round(e0[0]); l.w = e0[0] - h.w;
+    reinterpret_cast<float4*>(E_hi + row0 * ldE + o)[31 - lane] = h;
+    reinterpret_cast<float4*>(E_lo + row0 * ldE + o)[31 - lane] = l;
+    h.x = tf32_round(e1[3]); l.x = e1[3] - h.x;
+    h.y = tf32_round(e1[2]); l.y = e1[2] - h.y;
+    h.z = tf32_round(e1[1]); l.z = e1[1] - h.z;
+    h.w = tf32_round(e1[0]); l.w = e1[0] - h.w;
+    reinterpret_cast<float4*>(E_hi + (row0 + 1) * ldE + o)[31 - lane] = h;
+    reinterpret_cast<float4*>(E_lo + (row0 + 1) * ldE + o)[31 - lane] = l;
+}
+
+// Wr[:, c] = W[:, d-1-c] for the sweep (one float4 per thread step).
+__global__ void reverse_columns_kernel(const float* __restrict__ W, float* __restrict__ Wr, int r, int d) {
+    pdl_wait();
+    const size_t q = static_cast<size_t>(d / 4), total = static_cast<size_t>(r) * q;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t row = e / q, c4 = e % q;
+        const float4 x = reinterpret_cast<const float4*>(W + row * d)[q - 1 - c4];
+        reinterpret_cast<float4*>(Wr + row * d)[c4] = make_float4(x.w, x.z, x.y, x.x);
+    }
 }
 
 constexpr int kMaxDepth = 16;
@@ -600,6 +610,7 @@ struct Work {
     cudaStream_t ahead;              // stream of the look-ahead Schur updates
     cudaEvent_t evl;                 // "this node's L21 is complete"
     cudaEvent_t ev21[kMaxDepth], ev22[kMaxDepth];  // look-ahead updates done, per recursion depth
+    cudaEvent_t evv[kMaxDepth];  // a node's V21 (and its V^T split) complete on w.side, per depth
 };
 
 // Regions of a node's matrix that its parent's look-ahead update is still
@@ -666,6 +677,7 @@ int schur(Work& w, long long r0, long long c0, int m, int nn, long long lc, int 
 int wait_on(cudaStream_t st, cudaEvent_t ev) {
     if (!ev) return TB_OK;
     const cudaError_t e = cudaStreamWaitEvent(st, ev, 0);
+    pdl_fence(st);
     return e == cudaSuccess ? TB_OK : cuda_fail(e, "tb_obs_sparsegpt stream wait");
 }
 int record_on(cudaEvent_t ev, cudaStream_t st) {
@@ -718,7 +730,8 @@ int chol(Work& w, int off, int n, cudaStream_t st, int depth, Pending pend) {
     if ((rc = chol(w, off + n1, n2, st, depth + 1, child))) return rc;
     if ((rc = record_on(w.ev, st))) return rc;
     if ((rc = wait_on(w.side, w.ev))) return rc;
-    return trtri_v(w, off, n, depth, w.side);
+    if ((rc = trtri_v(w, off, n, depth, w.side))) return rc;
+    return record_on(w.evv[depth], w.side);
 }
 
 // Node steps of the triangular inverse V = L^-1 for the node [off, off+n):
@@ -767,63 +780,77 @@ void trtri_sizes(int n, int depth, size_t* need) {
 }
 
 struct Sweep {
-    float* W;
+    float* W;                        // the caller's weights (final values, natural order)
+    float* Wr;                       // working copy, columns reversed
     int r, d, n_keep;
-    const float *Ut, *Ut_hi, *Ut_lo;
+    const float *V, *VT_hi, *VT_lo;  // L^-1 of the reversed Hessian and its transpose's split
     uint8_t* mask;
-    float *E_hi, *E_lo;  // r x d, pitch d
+    float *E_hi, *E_lo;              // r x d errors, columns reversed, pitch d
     cudaStream_t ahead;              // look-ahead updates
-    cudaEvent_t evl;                 // "the left half's errors are complete"
+    cudaEvent_t evl;                 // "the high part's errors are complete"
     const cudaEvent_t* ev;           // [kMaxDepth] look-ahead update done, per depth
+    const cudaEvent_t* evv;          // [kMaxDepth] a node's V21 complete, per depth
+    bool* evv_waited;                // [kMaxDepth] st already waited on evv[depth]
 };
 
-// Column sweep of [a, a+n): recursive on the columns, like the triangular
-// solve.  After the left half is swept, its errors update the right half in
-// one GEMM, W[:, a+n1 : a+n] -= E[:, a : a+n1] U[a : a+n1, a+n1 : a+n], with
-// U[a : a+n1, a+n1 : a+n] = (Ut[a+n1 : a+n, a : a+n1])^T.  Every column block
-// therefore sees all earlier errors before its own sweep, as in the
-// block-by-block lazy update, but W is read and written once per level
-// instead of once per block, and the products have K up to d/2.
-// W[:, a+c0 : a+c0+nc] -= E[:, a : a+k] U[a : a+k, a+c0 : ...] (the errors of
-// columns [a, a+k) applied to nc later columns starting c0 after a).
-int sweep_update(const Sweep& s, int a, int k, int c0, int nc, cudaStream_t st) {
+// Column sweep in reversed coordinates.  With P the reversal, U = P V P, so
+// natural column q is reversed column d-1-q and the lazy update of later
+// columns, W[:, c] -= sum_{k < c} E[:, k] U[k][c], reads in reversed order
+//   Wr[:, c'] -= sum_{k' > c'} Er[:, k'] V[k'][c'],
+// a product whose right operand is V^T's block, rows c', columns k', as
+// stored.  The recursion is the factorisation's own: node [o, o+n) sweeps its
+// high part [o1, o+n) first (the earlier natural columns), then updates its low
+// part with Wr[:, o : o1] -= Er[:, o1 : o+n] (V^T[o : o1, o1 : o+n])^T, whose
+// right operand is exactly this node's V21 -- the last inverse step of the
+// node, which can therefore still be running while the high part is swept.
+// W[:, k0..] reversed: Wr[:, c0 : c0+nc] -= Er[:, k0 : k0+k] V^T[c0 : c0+nc, k0 : k0+k]^T.
+int sweep_update(const Sweep& s, int k0, int k, int c0, int nc, cudaStream_t st) {
     const long long d = s.d;
     umma::GemmOut o{};
-    o.C = s.W + a + c0; o.ldc = d;
-    o.Cin = s.W + a + c0; o.ldcin = d;
+    o.C = s.Wr + c0; o.ldc = d;
+    o.Cin = s.Wr + c0; o.ldcin = d;
     o.alpha = -1.0f; o.beta = 1.0f;
-    return umma::gemm_nt(umma::kTF32x3, {s.E_hi + a, s.E_lo + a, d},
-                         {s.Ut_hi + (a + c0) * d + a, s.Ut_lo + (a + c0) * d + a, d}, s.r, nc, k, o, st);
+    return umma::gemm_nt(umma::kTF32x3, {s.E_hi + k0, s.E_lo + k0, d},
+                         {s.VT_hi + c0 * d + k0, s.VT_lo + c0 * d + k0, d}, s.r, nc, k, o, st);
 }
 
-// pend: the parent's look-ahead update of this range's right half (columns
-// a + half_blocks(n) ..) is still running on s.ahead; null when complete.
-int sweep(const Sweep& s, int a, int n, cudaStream_t st, int depth, cudaEvent_t pend) {
-    const long long d = s.d;
+// pend: the parent's look-ahead update of this node's low part (reversed
+// columns o .. o + half_blocks(n)) is still running on s.ahead; null when complete.
+int sweep(const Sweep& s, int o, int n, cudaStream_t st, int depth, cudaEvent_t pend) {
     if (n == kB) {
         const cudaError_t e = launch_pdl(inblock_kernel, dim3((s.r + kIbRows - 1) / kIbRows), dim3(kIbThreads), kIbSmem,
-                                         st, s.W, s.r, s.d,
-                                         a, s.Ut, s.n_keep, s.mask, s.E_hi, s.E_lo, d);
+                                         st, s.W, static_cast<const float*>(s.Wr), s.r, s.d, s.d - o - kB, s.V,
+                                         s.n_keep, s.mask, s.E_hi, s.E_lo, static_cast<long long>(s.d));
         return e == cudaSuccess ? check_launch("inblock_kernel") : cuda_fail(e, "inblock_kernel launch");
     }
-    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
-    int rc = sweep(s, a, n1, st, depth + 1, nullptr);
-    if (!rc) rc = wait_on(st, pend);  // the right half has all earlier errors applied
+    const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1, o1 = o + n1;
+    int rc = sweep(s, o1, n2, st, depth + 1, nullptr);
+    if (!rc) rc = wait_on(st, pend);          // the low part has all earlier errors applied
+    // This node's V21 exists.  evv[depth] holds the record of the last node of
+    // this depth in the factorisation's post-order, the rightmost one, which is
+    // also the first node of this depth that the sweep (high parts first)
+    // reaches; every other node of the depth recorded earlier on the same
+    // stream, so one wait per depth covers them all.
+    if (!rc && !s.evv_waited[depth]) {
+        rc = wait_on(st, s.evv[depth]);
+        s.evv_waited[depth] = true;
+    }
     if (rc) return rc;
-    if (n2 >= kLookAhead && depth < kMaxDepth) {
-        // Look-ahead: the part of the right half that the child sweeps first is
-        // updated on st, the rest on s.ahead (ordered after the parent's piece
-        // there), and the child waits for it before its own update of it.
-        const int h1 = static_cast<int>(half_blocks(n2));
+    if (n1 >= kLookAhead && depth < kMaxDepth) {
+        // Look-ahead: the part of the low half that the child sweeps first (its
+        // high part) is updated on st, the rest on s.ahead (ordered after the
+        // parent's piece there), and the child waits for it before its own
+        // update of it.
+        const int h = static_cast<int>(half_blocks(n1));
         if ((rc = record_on(s.evl, st))) return rc;
         if ((rc = wait_on(s.ahead, s.evl))) return rc;
-        if ((rc = sweep_update(s, a, n1, n1 + h1, n2 - h1, s.ahead))) return rc;
+        if ((rc = sweep_update(s, o1, n2, o, h, s.ahead))) return rc;
         if ((rc = record_on(s.ev[depth], s.ahead))) return rc;
-        if ((rc = sweep_update(s, a, n1, n1, h1, st))) return rc;
-        return sweep(s, a + n1, n2, st, depth + 1, s.ev[depth]);
+        if ((rc = sweep_update(s, o1, n2, o + h, n1 - h, st))) return rc;
+        return sweep(s, o, n1, st, depth + 1, s.ev[depth]);
     }
-    if ((rc = sweep_update(s, a, n1, n1, n2, st))) return rc;
-    return sweep(s, a + n1, n2, st, depth + 1, nullptr);
+    if ((rc = sweep_update(s, o1, n2, o, n1, st))) return rc;
+    return sweep(s, o, n1, st, depth + 1, nullptr);
 }
 
 }  // namespace
@@ -832,7 +859,6 @@ int sweep(const Sweep& s, int a, int n, cudaStream_t st, int depth, cudaEvent_t 
 __global__ void split2d_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo, int rows,
                                int cols, long long ld) {
     pdl_wait();
-    pdl_trigger();
     const size_t total = static_cast<size_t>(rows) * cols;
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
         const size_t g = (e / cols) * ld + e % cols;
@@ -861,7 +887,8 @@ struct Workspace {
     size_t floats = 0;
     cudaStream_t side = nullptr, ahead = nullptr, chain = nullptr;
     cudaEvent_t ev = nullptr, join = nullptr, evl = nullptr, join_ahead = nullptr, fork = nullptr, done = nullptr;
-    cudaEvent_t ev21[kMaxDepth] = {}, ev22[kMaxDepth] = {};
+    cudaEvent_t wcopy = nullptr;
+    cudaEvent_t ev21[kMaxDepth] = {}, ev22[kMaxDepth] = {}, evv[kMaxDepth] = {};
 };
 std::mutex g_ws_mu;
 std::vector<Workspace> g_ws;
@@ -887,12 +914,13 @@ int workspace(size_t floats, Workspace* out) {
         if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&x.chain, cudaStreamNonBlocking, greatest);
         if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&x.side, cudaStreamNonBlocking, least);
         if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&x.ahead, cudaStreamNonBlocking, least);
-        cudaEvent_t* evs[] = {&x.ev, &x.join, &x.evl, &x.join_ahead, &x.fork, &x.done};
+        cudaEvent_t* evs[] = {&x.ev, &x.join, &x.evl, &x.join_ahead, &x.fork, &x.done, &x.wcopy};
         for (cudaEvent_t* p : evs)
             if (e == cudaSuccess) e = cudaEventCreateWithFlags(p, cudaEventDisableTiming);
         for (int k = 0; k < kMaxDepth && e == cudaSuccess; ++k) {
             e = cudaEventCreateWithFlags(&x.ev21[k], cudaEventDisableTiming);
             if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.ev22[k], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.evv[k], cudaEventDisableTiming);
         }
         if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt stream/event setup");
         g_ws.push_back(x);
@@ -928,6 +956,7 @@ extern "C" int tb_obs_hessian_scaled(const void* xt, int d, int n, float scale, 
     if (!xt || !H) return fail(TB_ERR_ARG, "tb_obs_hessian: null pointer");
     int rc = require_device(nullptr);
     if (rc) return rc;
+    pdl_fence(static_cast<cudaStream_t>(stream));  // the caller may have queued a cross-stream wait
     umma::GemmOut o{};
     o.C = H; o.ldc = d;
     o.alpha = scale;
@@ -949,13 +978,14 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     const size_t rd = static_cast<size_t>(r) * d;
     // Workspace: 9 d x d FP32 matrices (A, V, V^T with their splits), the
     // inverse steps' temporaries T (one per recursion depth, with split;
-    // about d^2/3 in all), the error matrix E (r x d, with split) and two scalars.
+    // about d^2/3 in all), the error matrix E (r x d, with split), the
+    // column-reversed copy of W (r x d) and two scalars.
     size_t tneed[kMaxDepth] = {};
     trtri_sizes(d, 0, tneed);
     size_t tsum = 0;
     for (size_t x : tneed) tsum += (x + 63) / 64 * 64;  // keep each buffer 256-byte aligned
     Workspace wsp;
-    const size_t ws_floats = 9 * dd + 2 * tsum + 2 * rd + 64;
+    const size_t ws_floats = 9 * dd + 2 * tsum + 3 * rd + 64;
     if ((rc = workspace(ws_floats, &wsp))) return rc;
     float* ws = wsp.ptr;
     cudaError_t e = cudaSuccess;
@@ -964,7 +994,11 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     const cudaStream_t st = wsp.chain;
     e = cudaEventRecord(wsp.fork, user);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(wsp.ahead, wsp.fork, 0);
     if (e != cudaSuccess) return cuda_fail(e, "tb_obs_sparsegpt stream fork");
+    pdl_fence(st);
+    pdl_fence(wsp.ahead);
+    pdl_fence(wsp.side);  // its first launch follows the previous call's last one
     Work w{};
     w.d = d;
     w.side = wsp.side;
@@ -974,6 +1008,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     for (int k = 0; k < kMaxDepth; ++k) {
         w.ev21[k] = wsp.ev21[k];
         w.ev22[k] = wsp.ev22[k];
+        w.evv[k] = wsp.evv[k];
     }
     w.A = ws; w.A_hi = ws + dd; w.A_lo = ws + 2 * dd;
     w.V = ws + 3 * dd; w.V_hi = ws + 4 * dd; w.V_lo = ws + 5 * dd;
@@ -987,7 +1022,8 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     }
     float* E_hi = tp;
     float* E_lo = E_hi + rd;
-    double* dsum = reinterpret_cast<double*>(E_lo + rd);
+    float* Wr = E_lo + rd;
+    double* dsum = reinterpret_cast<double*>(Wr + rd);
     w.bad = reinterpret_cast<int*>(dsum + 1);
     e = cudaFuncSetAttribute(base_chol_inv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kBaseSmem));
@@ -1005,32 +1041,34 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
                        w.VT_hi, w.VT_lo, d);
         rc = e == cudaSuccess ? check_launch("zero_adjacent_kernel") : cuda_fail(e, "zero_adjacent_kernel launch");
     }
+    if (!rc) {  // the sweep's reversed copy of W, on the look-ahead stream while the factorisation starts
+        e = launch_pdl(reverse_columns_kernel, dim3(148 * 8), dim3(256), 0, w.ahead, static_cast<const float*>(W), Wr,
+                       r, d);
+        if (e == cudaSuccess) e = cudaEventRecord(wsp.wcopy, w.ahead);
+        rc = e == cudaSuccess ? check_launch("reverse_columns_kernel") : cuda_fail(e, "reverse_columns launch");
+    }
     if (!rc) rc = chol(w, 0, d, st, 0, Pending{});
+    // The sweep starts as soon as the last 128-block is factored: it waits for
+    // each node's last inverse step only where it reads that node's V21.
+    if (!rc) rc = wait_on(st, wsp.wcopy);
+    bool evv_waited[kMaxDepth] = {};
+    if (!rc)
+        rc = sweep(Sweep{W, Wr, r, d, n_keep, w.V, w.VT_hi, w.VT_lo, mask, E_hi, E_lo, w.ahead, w.evl, w.ev21, w.evv,
+                         evv_waited},
+                   0, d, st, 0, nullptr);
     // join: the inverse steps (side) and look-ahead updates (ahead) finish
-    // before anything reads V or the next call reuses the workspace
+    // before anything reads V or the next call reuses the workspace (also on errors)
     e = cudaEventRecord(wsp.join, w.side);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.join, 0);
     if (e == cudaSuccess) e = cudaEventRecord(wsp.join_ahead, w.ahead);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.join_ahead, 0);
     if (e != cudaSuccess && !rc) rc = cuda_fail(e, "tb_obs_sparsegpt stream join");
-    // Ut (lower) = (P V P)^T into A's buffers (A is no longer needed).
-    float *Ut = w.A, *Ut_hi = w.A_hi, *Ut_lo = w.A_lo;
-    if (!rc) {
-        e = launch_pdl(reverse_transpose_kernel, dim3(d / 32, d / 32), dim3(32, 8), 0, st,
-                       static_cast<const float*>(w.V), d, Ut, Ut_hi, Ut_lo);
-        rc = e == cudaSuccess ? check_launch("reverse_transpose_kernel") : cuda_fail(e, "reverse_transpose launch");
-    }
-    if (!rc) rc = sweep(Sweep{W, r, d, n_keep, Ut, Ut_hi, Ut_lo, mask, E_hi, E_lo, w.ahead, w.evl, w.ev21}, 0, d, st, 0,
-                        nullptr);
-    if (!rc) {  // the look-ahead updates are all consumed by later steps; join anyway
-        e = cudaEventRecord(wsp.join_ahead, w.ahead);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, wsp.join_ahead, 0);
-        if (e != cudaSuccess) rc = cuda_fail(e, "tb_obs_sparsegpt stream join");
-    }
+    pdl_fence(st);
     int bad = 0;
     if (!rc && ut_out) {
-        e = cudaMemcpyAsync(ut_out, Ut, dd * sizeof(float), cudaMemcpyDeviceToDevice, st);
-        if (e != cudaSuccess) rc = cuda_fail(e, "tb_obs_sparsegpt Ut copy");
+        e = launch_pdl(reverse_transpose_kernel, dim3(d / 32, d / 32), dim3(32, 8), 0, st,
+                       static_cast<const float*>(w.V), d, ut_out);
+        rc = e == cudaSuccess ? check_launch("reverse_transpose_kernel") : cuda_fail(e, "reverse_transpose launch");
     }
     // join the chain stream back into the caller's stream (also on errors)
     e = cudaEventRecord(wsp.done, st);

@@ -274,7 +274,6 @@ gemm_nt_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ 
     // Everything above touched no global memory; the operands and outputs may
     // belong to the kernel before this one in the stream.
     pdl_wait();
-    pdl_trigger();
     // stage layout: A hi, B hi, A lo, B lo (op 0..3)
     auto tile = [&](int s, int op) {
         return smem_u32(smem + s * kStageBytes + (op >> 1) * (kABytes + kBBytes) + (op & 1) * kABytes);
@@ -515,7 +514,6 @@ gemm_nt_pair_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_consta
     fence_after();
     const uint32_t tmem = *tmem_slot;
     pdl_wait();
-    pdl_trigger();
     auto a_tile = [&](int s, int lo) { return smem_u32(smem + s * P::kStage + lo * kPairA); };
     auto b_tile = [&](int s, int lo) { return smem_u32(smem + s * P::kStage + P::kParts * kPairA + lo * P::kB); };
 
@@ -709,7 +707,7 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
     at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
+    at[1].val.programmaticStreamSerializationAllowed = pdl_allowed(st) ? 1 : 0;
     cfg.attrs = at;
     cfg.numAttrs = 2;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_nt_pair_kernel<KIND, NB>, a0, a1, b0, b1, nk, out);
@@ -821,6 +819,7 @@ extern "C" int tb_gemm_nt_tf32x3(const float* a_hi, const float* a_lo, long long
                                  const float* b_lo, long long ldb, int M, int N, int K, float alpha, float beta,
                                  const float* c_in, long long ldcin, float* c, long long ldc, int lower_only,
                                  void* stream) {
+    pdl_fence(static_cast<cudaStream_t>(stream));  // the caller may have queued a cross-stream wait
     int rc = require_device(nullptr);
     if (rc) return rc;
     umma::GemmOut o{};
@@ -838,6 +837,7 @@ extern "C" int tb_gemm_nt_tf32x3(const float* a_hi, const float* a_lo, long long
 extern "C" int tb_gemm_nt_bf16(const void* a, long long lda, const void* b, long long ldb, int M, int N, int K,
                                float alpha, float beta, const float* c_in, long long ldcin, float* c, long long ldc,
                                int lower_only, void* stream) {
+    pdl_fence(static_cast<cudaStream_t>(stream));  // the caller may have queued a cross-stream wait
     int rc = require_device(nullptr);
     if (rc) return rc;
     umma::GemmOut o{};
