@@ -36,8 +36,6 @@
 
 namespace tb {
 
-int tb_split_tf32_2d(const float* x, float* hi, float* lo, int rows, int cols, long long ld, cudaStream_t st);
-
 namespace {
 
 constexpr int kB = 128;  // diagonal / column block
@@ -304,12 +302,11 @@ __device__ __forceinline__ void v_row_finish(float* sV, float* sVT, const float*
 // product with V_ii during step i+1; the last row after the loop).  Every
 // product is written as rows times rows (V^T and S^T are kept for that), each
 // thread computing four rows of one column.
-// Writes L (lower part of A), V with its split (zeros above the diagonal) and
-// V^T with its split (zeros below), all over the full 128 x 128 block.
-__global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __restrict__ A, float* __restrict__ V,
+// Writes the tf32 split of V (zeros above the diagonal) and of V^T (zeros
+// below), all over the full 128 x 128 block; V itself is V_hi + V_lo exactly.
+__global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(const float* __restrict__ A,
                                                                      float* __restrict__ V_hi,
                                                                      float* __restrict__ V_lo,
-                                                                     float* __restrict__ VT,
                                                                      float* __restrict__ VT_hi,
                                                                      float* __restrict__ VT_lo, int ld, int off,
                                                                      int* __restrict__ bad) {
@@ -325,12 +322,27 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
     const size_t base = static_cast<size_t>(off) * ld + off;
     pdl_wait();
     if (t == 0) *sReady = 0;
-#pragma unroll 4
-    for (int e = t; e < kB * kB; e += kBaseThreads) {
-        const int i = e >> 7, j = e & 127;
-        sA[i * kP + j] = (j <= i) ? A[base + static_cast<size_t>(i) * ld + j] : 0.0f;
-        sV[i * kP + j] = 0.0f;
-        sVT[i * kP + j] = 0.0f;
+    {  // the lower triangle of the block, eight 16-byte loads in flight per thread
+        constexpr int kChunks = kB * kB / 4 / kBaseThreads;
+        float4 v[kChunks];
+#pragma unroll
+        for (int u = 0; u < kChunks; ++u) {
+            const int c = t + u * kBaseThreads, i = c >> 5, j0 = 4 * (c & 31);
+            v[u] = j0 <= i ? *reinterpret_cast<const float4*>(A + base + static_cast<size_t>(i) * ld + j0)
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < kChunks; ++u) {
+            const int c = t + u * kBaseThreads, i = c >> 5, j0 = 4 * (c & 31);
+            float4 x = v[u];
+            if (j0 + 1 > i) x.y = 0.0f;
+            if (j0 + 2 > i) x.z = 0.0f;
+            if (j0 + 3 > i) x.w = 0.0f;
+            *reinterpret_cast<float4*>(sA + i * kP + j0) = x;
+            *reinterpret_cast<float4*>(sV + i * kP + j0) = z;
+            *reinterpret_cast<float4*>(sVT + i * kP + j0) = z;
+        }
     }
     __syncthreads();
 #pragma unroll 1
@@ -374,33 +386,35 @@ __global__ void __launch_bounds__(kBaseThreads) base_chol_inv_kernel(float* __re
     // the last block row of V (its S was formed during the last diagonal step)
     v_row_finish(sV, sVT, sST, 3, warp, kBaseWarps, lane);
     __syncthreads();
-    // Write-out: V in FP32 (the final transpose reads it) with its split, and
-    // the split of V^T.  The factor of this block is not written back: after
-    // its diagonal block is factored nothing reads it (the triangular solves
-    // use V_cc, the inverse steps only off-diagonal blocks of L).
-#pragma unroll 2
-    for (int e = t; e < kB * kB; e += kBaseThreads) {
-        const int i = e >> 7, j = e & 127;
-        const size_t g = base + static_cast<size_t>(i) * ld + j;
-        const float v = sV[i * kP + j];
-        const float h = tf32_round(v);
-        V[g] = v;
-        V_hi[g] = h;
-        V_lo[g] = v - h;
-        const float vt = sVT[i * kP + j];
-        const float ht = tf32_round(vt);
-        VT_hi[g] = ht;
-        VT_lo[g] = vt - ht;
+    // Write-out: the splits of V and V^T, 16 bytes per store.  The factor of
+    // this block is not written back: after its diagonal block is factored
+    // nothing reads it (the triangular solves use V_cc, the inverse steps only
+    // off-diagonal blocks of L).
+#pragma unroll 4
+    for (int c = t; c < kB * kB / 4; c += kBaseThreads) {
+        const int i = c >> 5, j0 = 4 * (c & 31);
+        const size_t g = base + static_cast<size_t>(i) * ld + j0;
+        const float4 v = *reinterpret_cast<const float4*>(sV + i * kP + j0);
+        const float4 vt = *reinterpret_cast<const float4*>(sVT + i * kP + j0);
+        float4 h, l, ht, lt;
+        h.x = tf32_round(v.x); l.x = v.x - h.x;  ht.x = tf32_round(vt.x); lt.x = vt.x - ht.x;
+        h.y = tf32_round(v.y); l.y = v.y - h.y;  ht.y = tf32_round(vt.y); lt.y = vt.y - ht.y;
+        h.z = tf32_round(v.z); l.z = v.z - h.z;  ht.z = tf32_round(vt.z); lt.z = vt.z - ht.z;
+        h.w = tf32_round(v.w); l.w = v.w - h.w;  ht.w = tf32_round(vt.w); lt.w = vt.w - ht.w;
+        *reinterpret_cast<float4*>(V_hi + g) = h;
+        *reinterpret_cast<float4*>(V_lo + g) = l;
+        *reinterpret_cast<float4*>(VT_hi + g) = ht;
+        *reinterpret_cast<float4*>(VT_lo + g) = lt;
     }
 }
 
-// Zeroes the 128-blocks next to the diagonal that no other step writes: V's
-// block right of each diagonal block and V^T's block below it (with their
-// splits).  The inverse steps' CTA-pair products read one 128-block past the
-// triangle there.  One CTA per (block, row) pair, off the critical path.
-__global__ void __launch_bounds__(256) zero_adjacent_kernel(float* __restrict__ V, float* __restrict__ V_hi,
-                                                            float* __restrict__ V_lo, float* __restrict__ VT_hi,
-                                                            float* __restrict__ VT_lo, int d) {
+// Zeroes the 128-blocks next to the diagonal that no other step writes: the
+// split of V's block right of each diagonal block and of V^T's block below it.
+// The inverse steps' CTA-pair products read one 128-block past the triangle
+// there.  One CTA per (block, row) pair, off the critical path.
+__global__ void __launch_bounds__(256) zero_adjacent_kernel(float* __restrict__ V_hi, float* __restrict__ V_lo,
+                                                            float* __restrict__ VT_hi, float* __restrict__ VT_lo,
+                                                            int d) {
     pdl_wait();
     const int blk = blockIdx.y;  // diagonal block index, 0 .. d/128 - 2
     const size_t off = static_cast<size_t>(blk) * kB;
@@ -408,7 +422,7 @@ __global__ void __launch_bounds__(256) zero_adjacent_kernel(float* __restrict__ 
         const int i = e >> 7, j = e & 127;
         const size_t gr = (off + i) * d + off + kB + j;  // V[off+i][off+128+j]
         const size_t gb = (off + kB + i) * d + off + j;  // V^T[off+128+i][off+j]
-        V[gr] = 0.0f; V_hi[gr] = 0.0f; V_lo[gr] = 0.0f;
+        V_hi[gr] = 0.0f; V_lo[gr] = 0.0f;
         VT_hi[gb] = 0.0f; VT_lo[gb] = 0.0f;
     }
 }
@@ -416,14 +430,16 @@ constexpr size_t kBaseSmem = (3 * kB * kP + 3 * 32 * kSP + 32 * 32 + 32 + 4) * s
 
 // Ut = (P V P)^T on the lower triangle: Ut[i][j] = V[d-1-j][d-1-i] (the
 // factor U = chol(H^-1) transposed, for callers that ask for it).
-__global__ void reverse_transpose_kernel(const float* __restrict__ V, int d, float* __restrict__ Ut) {
+__global__ void reverse_transpose_kernel(const float* __restrict__ V_hi, const float* __restrict__ V_lo, int d,
+                                         float* __restrict__ Ut) {
     __shared__ float tile[32][33];
     const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // output tile (rows by.., cols bx..)
     pdl_wait();
     // source rows d-1-(bx+..), cols d-1-(by+..)
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
         const int sr = d - 1 - (bx + k), sc = d - 1 - (by + threadIdx.x);
-        tile[k][threadIdx.x] = V[static_cast<size_t>(sr) * d + sc];
+        const size_t g = static_cast<size_t>(sr) * d + sc;
+        tile[k][threadIdx.x] = V_hi[g] + V_lo[g];
     }
     __syncthreads();
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
@@ -491,8 +507,9 @@ __device__ __forceinline__ void obs_group_solve(float (&w)[4], float (&e)[4], ui
 }
 
 __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, const float* __restrict__ Wr,
-                                                             int r, int d, int i1, const float* __restrict__ V,
-                                                             int n_keep, uint8_t* __restrict__ mask,
+                                                             int r, int d, int i1, const float* __restrict__ V_hi,
+                                                             const float* __restrict__ V_lo, int n_keep,
+                                                             uint8_t* __restrict__ mask,
                                                              float* __restrict__ E_hi, float* __restrict__ E_lo,
                                                              long long ldE) {
     extern __shared__ float u1[];
@@ -500,18 +517,30 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
     const int o = d - i1 - kB;  // the block's first column in reversed order
     pdl_wait();
     // U[q][j] = V[o+vr][o+vc] with q = 127-vr, j = 127-vc (j >= q, i.e. vc <= vr),
-    // read along V's rows, sixteen loads in flight per thread
-    for (int b = threadIdx.x; b < kB * kB; b += kIbThreads * 16) {
-        float v[16];
+    // V = V_hi + V_lo (exact), read along V's rows 16 bytes at a time, ten
+    // loads of each part in flight per thread
+    constexpr int kIbChunks = (kB * kB / 4 + kIbThreads - 1) / kIbThreads;
+    {
+        float4 vh[kIbChunks], vl[kIbChunks];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const int e = b + u * kIbThreads, vc = e & 127, vr = e >> 7;
-            v[u] = (e < kB * kB && vc <= vr) ? V[static_cast<size_t>(o + vr) * d + o + vc] : 0.0f;
+        for (int u = 0; u < kIbChunks; ++u) {
+            const int c = threadIdx.x + u * kIbThreads, vr = c >> 5, vc0 = 4 * (c & 31);
+            const bool in = c < kB * kB / 4 && vc0 <= vr;
+            const size_t g = static_cast<size_t>(o + vr) * d + o + vc0;
+            vh[u] = in ? *reinterpret_cast<const float4*>(V_hi + g) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            vl[u] = in ? *reinterpret_cast<const float4*>(V_lo + g) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const int e = b + u * kIbThreads, j = 127 - (e & 127), q = 127 - (e >> 7);
-            if (e < kB * kB) u1[q * kU1 + (j & 3) * 32 + (j >> 2)] = v[u];
+        for (int u = 0; u < kIbChunks; ++u) {
+            const int c = threadIdx.x + u * kIbThreads, vr = c >> 5, vc0 = 4 * (c & 31);
+            if (c >= kB * kB / 4) continue;
+            const float x[4] = {vh[u].x + vl[u].x, vh[u].y + vl[u].y, vh[u].z + vl[u].z, vh[u].w + vl[u].w};
+            const int q = 127 - vr;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int vc = vc0 + k, j = 127 - vc;
+                u1[q * kU1 + (j & 3) * 32 + (j >> 2)] = vc <= vr ? x[k] : 0.0f;
+            }
         }
     }
     __syncthreads();
@@ -601,7 +630,7 @@ constexpr int kMaxDepth = 16;
 constexpr int kLookAhead = 1024;  // split the Schur update of nodes whose A22 is at least this wide
 
 struct Work {
-    float *A, *A_hi, *A_lo, *V, *V_hi, *V_lo, *VT, *VT_hi, *VT_lo;
+    float *A, *A_hi, *A_lo, *V_hi, *V_lo, *VT_hi, *VT_lo;
     float *T_hi[kMaxDepth], *T_lo[kMaxDepth];  // the inverse step's temporary, one per recursion depth
     int d;
     int* bad;
@@ -698,8 +727,9 @@ int record_on(cudaEvent_t ev, cudaStream_t st) {
 //    just before its own solve and update touch those regions.
 int chol(Work& w, int off, int n, cudaStream_t st, int depth, Pending pend) {
     if (n == kB) {
-        const cudaError_t e = launch_pdl(base_chol_inv_kernel, dim3(1), dim3(kBaseThreads), kBaseSmem, st, w.A, w.V,
-                                         w.V_hi, w.V_lo, w.VT, w.VT_hi, w.VT_lo, w.d, off, w.bad);
+        const cudaError_t e = launch_pdl(base_chol_inv_kernel, dim3(1), dim3(kBaseThreads), kBaseSmem, st,
+                                         static_cast<const float*>(w.A), w.V_hi, w.V_lo, w.VT_hi, w.VT_lo, w.d, off,
+                                         w.bad);
         return e == cudaSuccess ? check_launch("base_chol_inv_kernel") : cuda_fail(e, "base_chol_inv_kernel launch");
     }
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
@@ -760,14 +790,11 @@ int trtri_v(Work& w, int off, int n, int depth, cudaStream_t st) {
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1;
     const long long o1 = off + n1;
     umma::GemmOut o{};
-    o.C = at(w.V, o1, off); o.ldc = d;
     o.C_hi = at(w.V_hi, o1, off); o.C_lo = at(w.V_lo, o1, off); o.ld_split = d;
-    o.Ct = at(w.VT, off, o1); o.ldct = d;
+    o.Ct_hi = at(w.VT_hi, off, o1); o.Ct_lo = at(w.VT_lo, off, o1); o.ldct = d;
     o.alpha = -1.0f; o.beta = 0.0f;
     o.tri_a = 2;  // V22 lower
-    int rc = gemm(at(w.V_hi, o1, o1), at(w.V_lo, o1, o1), d, w.T_hi[depth], w.T_lo[depth], n2, n2, n1, n2, o, st);
-    if (rc) return rc;
-    return tb_split_tf32_2d(at(w.VT, off, o1), at(w.VT_hi, off, o1), at(w.VT_lo, off, o1), n1, n2, d, st);
+    return gemm(at(w.V_hi, o1, o1), at(w.V_lo, o1, o1), d, w.T_hi[depth], w.T_lo[depth], n2, n2, n1, n2, o, st);
 }
 
 // Largest n1 x n2 of the inverse steps at each recursion depth (T's size).
@@ -783,7 +810,7 @@ struct Sweep {
     float* W;                        // the caller's weights (final values, natural order)
     float* Wr;                       // working copy, columns reversed
     int r, d, n_keep;
-    const float *V, *VT_hi, *VT_lo;  // L^-1 of the reversed Hessian and its transpose's split
+    const float *V_hi, *V_lo, *VT_hi, *VT_lo;  // split of L^-1 (reversed Hessian) and of its transpose
     uint8_t* mask;
     float *E_hi, *E_lo;              // r x d errors, columns reversed, pitch d
     cudaStream_t ahead;              // look-ahead updates
@@ -819,8 +846,8 @@ int sweep_update(const Sweep& s, int k0, int k, int c0, int nc, cudaStream_t st)
 int sweep(const Sweep& s, int o, int n, cudaStream_t st, int depth, cudaEvent_t pend) {
     if (n == kB) {
         const cudaError_t e = launch_pdl(inblock_kernel, dim3((s.r + kIbRows - 1) / kIbRows), dim3(kIbThreads), kIbSmem,
-                                         st, s.W, static_cast<const float*>(s.Wr), s.r, s.d, s.d - o - kB, s.V,
-                                         s.n_keep, s.mask, s.E_hi, s.E_lo, static_cast<long long>(s.d));
+                                         st, s.W, static_cast<const float*>(s.Wr), s.r, s.d, s.d - o - kB, s.V_hi,
+                                         s.V_lo, s.n_keep, s.mask, s.E_hi, s.E_lo, static_cast<long long>(s.d));
         return e == cudaSuccess ? check_launch("inblock_kernel") : cuda_fail(e, "inblock_kernel launch");
     }
     const int n1 = static_cast<int>(half_blocks(n)), n2 = n - n1, o1 = o + n1;
@@ -854,27 +881,6 @@ int sweep(const Sweep& s, int o, int n, cudaStream_t st, int depth, cudaEvent_t 
 }
 
 }  // namespace
-
-// Strided 2-D tf32 split (rows x cols block with leading dimension ld).
-__global__ void split2d_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo, int rows,
-                               int cols, long long ld) {
-    pdl_wait();
-    const size_t total = static_cast<size_t>(rows) * cols;
-    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-        const size_t g = (e / cols) * ld + e % cols;
-        const float v = x[g];
-        const float h = tf32_round(v);
-        hi[g] = h;
-        lo[g] = v - h;
-    }
-}
-
-int tb_split_tf32_2d(const float* x, float* hi, float* lo, int rows, int cols, long long ld, cudaStream_t st) {
-    const size_t total = static_cast<size_t>(rows) * cols;
-    const unsigned grid = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 148u * 16u));
-    const cudaError_t e = launch_pdl(split2d_kernel, dim3(grid), dim3(256), 0, st, x, hi, lo, rows, cols, ld);
-    return e == cudaSuccess ? check_launch("split2d_kernel") : cuda_fail(e, "split2d_kernel launch");
-}
 
 namespace {
 
@@ -976,7 +982,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     const auto user = static_cast<cudaStream_t>(stream);
     const size_t dd = static_cast<size_t>(d) * d;
     const size_t rd = static_cast<size_t>(r) * d;
-    // Workspace: 9 d x d FP32 matrices (A, V, V^T with their splits), the
+    // Workspace: 7 d x d FP32 matrices (A with its split, the splits of V and V^T), the
     // inverse steps' temporaries T (one per recursion depth, with split;
     // about d^2/3 in all), the error matrix E (r x d, with split), the
     // column-reversed copy of W (r x d) and two scalars.
@@ -985,7 +991,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     size_t tsum = 0;
     for (size_t x : tneed) tsum += (x + 63) / 64 * 64;  // keep each buffer 256-byte aligned
     Workspace wsp;
-    const size_t ws_floats = 9 * dd + 2 * tsum + 3 * rd + 64;
+    const size_t ws_floats = 7 * dd + 2 * tsum + 3 * rd + 64;
     if ((rc = workspace(ws_floats, &wsp))) return rc;
     float* ws = wsp.ptr;
     cudaError_t e = cudaSuccess;
@@ -1011,9 +1017,9 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
         w.evv[k] = wsp.evv[k];
     }
     w.A = ws; w.A_hi = ws + dd; w.A_lo = ws + 2 * dd;
-    w.V = ws + 3 * dd; w.V_hi = ws + 4 * dd; w.V_lo = ws + 5 * dd;
-    w.VT = ws + 6 * dd; w.VT_hi = ws + 7 * dd; w.VT_lo = ws + 8 * dd;
-    float* tp = ws + 9 * dd;
+    w.V_hi = ws + 3 * dd; w.V_lo = ws + 4 * dd;
+    w.VT_hi = ws + 5 * dd; w.VT_lo = ws + 6 * dd;
+    float* tp = ws + 7 * dd;
     for (int k = 0; k < kMaxDepth; ++k) {
         const size_t sz = (tneed[k] + 63) / 64 * 64;
         w.T_hi[k] = tp;
@@ -1037,7 +1043,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
                        static_cast<const double*>(dsum), damp_frac, w.A, w.A_hi, w.A_lo);
     rc = e == cudaSuccess ? check_launch("hessian prep") : cuda_fail(e, "hessian prep launch");
     if (!rc && d > kB) {  // on the side stream, ahead of every inverse step there
-        e = launch_pdl(zero_adjacent_kernel, dim3(16, d / kB - 1), dim3(256), 0, w.side, w.V, w.V_hi, w.V_lo,
+        e = launch_pdl(zero_adjacent_kernel, dim3(16, d / kB - 1), dim3(256), 0, w.side, w.V_hi, w.V_lo,
                        w.VT_hi, w.VT_lo, d);
         rc = e == cudaSuccess ? check_launch("zero_adjacent_kernel") : cuda_fail(e, "zero_adjacent_kernel launch");
     }
@@ -1053,7 +1059,8 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     if (!rc) rc = wait_on(st, wsp.wcopy);
     bool evv_waited[kMaxDepth] = {};
     if (!rc)
-        rc = sweep(Sweep{W, Wr, r, d, n_keep, w.V, w.VT_hi, w.VT_lo, mask, E_hi, E_lo, w.ahead, w.evl, w.ev21, w.evv,
+        rc = sweep(Sweep{W, Wr, r, d, n_keep, w.V_hi, w.V_lo, w.VT_hi, w.VT_lo, mask, E_hi, E_lo, w.ahead, w.evl, w.ev21,
+                         w.evv,
                          evv_waited},
                    0, d, st, 0, nullptr);
     // join: the inverse steps (side) and look-ahead updates (ahead) finish
@@ -1067,7 +1074,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     int bad = 0;
     if (!rc && ut_out) {
         e = launch_pdl(reverse_transpose_kernel, dim3(d / 32, d / 32), dim3(32, 8), 0, st,
-                       static_cast<const float*>(w.V), d, ut_out);
+                       static_cast<const float*>(w.V_hi), static_cast<const float*>(w.V_lo), d, ut_out);
         rc = e == cudaSuccess ? check_launch("reverse_transpose_kernel") : cuda_fail(e, "reverse_transpose launch");
     }
     // join the chain stream back into the caller's stream (also on errors)

@@ -191,20 +191,27 @@ __device__ __forceinline__ void store_rows(const GemmOut& out, const float (&acc
                 *reinterpret_cast<float4*>(out.C_hi + grow * out.ld_split + gcol) = make_float4(h[0], h[1], h[2], h[3]);
                 *reinterpret_cast<float4*>(out.C_lo + grow * out.ld_split + gcol) = make_float4(l[0], l[1], l[2], l[3]);
             }
-            if (out.Ct) *sp = ov;  // final values back for the transposed copy
+            if (out.Ct || out.Ct_hi) *sp = ov;  // final values back for the transposed copy
         }
     }
-    if (out.Ct) {  // Ct[col][row]: lane = row again, 32 consecutive rows per store
+    if (out.Ct || out.Ct_hi) {  // Ct[col][row]: lane = row again, 32 consecutive rows per store
         __syncwarp();
 #pragma unroll 4
         for (int c = 0; c < TN / 4; ++c) {
             const float4 x = *reinterpret_cast<const float4*>(sbuf + lane * kPitch + 4 * c);
+            const float v[4] = {x.x, x.y, x.z, x.w};
             const long long col = col0 + 4 * c;
             const long long row = row0 + lane;
-            out.Ct[(col + 0) * out.ldct + row] = x.x;
-            out.Ct[(col + 1) * out.ldct + row] = x.y;
-            out.Ct[(col + 2) * out.ldct + row] = x.z;
-            out.Ct[(col + 3) * out.ldct + row] = x.w;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const long long g = (col + e) * out.ldct + row;
+                if (out.Ct) out.Ct[g] = v[e];
+                if (out.Ct_hi) {
+                    const float h = tf32_hi(v[e]);
+                    out.Ct_hi[g] = h;
+                    out.Ct_lo[g] = v[e] - h;
+                }
+            }
         }
     }
 }
@@ -729,7 +736,7 @@ int gemm_nt(Kind kind, const Operand& A, const Operand& B, int M, int N, int K, 
     if ((out.C && (!aligned16(out.C) || out.ldc % 4 || out.ldc < N)) ||
         (out.beta != 0.0f && (!out.Cin || !aligned16(out.Cin) || out.ldcin % 4 || out.ldcin < N)) ||
         (out.C_hi && (!out.C_lo || !aligned16(out.C_hi) || !aligned16(out.C_lo) || out.ld_split % 4 || out.ld_split < N)) ||
-        (out.Ct && out.ldct < M))
+        ((out.Ct || out.Ct_hi) && out.ldct < M) || (!out.Ct_hi != !out.Ct_lo))
         return fail(TB_ERR_ARG, "gemm_nt: output pointers must be 16-byte aligned with ld >= N and ld % 4 == 0");
     if (out.tri_a && (out.tri_a > 2 || M != K))
         return fail(TB_ERR_ARG, "gemm_nt: a triangular A must be square (M == K)");

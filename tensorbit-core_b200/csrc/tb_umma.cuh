@@ -41,6 +41,8 @@ struct GemmOut {
     long long ld_split;
     float* Ct;           // optional transposed copy of the output, ldct
     long long ldct;
+    float* Ct_hi;        // optional tf32 hi/lo split of the transposed copy (same ldct)
+    float* Ct_lo;
     float alpha, beta;
     int lower_only;      // compute only tiles with tile_row >= tile_col
     int tri_a;           // A is square and triangular (M == K): 1 = upper, so output tile row
