@@ -205,7 +205,7 @@ int tb_obs_hessian_scaled(const void* xt_bf16, int d, int n, float scale, float*
  * of whole column ranges).  Rows are independent, so a row range of W may be
  * pruned on its own (each rank of a row split passes its rows).  mask gets
  * r*d/4 bytes (bit k = keep column 4g+k, the .tb convention).  ut_out (d x d,
- * may be NULL) receives U^T.  A workspace of 9.5 d^2 + 3 r d floats is
+ * may be NULL) receives U^T.  A workspace of 7.5 d^2 + 3 r d floats is
  * allocated on first use and kept per device for later calls (grow-only;
  * ~8.3 GB at d = 14336, r = 4096), so calls on one device must not overlap;
  * two internal streams per device carry the parts of the factorisation and
