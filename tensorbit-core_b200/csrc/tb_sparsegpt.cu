@@ -449,26 +449,28 @@ __global__ void reverse_transpose_kernel(const float* __restrict__ V_hi, const f
     }
 }
 
-// In-block OBS sweep of columns [i1, i1+128) for every row: one warp per two
-// rows (two independent dependency chains per warp), lane l holding columns
-// 4l..4l+3 of both rows.  The sweep keeps W and the errors in reversed column
-// order (Wr[:, c] = W[:, d-1-c], likewise E), so that the later columns' updates
-// are plain products with V = L^-1 of the reversed Hessian; this kernel reads
-// its block from Wr, writes the block's final weights to W in natural order
-// (no later step touches them), and its errors to E reversed.  Its block of U
-// is U[i1+q][i1+j] = V[o+127-q][o+127-j], o = d-i1-128.  M must be 4 here (the lane's four columns are one
-// group); N:4 with N in {1, 2, 3}.  The block of U sits in shared memory with
-// column j of row q at q*kU1 + (j%4)*32 + j/4, so that the four values a lane
-// needs are bank-conflict free; 1/U_qq follows it.  Only pruned columns carry
-// an error (err = w_q / U_qq; a kept column's error is 0).  Per group, the
-// group's lane selects the mask and eliminates the group's pruned columns in
-// its own registers, then one broadcast round hands their errors to the lanes
-// of the later groups.  Errors go to E (row pitch ldE) at the block's own
-// columns, with their tf32 split.
-constexpr int kU1 = kB + 1;  // pitch of the in-block copy of U
-constexpr int kIbThreads = 448;                     // 14 warps, two rows each: 28 rows per CTA,
-constexpr int kIbRows = 2 * (kIbThreads / 32);      // so 4096 rows fill all 148 SMs
-constexpr size_t kIbSmem = (kB * kU1 + kB) * sizeof(float);
+// In-block OBS sweep of columns [i1, i1+128) for every row.  Eight lanes (an
+// octet) share a row; lane l of the octet holds groups l, l+8, l+16, l+24 of
+// the row (columns 4g..4g+3) in registers, the current one always in slot 0
+// (the slots shift down by one group after every eight groups).  Group g is
+// handled by its owning lane: it selects the mask, eliminates the group's
+// pruned columns inside the group, and hands the pruned columns' errors to
+// the octet by shuffle; every lane then applies them to its own later
+// columns.  Only pruned columns carry an error, so the update runs over
+// exactly the 4 - N pruned ones, in column order, as the sequential sweep
+// does: results are those of the plain row-by-row algorithm.  A finished
+// group (slot 0 after its eight groups) is written out at once.
+// The sweep keeps W and the errors in reversed column order (Wr[:, c] =
+// W[:, d-1-c], likewise E), so that the later columns' updates are plain
+// products with V = L^-1 of the reversed Hessian; this kernel reads its block
+// from Wr, writes the block's final weights to W in natural order (no later
+// step touches them), and its errors to E reversed.  Its block of U is
+// U[i1+q][i1+j] = V[o+127-q][o+127-j], o = d-i1-128, kept in shared memory
+// row by row.  M must be 4 here; N:4 with N in {1, 2, 3}.
+constexpr int kUp = kB + 4;                         // pitch of a row of U in shared memory
+constexpr int kIbThreads = 256;                     // eight warps of four rows: 32 rows per CTA,
+constexpr int kIbRows = 32;                         // so 4096 rows take 128 SMs
+constexpr size_t kIbSmem = (kB * kUp + kB) * sizeof(float);
 
 __device__ __forceinline__ uint32_t obs_keep_bits(const float (&w)[4], const float* rv, int n_keep) {
     float s[4];
@@ -488,24 +490,6 @@ __device__ __forceinline__ uint32_t obs_keep_bits(const float (&w)[4], const flo
     return bits;
 }
 
-// Eliminates the pruned columns of one group inside its lane: for k in order,
-// a pruned column's error x = w_k / U_qq updates the group's later columns.
-__device__ __forceinline__ void obs_group_solve(float (&w)[4], float (&e)[4], uint32_t bits, const float* u1,
-                                                const float* rinv, int g) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int q = 4 * g + k;
-        float x = 0.0f;
-        if (!((bits >> k) & 1u)) {
-            x = w[k] * rinv[q];
-#pragma unroll
-            for (int kk = k + 1; kk < 4; ++kk) w[kk] = fmaf(-x, u1[q * kU1 + kk * 32 + g], w[kk]);
-            w[k] = 0.0f;
-        }
-        e[k] = x;
-    }
-}
-
 __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__ W, const float* __restrict__ Wr,
                                                              int r, int d, int i1, const float* __restrict__ V_hi,
                                                              const float* __restrict__ V_lo, int n_keep,
@@ -513,106 +497,132 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
                                                              float* __restrict__ E_hi, float* __restrict__ E_lo,
                                                              long long ldE) {
     extern __shared__ float u1[];
-    float* rinv = u1 + kB * kU1;
+    float* rinv = u1 + kB * kUp;
     const int o = d - i1 - kB;  // the block's first column in reversed order
     pdl_wait();
     // U[q][j] = V[o+vr][o+vc] with q = 127-vr, j = 127-vc (j >= q, i.e. vc <= vr),
-    // V = V_hi + V_lo (exact), read along V's rows 16 bytes at a time, ten
-    // loads of each part in flight per thread
-    constexpr int kIbChunks = (kB * kB / 4 + kIbThreads - 1) / kIbThreads;
-    {
-        float4 vh[kIbChunks], vl[kIbChunks];
+    // V = V_hi + V_lo (exact), read along V's rows 16 bytes at a time, eight
+    // chunks of each part in flight per thread
+    constexpr int kIbChunks = kB * kB / 4 / kIbThreads;  // 16
+#pragma unroll 1
+    for (int u0 = 0; u0 < kIbChunks; u0 += 8) {
+        float4 h[8], l[8];
 #pragma unroll
-        for (int u = 0; u < kIbChunks; ++u) {
-            const int c = threadIdx.x + u * kIbThreads, vr = c >> 5, vc0 = 4 * (c & 31);
-            const bool in = c < kB * kB / 4 && vc0 <= vr;
+        for (int u = 0; u < 8; ++u) {
+            const int c = threadIdx.x + (u0 + u) * kIbThreads, vr = c >> 5, vc0 = 4 * (c & 31);
             const size_t g = static_cast<size_t>(o + vr) * d + o + vc0;
-            vh[u] = in ? *reinterpret_cast<const float4*>(V_hi + g) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            vl[u] = in ? *reinterpret_cast<const float4*>(V_lo + g) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const bool in = vc0 <= vr;
+            h[u] = in ? *reinterpret_cast<const float4*>(V_hi + g) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            l[u] = in ? *reinterpret_cast<const float4*>(V_lo + g) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
 #pragma unroll
-        for (int u = 0; u < kIbChunks; ++u) {
-            const int c = threadIdx.x + u * kIbThreads, vr = c >> 5, vc0 = 4 * (c & 31);
-            if (c >= kB * kB / 4) continue;
-            const float x[4] = {vh[u].x + vl[u].x, vh[u].y + vl[u].y, vh[u].z + vl[u].z, vh[u].w + vl[u].w};
-            const int q = 127 - vr;
+        for (int u = 0; u < 8; ++u) {
+            const int c = threadIdx.x + (u0 + u) * kIbThreads, vr = c >> 5, vc0 = 4 * (c & 31);
+            const float x[4] = {h[u].x + l[u].x, h[u].y + l[u].y, h[u].z + l[u].z, h[u].w + l[u].w};
+            float* ur = u1 + (127 - vr) * kUp + 127 - vc0;  // U[127-vr][127-vc0-k] = ur[-k]
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int vc = vc0 + k, j = 127 - vc;
-                u1[q * kU1 + (j & 3) * 32 + (j >> 2)] = vc <= vr ? x[k] : 0.0f;
-            }
+            for (int k = 0; k < 4; ++k) ur[-k] = vc0 + k <= vr ? x[k] : 0.0f;
         }
     }
     __syncthreads();
-    if (threadIdx.x < kB) {
-        const int q = threadIdx.x;
-        rinv[q] = __frcp_rn(u1[q * kU1 + (q & 3) * 32 + (q >> 2)]);
-    }
+    if (threadIdx.x < kB) rinv[threadIdx.x] = __frcp_rn(u1[threadIdx.x * kUp + threadIdx.x]);
     __syncthreads();
+
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t row0 = static_cast<size_t>(blockIdx.x) * kIbRows + 2 * warp;
-    if (row0 >= static_cast<size_t>(r)) return;  // r is even: both rows of the warp exist
-    float* wr0 = W + row0 * d + i1;
-    float* wr1 = wr0 + d;
-    float w0[4], w1[4];
-    {  // columns 4l..4l+3 sit reversed in Wr's float4 31-l of the block
-        const float* rr0 = Wr + row0 * d + o;
-        const float4 x = reinterpret_cast<const float4*>(rr0)[31 - lane];
-        const float4 y = reinterpret_cast<const float4*>(rr0 + d)[31 - lane];
-        w0[0] = x.w; w0[1] = x.z; w0[2] = x.y; w0[3] = x.x;
-        w1[0] = y.w; w1[1] = y.z; w1[2] = y.y; w1[3] = y.x;
+    const int ql = lane & 7, oct = lane & ~7;
+    const size_t row = static_cast<size_t>(blockIdx.x) * kIbRows + 4 * warp + (lane >> 3);
+    if (row >= static_cast<size_t>(r)) return;  // r % 128 == 0: whole octets only
+    // slot s (w[4s..4s+3]) = natural columns 4(8s+ql)..+3 = Wr columns o+124-32s-4ql..o+127-32s-4ql
+    float w[16];
+    const float* wsrc = Wr + row * d + o;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const float4 x = *reinterpret_cast<const float4*>(wsrc + 124 - 32 * s - 4 * ql);
+        w[4 * s] = x.w; w[4 * s + 1] = x.z; w[4 * s + 2] = x.y; w[4 * s + 3] = x.x;
     }
-    float e0[4] = {0, 0, 0, 0}, e1[4] = {0, 0, 0, 0};
-    uint32_t own0 = 0, own1 = 0;
-    for (int g = 0; g < kB / 4; ++g) {
-        uint32_t b0 = 0, b1 = 0;
-        if (lane == g) {
-            b0 = obs_keep_bits(w0, rinv + 4 * g, n_keep);
-            b1 = obs_keep_bits(w1, rinv + 4 * g, n_keep);
-            own0 = b0;
-            own1 = b1;
-            obs_group_solve(w0, e0, b0, u1, rinv, g);
-            obs_group_solve(w1, e1, b1, u1, rinv, g);
-        }
-        b0 = __shfl_sync(kFull, b0, g);
-        b1 = __shfl_sync(kFull, b1, g);
-        float x0[4], x1[4];
+    float* wdst = W + row * d + i1;
+    float* ehi = E_hi + row * ldE + o;
+    float* elo = E_lo + row * ldE + o;
+    uint8_t* mrow = mask + (row * d + i1) / 4;
+    const int n_prune = 4 - n_keep;
+#pragma unroll 1
+    for (int m = 0; m < 4; ++m) {  // groups 8m..8m+7; this lane's group 8m+ql sits in slot 0
+        float e_own[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t bits_own = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            x0[k] = __shfl_sync(kFull, e0[k], g);
-            x1[k] = __shfl_sync(kFull, e1[k], g);
-        }
-        if (lane > g) {
+        for (int j = 0; j < 8; ++j) {
+            const int q0 = 4 * (8 * m + j);
+            uint32_t bits = 0;
+            float xp[3] = {0.0f, 0.0f, 0.0f};  // errors of the pruned columns, in column order
+            if (ql == j) {
+                float wg[4] = {w[0], w[1], w[2], w[3]};
+                bits = obs_keep_bits(wg, rinv + q0, n_keep);
+                int p = 0;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (((b0 & b1) >> k) & 1u) continue;  // kept in both rows: no error (warp-uniform)
-                const float* ur = u1 + (4 * g + k) * kU1 + lane;
+                for (int k = 0; k < 4; ++k) {
+                    if (!((bits >> k) & 1u)) {
+                        const float x = wg[k] * rinv[q0 + k];
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const float u = ur[kk * 32];
-                    w0[kk] = fmaf(-x0[k], u, w0[kk]);
-                    w1[kk] = fmaf(-x1[k], u, w1[kk]);
+                        for (int kk = k + 1; kk < 4; ++kk) wg[kk] = fmaf(-x, u1[(q0 + k) * kUp + q0 + kk], wg[kk]);
+                        wg[k] = 0.0f;
+                        e_own[k] = x;
+                        if (p == 0) xp[0] = x;
+                        else if (p == 1) xp[1] = x;
+                        else xp[2] = x;
+                        ++p;
+                    }
+                }
+                w[0] = wg[0]; w[1] = wg[1]; w[2] = wg[2]; w[3] = wg[3];
+                bits_own = bits;
+            }
+            bits = __shfl_sync(kFull, bits, oct | j);
+            xp[0] = __shfl_sync(kFull, xp[0], oct | j);
+            if (n_prune > 1) xp[1] = __shfl_sync(kFull, xp[1], oct | j);
+            if (n_prune > 2) xp[2] = __shfl_sync(kFull, xp[2], oct | j);
+            // pruned column indices inside the group, in order (exactly n_prune
+            // of them unless a score is NaN, which a failed pivot reports anyway)
+            uint32_t rest = ~bits & 0xFu;
+            const int np = min(n_prune, __popc(rest));
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                if (p >= np) break;
+                const int k = __ffs(rest) - 1;
+                rest &= rest - 1;
+                const float x = xp[p];
+                const float* ur = u1 + (q0 + k) * kUp + 4 * ql;
+                if (ql > j) {  // slot 0 lies after the group
+                    const float4 uu = *reinterpret_cast<const float4*>(ur + 32 * m);
+                    w[0] = fmaf(-x, uu.x, w[0]); w[1] = fmaf(-x, uu.y, w[1]);
+                    w[2] = fmaf(-x, uu.z, w[2]); w[3] = fmaf(-x, uu.w, w[3]);
+                }
+#pragma unroll
+                for (int s = 1; s < 4; ++s) {
+                    if (m + s < 4) {
+                        const float4 uu = *reinterpret_cast<const float4*>(ur + 32 * (m + s));
+                        w[4 * s] = fmaf(-x, uu.x, w[4 * s]);
+                        w[4 * s + 1] = fmaf(-x, uu.y, w[4 * s + 1]);
+                        w[4 * s + 2] = fmaf(-x, uu.z, w[4 * s + 2]);
+                        w[4 * s + 3] = fmaf(-x, uu.w, w[4 * s + 3]);
+                    }
                 }
             }
         }
+        // slot 0 is final: natural columns 32m+4ql..+3, errors reversed, the mask byte
+        *reinterpret_cast<float4*>(wdst + 32 * m + 4 * ql) = make_float4(w[0], w[1], w[2], w[3]);
+        float hv[4], lv[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float v = e_own[3 - t];
+            hv[t] = tf32_round(v);
+            lv[t] = v - hv[t];
+        }
+        *reinterpret_cast<float4*>(ehi + 124 - 32 * m - 4 * ql) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<float4*>(elo + 124 - 32 * m - 4 * ql) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+        mrow[8 * m + ql] = static_cast<uint8_t>(bits_own);
+#pragma unroll
+        for (int k = 0; k < 12; ++k) w[k] = w[k + 4];
+        w[12] = w[13] = w[14] = w[15] = 0.0f;
     }
-    reinterpret_cast<float4*>(wr0)[lane] = make_float4(w0[0], w0[1], w0[2], w0[3]);
-    reinterpret_cast<float4*>(wr1)[lane] = make_float4(w1[0], w1[1], w1[2], w1[3]);
-    mask[(row0 * d + i1) / 4 + lane] = static_cast<uint8_t>(own0);
-    mask[((row0 + 1) * d + i1) / 4 + lane] = static_cast<uint8_t>(own1);
-    float4 h, l;  // errors reversed, like Wr
-    h.x = tf32_round(e0[3]); l.x = e0[3] - h.x;
-    h.y = tf32_round(e0[2]); l.y = e0[2] - h.y;
-    h.z = tf32_round(e0[1]); l.z = e0[1] - h.z;
-    h.w = tf32_round(e0[0]); l.w = e0[0] - h.w;
-    reinterpret_cast<float4*>(E_hi + row0 * ldE + o)[31 - lane] = h;
-    reinterpret_cast<float4*>(E_lo + row0 * ldE + o)[31 - lane] = l;
-    h.x = tf32_round(e1[3]); l.x = e1[3] - h.x;
-    h.y = tf32_round(e1[2]); l.y = e1[2] - h.y;
-    h.z = tf32_round(e1[1]); l.z = e1[1] - h.z;
-    h.w = tf32_round(e1[0]); l.w = e1[0] - h.w;
-    reinterpret_cast<float4*>(E_hi + (row0 + 1) * ldE + o)[31 - lane] = h;
-    reinterpret_cast<float4*>(E_lo + (row0 + 1) * ldE + o)[31 - lane] = l;
 }
 
 // Wr[:, c] = W[:, d-1-c] for the sweep (one float4 per thread step).
