@@ -552,25 +552,31 @@ __global__ void __launch_bounds__(kIbThreads) inblock_kernel(float* __restrict__
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int q0 = 4 * (8 * m + j);
+            // the group's 1/U_qq and in-group U entries, loaded by every lane ahead of the branch
+            const float4 rq = *reinterpret_cast<const float4*>(rinv + q0);
+            const float4 ua = *reinterpret_cast<const float4*>(u1 + q0 * kUp + q0);
+            const float4 ub = *reinterpret_cast<const float4*>(u1 + (q0 + 1) * kUp + q0);
+            const float4 uc = *reinterpret_cast<const float4*>(u1 + (q0 + 2) * kUp + q0);
             uint32_t bits = 0;
             float xp[3] = {0.0f, 0.0f, 0.0f};  // errors of the pruned columns, in column order
             if (ql == j) {
+                const float rv[4] = {rq.x, rq.y, rq.z, rq.w};
+                const float ug[3][4] = {{ua.x, ua.y, ua.z, ua.w}, {ub.x, ub.y, ub.z, ub.w}, {uc.x, uc.y, uc.z, uc.w}};
                 float wg[4] = {w[0], w[1], w[2], w[3]};
-                bits = obs_keep_bits(wg, rinv + q0, n_keep);
+                bits = obs_keep_bits(wg, rv, n_keep);
                 int p = 0;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    if (!((bits >> k) & 1u)) {
-                        const float x = wg[k] * rinv[q0 + k];
+                    const bool pruned = !((bits >> k) & 1u);
+                    const float x = pruned ? wg[k] * rv[k] : 0.0f;
 #pragma unroll
-                        for (int kk = k + 1; kk < 4; ++kk) wg[kk] = fmaf(-x, u1[(q0 + k) * kUp + q0 + kk], wg[kk]);
-                        wg[k] = 0.0f;
-                        e_own[k] = x;
-                        if (p == 0) xp[0] = x;
-                        else if (p == 1) xp[1] = x;
-                        else xp[2] = x;
-                        ++p;
-                    }
+                    for (int kk = k + 1; kk < 4; ++kk) wg[kk] = pruned ? fmaf(-x, ug[k][kk], wg[kk]) : wg[kk];
+                    wg[k] = pruned ? 0.0f : wg[k];
+                    e_own[k] = x;
+                    xp[0] = pruned && p == 0 ? x : xp[0];
+                    xp[1] = pruned && p == 1 ? x : xp[1];
+                    xp[2] = pruned && p == 2 ? x : xp[2];
+                    p += pruned ? 1 : 0;
                 }
                 w[0] = wg[0]; w[1] = wg[1]; w[2] = wg[2]; w[3] = wg[3];
                 bits_own = bits;
