@@ -157,30 +157,33 @@ __device__ __noinline__ void diag_factor(float* D, float* Lc, float* rinv, volat
     }
     bool all_ok = true;
     float my_r = 1.0f;
+    float piv = a[0];  // the next pivot, meaningful on the lane of the next column
 #pragma unroll 1
     for (int jb = 0; jb < 32; jb += 4) {
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int j = jb + jj;
-            const float djj = __shfl_sync(kFull, a[jj], j);
+            const float djj = __shfl_sync(kFull, piv, j);
             const bool ok = djj > 0.0f;
             all_ok = all_ok && ok;
             const float rj = ok ? rsqrtf(djj) : 1.0f;
-            // lanes above j hold a[jj] = 0 (upper triangle)
+            // Lanes above the diagonal (lane < j) compute garbage from here on, without
+            // predicates; their entries are never published nor written back.
             const float l = (lane == j) ? (ok ? djj * rj : 1.0f) : a[jj] * rj;
             a[jj] = l;
             if (lane == j) my_r = rj;
-            if (lane == j + 1) a[jj + 1] = fmaf(-l, l, a[jj + 1]);  // next pivot first
+            piv = fmaf(-l, l, a[jj + 1]);  // on lane j + 1: its pivot, ahead of the column's update
             if (lane >= j) Lc[j * 32 + (lane - j)] = l;
             __syncwarp();
             float lc[32];
             load_column(Lc, j, lc);
 #pragma unroll
-            for (int k = 1; k < 32 - jj; ++k)
-                if (lane >= j + k && !(k == 1 && lane == j + 1)) a[jj + k] = fmaf(-l, lc[k], a[jj + k]);
+            for (int k = 1; k < 32 - jj; ++k) a[jj + k] = fmaf(-l, lc[k], a[jj + k]);
         }
         // columns jb..jb+3 are final: L into D (zeros above), 1/L_jj, then publish
-        *reinterpret_cast<float4*>(D + lane * kP + jb) = make_float4(a[0], a[1], a[2], a[3]);
+        *reinterpret_cast<float4*>(D + lane * kP + jb) =
+            make_float4(lane >= jb ? a[0] : 0.0f, lane >= jb + 1 ? a[1] : 0.0f, lane >= jb + 2 ? a[2] : 0.0f,
+                        lane >= jb + 3 ? a[3] : 0.0f);
         if (lane >= jb && lane < jb + 4) rinv[lane] = my_r;
         __threadfence_block();
         __syncwarp();
