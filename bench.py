@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-obs", action="store_true", help="skip the configuration-4 OBS measurement")
+    ap.add_argument("--no-block-obs", action="store_true", help="skip the reference-semantics block OBS timing")
     ap.add_argument("--obs-only", action="store_true", help="only the configuration-4 OBS measurement")
     ap.add_argument("--obs-steps", type=int, default=3)
     ap.add_argument("--obs-shape", type=int, nargs=3, metavar=("R", "D", "N"),
@@ -268,6 +269,11 @@ def run_ours(args):
     if not args.no_obs:
         obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape, dist if world > 1 else None)
 
+    # ---- reference-semantics block OBS (wall time; rank 0, single GPU) ------
+    block_obs = None
+    if rank == 0 and world == 1 and not args.no_block_obs:
+        block_obs = run_block_obs(torch, tb, dev)
+
     # ---- CPU baseline (rank 0, single GPU only) ----------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -303,6 +309,7 @@ def run_ours(args):
             "clocks": clk,
             "e2e": e2e,
             "obs": obs,
+            "block_obs": block_obs,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -480,6 +487,58 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None):
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference's own CPU code (oracle/_ref) or the port
 # ---------------------------------------------------------------------------
+def run_block_obs(torch, tb, dev, passes=3):
+    """tb-prune --strategy BlockOBS on one 4096 x 4096 q_proj (the reference's
+    prune_block_obs semantics: 128-element blocks, Fisher from one gradient
+    sample, four scaled snapshots of it, sparsity 0.5): wall time per tensor,
+    and the reference's own CPU code (one thread, as it runs) on a bounded
+    sample of the same tensor's blocks, per block."""
+    import numpy as np
+    n, block, K = 4096 * 4096, 128, 4
+    gen = torch.Generator(device=dev).manual_seed(77)
+    w0 = torch.randn(n, device=dev, generator=gen) * 0.02
+    g = torch.randn(n, device=dev, generator=gen) * 1e-3
+    F = (g * g) * 0.01
+    hist = [g * (0.9 + 0.02 * k) for k in range(K)]
+    ptrs = (C.c_void_p * K)(*[h.data_ptr() for h in hist])
+    w = torch.empty_like(w0)
+    L = tb.lib()
+    ms = []
+    pruned = C.c_uint64()
+    for k in range(passes + 1):  # the first pass warms up
+        w.copy_(w0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        tb.check(L.tb_block_obs(w.data_ptr(), F.data_ptr(), ptrs, K, n, block, 0.5, 0.01, 0.01, C.byref(pruned),
+                                torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        if k:
+            ms.append((time.perf_counter() - t0) * 1e3)
+    t = statistics.median(ms)
+    out = {"workload": "tb-prune BlockOBS on one 4096x4096 q_proj (FP32 weights), 128-element blocks, Fisher from "
+                       "one gradient sample, 4 scaled snapshots, sparsity 0.5, damping 0.01",
+           "ms_per_tensor": round(t, 2), "passes": passes, "blocks": n // block,
+           "blocks_per_s": round(n / block / (t / 1e3)), "gparams_per_s": round(n / (t / 1e3) / 1e9, 4),
+           "pruned": pruned.value}
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle, ref_available
+    if ref_available():
+        m = 256 * block  # the tensor's first 256 blocks
+        wc = w0[:m].cpu().numpy()
+        gc = g[:m].cpu().numpy()[None, :]
+        hc = np.stack([h[:m].cpu().numpy() for h in hist])
+        o = Oracle("ref")
+        t0 = time.perf_counter()
+        rc, _, _ = o.block_obs(wc, gc, hc, block=block, sparsity=0.5)
+        el = time.perf_counter() - t0
+        assert rc == 0, rc
+        out["cpu_reference"] = {"blocks_per_s": round(256 / el, 1), "cores": 1, "kind": "reference",
+                                "sample": f"the first 256 blocks (32,768 params) of the same tensor, one thread, "
+                                          f"{el:.2f} s",
+                                "ms_per_tensor_extrapolated": round(el / 256 * (n // block) * 1e3)}
+    return out
+
+
 def cpu_sample(torch, dev):
     import numpy as np
     n = 4096 * 4096

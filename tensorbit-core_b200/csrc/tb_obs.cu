@@ -167,6 +167,10 @@ __global__ void __launch_bounds__(kObsThreads) block_obs_kernel(const ObsParams 
     }
     __syncthreads();
 
+    // the rank-1 updates: ung column sets of bs rows each, row ui of set ug
+    const int ung = kObsThreads / bs > 0 ? kObsThreads / bs : 1;
+    const int ui = (t < ung * bs) ? t % bs : -1, ug = (t < ung * bs) ? t / bs : 0;
+    // (bs <= kMaxBlock < kObsThreads, so every row has a thread)
     uint32_t done = 0;
     while (done < target) {
         // argmin_i w_i^2 / H_ii over H_ii > 0, first index on ties
@@ -204,9 +208,13 @@ __global__ void __launch_bounds__(kObsThreads) block_obs_kernel(const ObsParams 
         }
         __syncthreads();
         if (t == 0) wv[best] = 0.0f;
-        for (int e = t; e < bs * bs; e += kObsThreads) {
-            const int i = e % bs, j = e / bs;
-            H[e] = __fsub_rn(H[e], __fdiv_rn(__fmul_rn(col[i], col[j]), hbb));
+        // H -= col col^T / h_bb: thread (row ui, column set ug) walks its columns
+        if (ui >= 0) {
+            const float ci = col[ui];
+            for (int j = ug; j < bs; j += ung) {
+                float* h = H + j * bs + ui;
+                *h = __fsub_rn(*h, __fdiv_rn(__fmul_rn(ci, col[j]), hbb));
+            }
         }
         __syncthreads();
         ++done;
