@@ -57,6 +57,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-obs", action="store_true", help="skip the configuration-4 OBS measurement")
     ap.add_argument("--no-block-obs", action="store_true", help="skip the reference-semantics block OBS timing")
+    ap.add_argument("--no-ties", action="store_true", help="skip the untimed near-tie counting pass")
     ap.add_argument("--obs-only", action="store_true", help="only the configuration-4 OBS measurement")
     ap.add_argument("--obs-steps", type=int, default=3)
     ap.add_argument("--obs-shape", type=int, nargs=3, metavar=("R", "D", "N"),
@@ -257,6 +258,23 @@ def run_ours(args):
     achieved = per_launch_bytes / (kernel_ms / launches / 1e3) / 1e9
     traffic_pp = ncu_traffic_per_param()
 
+    # ---- near-tie groups of the pass (one extra, untimed pass with the counter) --
+    ties = None
+    if not args.no_ties:
+        cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+        for _, a in plan:
+            a.near_ties = cnt.data_ptr()
+            rc = tb.lib().tb_score_mask_pack(C.byref(a), sptr)
+            a.near_ties = None
+            if rc:
+                raise tb.TbError(rc, tb.lib().tb_last_error().decode())
+        torch.cuda.synchronize()
+        groups = PARAMS_PER_STEP // 4
+        ties = {"groups": groups, "near_tie_groups": int(cnt.item()),
+                "rule": "|s(N) - s(N+1)| <= 1e-6 max(|s(N)|, FLT_MIN) among a group's sorted scores; the masks of "
+                        "these groups are bit-exact too (the reference's selection and tie order are reproduced, "
+                        "for top-N through its nth_element tie tables)"}
+
     # ---- end to end through the host-buffer entry point --------------------
     e2e = None
     del sets
@@ -306,6 +324,7 @@ def run_ours(args):
                          "kernel": "fused_vec_kernel<BF16,BF16,M=4>",
                          "kernel_ms_total": round(kernel_ms, 3)},
             "gpu_launches": launches,
+            "near_ties": ties,
             "clocks": clk,
             "e2e": e2e,
             "obs": obs,
