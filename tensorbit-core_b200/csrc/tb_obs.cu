@@ -34,6 +34,7 @@ namespace {
 constexpr int kMaxK = 16;
 constexpr int kObsThreads = 256;
 constexpr int kMaxBlock = 224;  // B x B floats must fit in shared memory
+constexpr int kLazyChunk = 16;  // earlier downdates whose terms one pass of the lazy row computes
 
 struct ObsParams {
     float* w;
@@ -47,6 +48,7 @@ struct ObsParams {
     int B;
     const uint32_t* targets;
     unsigned long long* pruned;
+    int tcap;        // the largest target: rows of the kept downdate columns (lazy form)
 };
 
 __global__ void block_importance_kernel(const float* __restrict__ w, const float* __restrict__ F, float damp,
@@ -110,6 +112,13 @@ __device__ __forceinline__ void argmin_merge(float& v, int& i, float v2, int i2)
     if (v2 < v || (v2 == v && i2 < i)) { v = v2; i = i2; }
 }
 
+// LAZY: H stays the initial inverse H0; the greedy loop keeps only its diagonal
+// and the downdate columns c_s, h_s, and forms the one row it needs each step,
+// H0[best][j] minus the block's earlier downdates c_s[j] c_s[best] / h_s in
+// step order -- the same operations, in the same order, as the element of the
+// updated H would have seen, so the results are the same bits, with ~1/4 of
+// the correctly rounded divisions (those dominate a step).
+template <bool LAZY>
 __global__ void __launch_bounds__(kObsThreads) block_obs_kernel(const ObsParams p) {
     extern __shared__ float smem[];
     const size_t b = blockIdx.x;
@@ -171,13 +180,21 @@ __global__ void __launch_bounds__(kObsThreads) block_obs_kernel(const ObsParams 
     const int ung = kObsThreads / bs > 0 ? kObsThreads / bs : 1;
     const int ui = (t < ung * bs) ? t % bs : -1, ug = (t < ung * bs) ? t / bs : 0;
     // (bs <= kMaxBlock < kObsThreads, so every row has a thread)
+    float* diag = Minv + kMaxK * kMaxK;  // LAZY: the current diagonal of H
+    float* Cs = diag + bs;               // LAZY: tcap x bs downdate columns
+    float* hs = Cs + p.tcap * bs;        // LAZY: their pivots
+    float* terms = hs + p.tcap;          // LAZY: kLazyChunk x bs downdate terms of one row
+    if constexpr (LAZY) {
+        for (int i = t; i < bs; i += kObsThreads) diag[i] = H[i * bs + i];
+        __syncthreads();
+    }
     uint32_t done = 0;
     while (done < target) {
         // argmin_i w_i^2 / H_ii over H_ii > 0, first index on ties
         float v = FLT_MAX;
         int bi = 0x7FFFFFFF;
         for (int i = t; i < bs; i += kObsThreads) {
-            const float hii = H[i * bs + i];
+            const float hii = LAZY ? diag[i] : H[i * bs + i];
             if (hii <= 0.0f) continue;
             const float sc = __fdiv_rn(__fmul_rn(wv[i], wv[i]), hii);
             if (sc < v) { v = sc; bi = i; }   // ascending i per thread: first wins
@@ -199,9 +216,41 @@ __global__ void __launch_bounds__(kObsThreads) block_obs_kernel(const ObsParams 
         __syncthreads();
         if (s_min >= FLT_MAX / 2) break;
         const int best = s_best;
-        const float hbb = H[best * bs + best];
+        const float hbb = LAZY ? diag[best] : H[best * bs + best];
         const float wi_old = wv[best];
         const float inv_h = __fdiv_rn(1.0f, hbb);
+        if constexpr (LAZY) {
+            // The terms of up to kLazyChunk earlier steps at once on every thread,
+            // then each row element subtracts them in step order.
+            float x = (t < bs) ? H[best * bs + t] : 0.0f;
+            for (uint32_t q0 = 0; q0 < done; q0 += kLazyChunk) {
+                const int nq = static_cast<int>(min(static_cast<uint32_t>(kLazyChunk), done - q0));
+                if (ui >= 0)
+                    for (int q = ug; q < nq; q += ung) {
+                        const float* cq = Cs + (q0 + q) * bs;
+                        terms[q * bs + ui] = __fdiv_rn(__fmul_rn(cq[ui], cq[best]), hs[q0 + q]);
+                    }
+                __syncthreads();
+                if (t < bs)
+                    for (int q = 0; q < nq; ++q) x = __fsub_rn(x, terms[q * bs + t]);
+                __syncthreads();
+            }
+            if (t < bs) col[t] = x;
+            __syncthreads();
+            for (int j = t; j < bs; j += kObsThreads) {
+                const float cj = col[j];
+                if (j != best) wv[j] = __fsub_rn(wv[j], __fmul_rn(__fmul_rn(wi_old, inv_h), cj));
+                diag[j] = __fsub_rn(diag[j], __fdiv_rn(__fmul_rn(cj, cj), hbb));
+                Cs[done * bs + j] = cj;
+            }
+            if (t == 0) {
+                wv[best] = 0.0f;
+                hs[done] = hbb;
+            }
+            __syncthreads();
+            ++done;
+            continue;
+        }
         for (int j = t; j < bs; j += kObsThreads) {
             col[j] = H[best * bs + j];
             if (j != best) wv[j] = __fsub_rn(wv[j], __fmul_rn(__fmul_rn(wi_old, inv_h), H[best * bs + j]));
@@ -318,8 +367,19 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
     p.B = static_cast<int>(B);
     p.targets = d_tgt;
     p.pruned = d_cnt;
-    const size_t smem = obs_smem_bytes(static_cast<int>(B), K ? K : 1);
-    e = cudaFuncSetAttribute(block_obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    uint32_t tmax = 0;
+    for (uint32_t x : tgt) tmax = std::max(tmax, x);
+    // the lazy form where its downdate columns fit in shared memory beside H0
+    const size_t smem_eager = obs_smem_bytes(static_cast<int>(B), K ? K : 1);
+    const size_t smem_lazy =
+        smem_eager + sizeof(float) * (B + static_cast<size_t>(tmax) * B + tmax + static_cast<size_t>(kLazyChunk) * B);
+    const bool lazy = smem_lazy <= 227 * 1024;
+    const size_t smem = lazy ? smem_lazy : smem_eager;
+    p.tcap = static_cast<int>(tmax);
+    e = lazy ? cudaFuncSetAttribute(block_obs_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem))
+             : cudaFuncSetAttribute(block_obs_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem));
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_tgt, tgt.data(), nb * sizeof(uint32_t), cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(d_cnt, 0, sizeof(unsigned long long), st);
     if (e != cudaSuccess) { release(); return cuda_fail(e, "tb_block_obs setup"); }
@@ -333,7 +393,10 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
         for (int k = 0; k < K; ++k) q.hist[k] = p.hist[k] + b0 * B;
         q.N = N - b0 * B;
         q.targets = p.targets + b0;
-        block_obs_kernel<<<static_cast<unsigned>(nslice), kObsThreads, smem, st>>>(q);
+        if (lazy)
+            block_obs_kernel<true><<<static_cast<unsigned>(nslice), kObsThreads, smem, st>>>(q);
+        else
+            block_obs_kernel<false><<<static_cast<unsigned>(nslice), kObsThreads, smem, st>>>(q);
     }
     if ((rc = check_launch("block_obs_kernel"))) { release(); return rc; }
     unsigned long long cnt = 0;
