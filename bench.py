@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--no-block-obs", action="store_true", help="skip the reference-semantics block OBS timing")
     ap.add_argument("--no-ties", action="store_true", help="skip the untimed near-tie counting pass")
     ap.add_argument("--obs-only", action="store_true", help="only the configuration-4 OBS measurement")
+    ap.add_argument("--block-obs-only", action="store_true", help="only the reference-semantics block OBS timing")
+    ap.add_argument("--block-obs-size", type=int, default=4096 * 4096,
+                    help="weights of the block OBS tensor (default one 4096 x 4096 q_proj)")
     ap.add_argument("--obs-steps", type=int, default=3)
     ap.add_argument("--obs-shape", type=int, nargs=3, metavar=("R", "D", "N"),
                     help="rows, columns and tokens of the exact-OBS pass (default: the 4096 x 14336, 2048-token down_proj)")
@@ -192,6 +195,13 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"gemm_probe": gemm_probe(torch, tb, dev, *args.gemm_probe)}), flush=True)
         return
+    if args.block_obs_only:
+        if rank == 0:
+            print(json.dumps({"block_obs": run_block_obs(torch, tb, dev, n=args.block_obs_size,
+                                                         cpu=not args.no_cpu)}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if args.obs_only:
         obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape, dist if world > 1 else None)
         if rank == 0:
@@ -290,7 +300,7 @@ def run_ours(args):
     # ---- reference-semantics block OBS (wall time; rank 0, single GPU) ------
     block_obs = None
     if rank == 0 and world == 1 and not args.no_block_obs:
-        block_obs = run_block_obs(torch, tb, dev)
+        block_obs = run_block_obs(torch, tb, dev, cpu=not args.no_cpu)
 
     # ---- CPU baseline (rank 0, single GPU only) ----------------------------
     cpu = None
@@ -506,14 +516,14 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None):
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference's own CPU code (oracle/_ref) or the port
 # ---------------------------------------------------------------------------
-def run_block_obs(torch, tb, dev, passes=3):
-    """tb-prune --strategy BlockOBS on one 4096 x 4096 q_proj (the reference's
+def run_block_obs(torch, tb, dev, passes=3, n=4096 * 4096, cpu=True):
+    """tb-prune --strategy BlockOBS on one 4096 x 4096 q_proj (n weights; the reference's
     prune_block_obs semantics: 128-element blocks, Fisher from one gradient
     sample, four scaled snapshots of it, sparsity 0.5): wall time per tensor,
     and the reference's own CPU code (one thread, as it runs) on a bounded
     sample of the same tensor's blocks, per block."""
     import numpy as np
-    n, block, K = 4096 * 4096, 128, 4
+    block, K = 128, 4
     gen = torch.Generator(device=dev).manual_seed(77)
     w0 = torch.randn(n, device=dev, generator=gen) * 0.02
     g = torch.randn(n, device=dev, generator=gen) * 1e-3
@@ -534,14 +544,15 @@ def run_block_obs(torch, tb, dev, passes=3):
         if k:
             ms.append((time.perf_counter() - t0) * 1e3)
     t = statistics.median(ms)
-    out = {"workload": "tb-prune BlockOBS on one 4096x4096 q_proj (FP32 weights), 128-element blocks, Fisher from "
+    shape = "one 4096x4096 q_proj" if n == 4096 * 4096 else f"{n} weights"
+    out = {"workload": f"tb-prune BlockOBS on {shape} (FP32 weights), 128-element blocks, Fisher from "
                        "one gradient sample, 4 scaled snapshots, sparsity 0.5, damping 0.01",
            "ms_per_tensor": round(t, 2), "passes": passes, "blocks": n // block,
            "blocks_per_s": round(n / block / (t / 1e3)), "gparams_per_s": round(n / (t / 1e3) / 1e9, 4),
            "pruned": pruned.value}
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from oracle import Oracle, ref_available
-    if ref_available():
+    if cpu and ref_available() and n >= 256 * block:
         m = 256 * block  # the tensor's first 256 blocks
         wc = w0[:m].cpu().numpy()
         gc = g[:m].cpu().numpy()[None, :]

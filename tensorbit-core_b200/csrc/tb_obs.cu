@@ -8,18 +8,18 @@
 //   with the remainder handed to the last blocks (ehap.hpp:538-577).  These are
 //   O(N/B) scalars; the host runs them with the same C library as the
 //   reference (std::exp on float) so the targets are identical.
-// Phase 3 (device, one CTA per block): D^-1, U (K gradient snapshots or
-//   sqrt(alpha) w), M = I + U^T D^-1 U, M^-1 by pivoted LDL^T, the full B x B
-//   H^-1 = D^-1 - D^-1 (sum Minv_kl u_k u_l^T) D^-1 in shared memory, then the
-//   greedy loop: argmin w_i^2 / H^-1_ii (lowest index on ties), OBS update of
-//   the other weights, rank-1 Sherman-Morrison deflation of H^-1
-//   (ehap.hpp:582-701).
+// Phase 3 (device, one CTA per block, one thread per row): D^-1, U (K gradient
+//   snapshots or sqrt(alpha) w), M = I + U^T D^-1 U, M^-1 by pivoted LDL^T,
+//   then the greedy loop: argmin w_i^2 / H^-1_ii (lowest index on ties), OBS
+//   update of the other weights, rank-1 Sherman-Morrison deflation of
+//   H^-1 = D^-1 - D^-1 (sum Minv_kl u_k u_l^T) D^-1 (ehap.hpp:582-701), with
+//   the deflation applied lazily to the rows the greedy reads.
 //
 // Every float operation keeps the reference's expression tree (products
 // accumulated over the inner index in order from zero, no fused multiply-add);
 // the K x K factorisation follows the pivoted LDL^T the reference oracle is
-// built with.  The loop is latency-bound CUDA-core work (B^2 divisions per
-// pruned weight); there is no tensor-core formulation of its serial greedy.
+// built with.  The loop is latency-bound CUDA-core work (correctly rounded
+// divisions); there is no tensor-core formulation of its serial greedy.
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -32,9 +32,8 @@ namespace tb {
 namespace {
 
 constexpr int kMaxK = 16;
-constexpr int kObsThreads = 256;
-constexpr int kMaxBlock = 224;  // B x B floats must fit in shared memory
-constexpr int kLazyChunk = 16;  // earlier downdates whose terms one pass of the lazy row computes
+constexpr int kMaxBlock = 224;       // one thread per row; the downdate columns must fit in shared memory
+constexpr int kObsMaxThreads = 224;  // kMaxBlock rounded up to whole warps
 
 struct ObsParams {
     float* w;
@@ -47,8 +46,9 @@ struct ObsParams {
     size_t N;
     int B;
     const uint32_t* targets;
+    const uint32_t* order;   // the block of each CTA
     unsigned long long* pruned;
-    int tcap;        // the largest target: rows of the kept downdate columns (lazy form)
+    int tcap;        // the largest target: rows of the kept downdate columns
 };
 
 __global__ void block_importance_kernel(const float* __restrict__ w, const float* __restrict__ F, float damp,
@@ -107,54 +107,64 @@ __device__ void ldlt_inverse(float* a, int n, float* inv) {
     }
 }
 
-// argmin over (value, index): smaller value wins, equal values -> lower index.
-__device__ __forceinline__ void argmin_merge(float& v, int& i, float v2, int i2) {
-    if (v2 < v || (v2 == v && i2 < i)) { v = v2; i = i2; }
+// A candidate of the greedy argmin: its score, row, weight and diagonal entry.
+struct ObsCand {
+    float v;
+    int i;
+    float w;
+    float h;
+};
+
+// smaller score wins, equal scores -> lower row index
+__device__ __forceinline__ void cand_merge(ObsCand& a, const ObsCand& b) {
+    if (b.v < a.v || (b.v == a.v && b.i < a.i)) a = b;
 }
 
-// LAZY: H stays the initial inverse H0; the greedy loop keeps only its diagonal
-// and the downdate columns c_s, h_s, and forms the one row it needs each step,
-// H0[best][j] minus the block's earlier downdates c_s[j] c_s[best] / h_s in
-// step order -- the same operations, in the same order, as the element of the
-// updated H would have seen, so the results are the same bits, with ~1/4 of
-// the correctly rounded divisions (those dominate a step).
-template <bool LAZY>
-__global__ void __launch_bounds__(kObsThreads) block_obs_kernel(const ObsParams p) {
+// One CTA per block, one thread per row of the block (blockDim = B rounded up
+// to whole warps).  The reference keeps the full B x B inverse and deflates all
+// of it after every pruned weight; here the greedy loop keeps only what it
+// reads: the diagonal of H^-1 and the weights (each in its row's thread), the
+// downdate columns c_s = H^-1[best_s][:] and their pivots h_s.  The one row a
+// step needs is formed as the reference's element would have been: H0[best][j]
+// (recomputed from U, M^-1 and D^-1 by the same expression tree), minus
+// c_s[j] c_s[best] / h_s for every earlier step s in step order -- the same
+// operations in the same order, so the same bits, with about a quarter of the
+// reference's correctly rounded divisions (they dominate a step) and no B x B
+// array, which leaves room for three CTAs per SM.
+__global__ void __launch_bounds__(kObsMaxThreads) block_obs_kernel(const ObsParams p) {
     extern __shared__ float smem[];
-    const size_t b = blockIdx.x;
+    const size_t b = p.order[blockIdx.x];
     const size_t st = b * p.B;
     const int bs = static_cast<int>((st + p.B < p.N ? st + p.B : p.N) - st);
     const uint32_t target = p.targets[b];
-    if (target == 0 || target >= static_cast<uint32_t>(bs)) return;
+    if (target == 0 || target >= static_cast<uint32_t>(bs) || target > static_cast<uint32_t>(p.tcap)) return;
     const int K = p.K ? p.K : 1;
-    float* H = smem;                      // bs*bs, column-major
-    float* U = H + bs * bs;               // bs*K, column-major
+    float* U = smem;                      // bs*K, column-major (snapshot k at U + k*bs)
     float* Dinv = U + bs * K;             // bs
-    float* wv = Dinv + bs;                // bs
-    float* col = wv + bs;                 // bs
-    float* M = col + bs;                  // K*K
+    float* M = Dinv + bs;                 // K*K
     float* Minv = M + kMaxK * kMaxK;      // K*K
-    __shared__ float red_v[kObsThreads / 32];
-    __shared__ int red_i[kObsThreads / 32];
-    __shared__ float s_min;
-    __shared__ int s_best;
+    float* hs = Minv + kMaxK * kMaxK;     // tcap pivots h_s
+    float* Cs = hs + p.tcap;              // tcap x bs downdate columns c_s
+    __shared__ ObsCand red[2][kObsMaxThreads / 32];
     const int t = threadIdx.x;
+    const int nt = blockDim.x;
+    const bool own = t < bs;
 
-    for (int i = t; i < bs; i += kObsThreads) {
-        const float d = p.F ? __fadd_rn(p.damp, p.F[st + i]) : p.damp;
-        Dinv[i] = d > 0.0f ? __fdiv_rn(1.0f, d) : 1.0f;
-        const float wi = p.w[st + i];
-        wv[i] = wi;
+    float my_w = 0.0f;
+    if (own) {
+        const float d = p.F ? __fadd_rn(p.damp, p.F[st + t]) : p.damp;
+        Dinv[t] = d > 0.0f ? __fdiv_rn(1.0f, d) : 1.0f;
+        my_w = p.w[st + t];
         if (p.K) {
-            for (int k = 0; k < K; ++k) U[k * bs + i] = __fmul_rn(p.wk[k], p.hist[k][st + i]);
+            for (int k = 0; k < K; ++k) U[k * bs + t] = __fmul_rn(p.wk[k], p.hist[k][st + t]);
         } else {
-            U[i] = __fmul_rn(p.sa, wi);
+            U[t] = __fmul_rn(p.sa, my_w);
         }
     }
     __syncthreads();
     // M = I + 1e-8 I + (U^T D^-1) U: one thread per entry, inner index in order.
-    if (t < K * K) {
-        const int i = t % K, j = t / K;
+    for (int e = t; e < K * K; e += nt) {
+        const int i = e % K, j = e / K;
         float acc = 0.0f;
         for (int x = 0; x < bs; ++x)
             acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(U[i * bs + x], Dinv[x]), U[j * bs + x]));
@@ -164,117 +174,80 @@ __global__ void __launch_bounds__(kObsThreads) block_obs_kernel(const ObsParams 
     __syncthreads();
     if (t == 0) ldlt_inverse(M, K, Minv);
     __syncthreads();
-    // H^-1 = D^-1 - D^-1 S D^-1 with S = sum_k1 sum_k2 Minv(k1,k2) u_k1 u_k2^T.
-    for (int e = t; e < bs * bs; e += kObsThreads) {
-        const int i = e % bs, j = e / bs;
-        float S = 0.0f;
-        for (int k1 = 0; k1 < K; ++k1)
-            for (int k2 = 0; k2 < K; ++k2)
-                S = __fadd_rn(S, __fmul_rn(Minv[k2 * K + k1], __fmul_rn(U[k1 * bs + i], U[k2 * bs + j])));
-        const float h0 = (i == j) ? Dinv[i] : 0.0f;
-        H[e] = __fsub_rn(h0, __fmul_rn(__fmul_rn(Dinv[i], S), Dinv[j]));
-    }
-    __syncthreads();
 
-    // the rank-1 updates: ung column sets of bs rows each, row ui of set ug
-    const int ung = kObsThreads / bs > 0 ? kObsThreads / bs : 1;
-    const int ui = (t < ung * bs) ? t % bs : -1, ug = (t < ung * bs) ? t / bs : 0;
-    // (bs <= kMaxBlock < kObsThreads, so every row has a thread)
-    float* diag = Minv + kMaxK * kMaxK;  // LAZY: the current diagonal of H
-    float* Cs = diag + bs;               // LAZY: tcap x bs downdate columns
-    float* hs = Cs + p.tcap * bs;        // LAZY: their pivots
-    float* terms = hs + p.tcap;          // LAZY: kLazyChunk x bs downdate terms of one row
-    if constexpr (LAZY) {
-        for (int i = t; i < bs; i += kObsThreads) diag[i] = H[i * bs + i];
-        __syncthreads();
-    }
+    const float dt = own ? Dinv[t] : 0.0f;
+    // H0[j][t] = D^-1 - D^-1 (sum_k1 sum_k2 Minv(k1,k2) u_k1 u_k2^T) D^-1 at
+    // (row t, column j), k1 outer and k2 inner as the full inverse is summed.
+    auto h0 = [&](int j) {
+        float S = 0.0f;
+        for (int k1 = 0; k1 < K; ++k1) {
+            const float ui = U[k1 * bs + t];
+            for (int k2 = 0; k2 < K; ++k2)
+                S = __fadd_rn(S, __fmul_rn(Minv[k2 * K + k1], __fmul_rn(ui, U[k2 * bs + j])));
+        }
+        const float d0 = (j == t) ? dt : 0.0f;
+        return __fsub_rn(d0, __fmul_rn(__fmul_rn(dt, S), Dinv[j]));
+    };
+    float my_d = own ? h0(t) : 0.0f;
+
     uint32_t done = 0;
+    int par = 0;
     while (done < target) {
         // argmin_i w_i^2 / H_ii over H_ii > 0, first index on ties
-        float v = FLT_MAX;
-        int bi = 0x7FFFFFFF;
-        for (int i = t; i < bs; i += kObsThreads) {
-            const float hii = LAZY ? diag[i] : H[i * bs + i];
-            if (hii <= 0.0f) continue;
-            const float sc = __fdiv_rn(__fmul_rn(wv[i], wv[i]), hii);
-            if (sc < v) { v = sc; bi = i; }   // ascending i per thread: first wins
+        ObsCand c{FLT_MAX, 0x7FFFFFFF, 0.0f, 0.0f};
+        if (own && my_d > 0.0f) {
+            const float sc = __fdiv_rn(__fmul_rn(my_w, my_w), my_d);
+            if (sc < c.v) c = ObsCand{sc, t, my_w, my_d};
         }
+#pragma unroll
         for (int off = 16; off; off >>= 1) {
-            const float v2 = __shfl_down_sync(0xFFFFFFFFu, v, off);
-            const int i2 = __shfl_down_sync(0xFFFFFFFFu, bi, off);
-            argmin_merge(v, bi, v2, i2);
+            ObsCand o;
+            o.v = __shfl_down_sync(0xFFFFFFFFu, c.v, off);
+            o.i = __shfl_down_sync(0xFFFFFFFFu, c.i, off);
+            o.w = __shfl_down_sync(0xFFFFFFFFu, c.w, off);
+            o.h = __shfl_down_sync(0xFFFFFFFFu, c.h, off);
+            cand_merge(c, o);
         }
-        if ((t & 31) == 0) { red_v[t >> 5] = v; red_i[t >> 5] = bi; }
+        if ((t & 31) == 0) red[par][t >> 5] = c;
         __syncthreads();
-        if (t == 0) {
-            float vv = red_v[0];
-            int ii = red_i[0];
-            for (int q = 1; q < kObsThreads / 32; ++q) argmin_merge(vv, ii, red_v[q], red_i[q]);
-            s_min = vv;
-            s_best = ii;
-        }
-        __syncthreads();
-        if (s_min >= FLT_MAX / 2) break;
-        const int best = s_best;
-        const float hbb = LAZY ? diag[best] : H[best * bs + best];
-        const float wi_old = wv[best];
-        const float inv_h = __fdiv_rn(1.0f, hbb);
-        if constexpr (LAZY) {
-            // The terms of up to kLazyChunk earlier steps at once on every thread,
-            // then each row element subtracts them in step order.
-            float x = (t < bs) ? H[best * bs + t] : 0.0f;
-            for (uint32_t q0 = 0; q0 < done; q0 += kLazyChunk) {
-                const int nq = static_cast<int>(min(static_cast<uint32_t>(kLazyChunk), done - q0));
-                if (ui >= 0)
-                    for (int q = ug; q < nq; q += ung) {
-                        const float* cq = Cs + (q0 + q) * bs;
-                        terms[q * bs + ui] = __fdiv_rn(__fmul_rn(cq[ui], cq[best]), hs[q0 + q]);
-                    }
-                __syncthreads();
-                if (t < bs)
-                    for (int q = 0; q < nq; ++q) x = __fsub_rn(x, terms[q * bs + t]);
-                __syncthreads();
+        // every thread merges the warps' winners itself (the same total order),
+        // so one barrier per step; red[] alternates so the next step's writes
+        // never meet this step's reads
+        ObsCand r = red[par][0];
+        for (int q = 1; q < nt / 32; ++q) cand_merge(r, red[par][q]);
+        par ^= 1;
+        if (r.v >= FLT_MAX / 2) break;
+        const int best = r.i;
+        const float wi_old = r.w, hbb = r.h;
+        if (own) {
+            float x = h0(best);
+            const float* cq = Cs;
+#pragma unroll 4
+            for (uint32_t q = 0; q < done; ++q, cq += bs)
+                x = __fsub_rn(x, __fdiv_rn(__fmul_rn(cq[t], cq[best]), hs[q]));
+            if (t != best) {
+                const float inv_h = __fdiv_rn(1.0f, hbb);
+                my_w = __fsub_rn(my_w, __fmul_rn(__fmul_rn(wi_old, inv_h), x));
+            } else {
+                my_w = 0.0f;
             }
-            if (t < bs) col[t] = x;
-            __syncthreads();
-            for (int j = t; j < bs; j += kObsThreads) {
-                const float cj = col[j];
-                if (j != best) wv[j] = __fsub_rn(wv[j], __fmul_rn(__fmul_rn(wi_old, inv_h), cj));
-                diag[j] = __fsub_rn(diag[j], __fdiv_rn(__fmul_rn(cj, cj), hbb));
-                Cs[done * bs + j] = cj;
-            }
-            if (t == 0) {
-                wv[best] = 0.0f;
-                hs[done] = hbb;
-            }
-            __syncthreads();
-            ++done;
-            continue;
+            my_d = __fsub_rn(my_d, __fdiv_rn(__fmul_rn(x, x), hbb));
+            Cs[done * bs + t] = x;
         }
-        for (int j = t; j < bs; j += kObsThreads) {
-            col[j] = H[best * bs + j];
-            if (j != best) wv[j] = __fsub_rn(wv[j], __fmul_rn(__fmul_rn(wi_old, inv_h), H[best * bs + j]));
-        }
-        __syncthreads();
-        if (t == 0) wv[best] = 0.0f;
-        // H -= col col^T / h_bb: thread (row ui, column set ug) walks its columns
-        if (ui >= 0) {
-            const float ci = col[ui];
-            for (int j = ug; j < bs; j += ung) {
-                float* h = H + j * bs + ui;
-                *h = __fsub_rn(*h, __fdiv_rn(__fmul_rn(ci, col[j]), hbb));
-            }
-        }
-        __syncthreads();
+        if (t == 0) hs[done] = hbb;
         ++done;
     }
-    for (int i = t; i < bs; i += kObsThreads) p.w[st + i] = wv[i];
+    if (own) p.w[st + t] = my_w;
     if (t == 0) atomicAdd(p.pruned, static_cast<unsigned long long>(done));
 }
 
-size_t obs_smem_bytes(int B, int K) {
-    return sizeof(float) * (static_cast<size_t>(B) * B + static_cast<size_t>(B) * K + 3 * B + 2 * kMaxK * kMaxK);
+// dynamic shared memory of block_obs_kernel for blocks of B rows, K snapshots
+// and at most tcap pruned weights per block
+constexpr size_t obs_smem_bytes(size_t B, size_t K, size_t tcap) {
+    return sizeof(float) * (B * K + B + 2 * kMaxK * kMaxK + tcap + tcap * B);
 }
+static_assert(obs_smem_bytes(kMaxBlock, kMaxK, kMaxBlock - 1) <= 227 * 1024,
+              "the largest block's downdate columns must fit in shared memory");
 
 }  // namespace
 }  // namespace tb
@@ -307,7 +280,8 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
     uint32_t* d_tgt = nullptr;
     unsigned long long* d_cnt = nullptr;
     cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d_imp), nb * sizeof(float), st);
-    if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&d_tgt), nb * sizeof(uint32_t), st);
+    // targets by block, then the launch order of the blocks
+    if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&d_tgt), 2 * nb * sizeof(uint32_t), st);
     if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&d_cnt), sizeof(unsigned long long), st);
     if (e != cudaSuccess) return cuda_fail(e, "tb_block_obs scratch");
     auto release = [&] {
@@ -369,34 +343,67 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
     p.pruned = d_cnt;
     uint32_t tmax = 0;
     for (uint32_t x : tgt) tmax = std::max(tmax, x);
-    // the lazy form where its downdate columns fit in shared memory beside H0
-    const size_t smem_eager = obs_smem_bytes(static_cast<int>(B), K ? K : 1);
-    const size_t smem_lazy =
-        smem_eager + sizeof(float) * (B + static_cast<size_t>(tmax) * B + tmax + static_cast<size_t>(kLazyChunk) * B);
-    const bool lazy = smem_lazy <= 227 * 1024;
-    const size_t smem = lazy ? smem_lazy : smem_eager;
-    p.tcap = static_cast<int>(tmax);
-    e = lazy ? cudaFuncSetAttribute(block_obs_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem))
-             : cudaFuncSetAttribute(block_obs_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem));
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d_tgt, tgt.data(), nb * sizeof(uint32_t), cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(d_cnt, 0, sizeof(unsigned long long), st);
+    const unsigned threads = static_cast<unsigned>((B + 31) / 32 * 32);
+    e = cudaFuncSetAttribute(block_obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(obs_smem_bytes(B, K ? K : 1, tmax)));
+    // CTAs per SM for each target: the downdate columns in shared memory grow
+    // with it, so blocks that prune fewer weights fit more CTAs on an SM
+    std::vector<int> occ(tmax + 1, 0);
+    for (uint32_t t = 1; t <= tmax && e == cudaSuccess; ++t)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[t], block_obs_kernel, static_cast<int>(threads),
+                                                          obs_smem_bytes(B, K ? K : 1, t));
     if (e != cudaSuccess) { release(); return cuda_fail(e, "tb_block_obs setup"); }
-    // Blocks beyond 2^31-1 are launched in slices.
+    // Within each slice of at most 2^30 blocks (block ids stay 32-bit), the
+    // blocks run in descending order of target (counting sort, block id order
+    // within a target; target-0 blocks are left out), one launch per run of
+    // targets with the same CTAs per SM, each sized for its own largest target.
+    struct Launch {
+        size_t b0, first, count;
+        uint32_t tcap;
+    };
+    std::vector<Launch> launches;
+    std::vector<uint32_t> order(nb);
     const size_t slice = (size_t)1 << 30;
     for (size_t b0 = 0; b0 < nb; b0 += slice) {
+        const size_t ns = std::min(slice, nb - b0);
+        std::vector<size_t> start(tmax + 2, 0);  // start[t]: first position of target t
+        for (size_t b = b0; b < b0 + ns; ++b) ++start[tgt[b]];
+        size_t pos = 0;
+        for (uint32_t t = tmax; t >= 1; --t) {
+            const size_t c = start[t];
+            start[t] = pos;
+            pos += c;
+        }
+        const size_t nrun = pos;
+        for (size_t b = b0; b < b0 + ns; ++b)
+            if (tgt[b]) order[b0 + start[tgt[b]]++] = static_cast<uint32_t>(b - b0);
+        size_t first = 0;
+        for (uint32_t t = tmax; t >= 1 && first < nrun; --t) {
+            const size_t c = (t == tmax ? start[t] : start[t] - start[t + 1]);
+            if (c == 0) continue;
+            if (!launches.empty() && launches.back().b0 == b0 && occ[launches.back().tcap] == occ[t]) {
+                launches.back().count += c;
+            } else {
+                launches.push_back({b0, first, c, t});
+            }
+            first += c;
+        }
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_tgt, tgt.data(), nb * sizeof(uint32_t), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(d_tgt + nb, order.data(), nb * sizeof(uint32_t), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(d_cnt, 0, sizeof(unsigned long long), st);
+    if (e != cudaSuccess) { release(); return cuda_fail(e, "tb_block_obs setup"); }
+    for (const Launch& l : launches) {
         ObsParams q = p;
-        const size_t nslice = std::min(slice, nb - b0);
-        q.w = p.w + b0 * B;
-        if (p.F) q.F = p.F + b0 * B;
-        for (int k = 0; k < K; ++k) q.hist[k] = p.hist[k] + b0 * B;
-        q.N = N - b0 * B;
-        q.targets = p.targets + b0;
-        if (lazy)
-            block_obs_kernel<true><<<static_cast<unsigned>(nslice), kObsThreads, smem, st>>>(q);
-        else
-            block_obs_kernel<false><<<static_cast<unsigned>(nslice), kObsThreads, smem, st>>>(q);
+        q.w = p.w + l.b0 * B;
+        if (p.F) q.F = p.F + l.b0 * B;
+        for (int k = 0; k < K; ++k) q.hist[k] = p.hist[k] + l.b0 * B;
+        q.N = N - l.b0 * B;
+        q.targets = p.targets + l.b0;
+        q.order = d_tgt + nb + l.b0 + l.first;
+        q.tcap = static_cast<int>(l.tcap);
+        block_obs_kernel<<<static_cast<unsigned>(l.count), threads, obs_smem_bytes(B, K ? K : 1, l.tcap), st>>>(q);
     }
     if ((rc = check_launch("block_obs_kernel"))) { release(); return rc; }
     unsigned long long cnt = 0;
