@@ -35,6 +35,11 @@ CASES = [  # N, block, K, S, use_fisher, sparsity
     (5000, 224, 3, 1, True, 0.7),
     (3000, 32, 1, 1, True, 0.9),
     (65536, 128, 4, 1, True, 0.5),
+    (8000, 224, 16, 1, True, 0.5),    # largest block and history: ~218 KB of shared memory
+    (4097, 128, 4, 1, True, 0.5),     # last block of one weight (target 0)
+    (20000, 128, 4, 1, True, 0.98),   # 2 % pruned: many blocks with target 0 or 1
+    (300, 2, 1, 1, True, 0.5),        # blocks of two weights
+    (131072, 128, 4, 1, True, 0.5),   # 1024 blocks over many target groups
 ]
 
 
