@@ -154,7 +154,10 @@ int tb_compensate(float* weights, const uint8_t* mask, const float* importance, 
  * allocation; each block is pruned greedily by w_i^2 / [H^-1]_ii with OBS
  * updates and rank-1 deflation.  Weights are updated in place; the number
  * pruned goes to *pruned_out (host) and the call synchronises the stream.
- * block <= 224 (the B x B inverse lives in shared memory). */
+ * Scratch (the per-block importances, targets and launch order, ~12 bytes per
+ * block) is stream-ordered (cudaMallocAsync) and freed before returning.
+ * block <= 224 (one thread per row; a block's downdate columns, up to
+ * block - 1 of them, live in shared memory). */
 int tb_block_obs(float* weights, const float* fisher, const float* const* hist, int K, size_t N,
                  size_t block, float sparsity, float damping, float off_diag_alpha, uint64_t* pruned_out,
                  void* stream);
