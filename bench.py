@@ -1,6 +1,6 @@
 """Throughput of the fused score -> 2:4 mask -> pack pass on B200.
 
-Workload (default, BASELINE configuration 3): a 7B-class decoder - 32 layers of
+Workload (default): a 7B-class decoder - 32 layers of
 q/k/v/o (4096x4096, 1024x4096 x2, 4096x4096), gate/up (14336x4096) and down
 (4096x14336) BF16 matrices, 6,979,321,856 prunable parameters - each matrix
 with 64 BF16 gradient samples ~ N(0, 1e-3^2), weights ~ N(0, 0.02^2); Fisher EMA
@@ -55,10 +55,10 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-obs", action="store_true", help="skip the configuration-4 OBS measurement")
+    ap.add_argument("--no-obs", action="store_true", help="skip the column-block exact OBS measurement")
     ap.add_argument("--no-block-obs", action="store_true", help="skip the reference-semantics block OBS timing")
     ap.add_argument("--no-ties", action="store_true", help="skip the untimed near-tie counting pass")
-    ap.add_argument("--obs-only", action="store_true", help="only the configuration-4 OBS measurement")
+    ap.add_argument("--obs-only", action="store_true", help="only the column-block exact OBS measurement")
     ap.add_argument("--block-obs-only", action="store_true", help="only the reference-semantics block OBS timing")
     ap.add_argument("--block-obs-size", type=int, default=4096 * 4096,
                     help="weights of the block OBS tensor (default one 4096 x 4096 q_proj)")
@@ -292,7 +292,7 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = run_e2e(torch, tb, dev, gen, args, world, rank, local)
 
-    # ---- configuration 4 (OBS on tensor cores) -----------------------------
+    # ---- column-block exact OBS on tensor cores ------------------------------
     obs = None
     if not args.no_obs:
         obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape, dist if world > 1 else None)
@@ -393,7 +393,7 @@ def run_e2e(torch, tb, dev, gen, args, world, rank, local):
 
 
 # ---------------------------------------------------------------------------
-# configuration 4: column-block exact OBS on tensor cores
+# column-block exact OBS on tensor cores
 # ---------------------------------------------------------------------------
 OBS_D, OBS_R, OBS_N, OBS_B = 14336, 4096, 2048, 128
 
@@ -448,7 +448,7 @@ def sparsegpt_flops(d, r, n):
 
 
 def run_obs(torch, tb, dev, steps, shape=None, dist=None):
-    """Configuration 4 on tensor cores.  With several ranks the tokens are
+    """Column-block exact OBS of one down_proj on tensor cores.  With several ranks the tokens are
     split for X^T X (one NCCL all-reduce of H) and the rows of W for the sweep;
     the factorisation of H is replicated on every rank.  Time per pass is the
     maximum over ranks."""
@@ -500,7 +500,7 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None):
     bf16_peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
     tflops = f / (t / 1e3) / 1e12
-    return {"workload": f"cfg4: {OBS_R}x{OBS_D} down_proj (BF16 -> FP32), X {OBS_N}x{OBS_D} BF16 N(0,1) with 1% columns x20, "
+    return {"workload": f"column-block exact OBS: {OBS_R}x{OBS_D} down_proj (BF16 -> FP32), X {OBS_N}x{OBS_D} BF16 N(0,1) with 1% columns x20, "
                         "damp 0.01 mean(diag), 128-column blocks, 2:4",
             "ms_per_pass": round(t, 2), "passes": steps, "flops_per_pass": f, "tflops": round(tflops, 1),
             "unit": "TFLOP/s", "flop_count": "algorithmic for this route: d(d+1)n + 2d^3/3 + r d^2 (bench.obs_flops)",

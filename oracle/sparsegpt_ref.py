@@ -1,8 +1,8 @@
-"""Float64 restatement of column-block exact OBS.
+"""Float64 restatement of column-block exact OBS on an activation Hessian.
 
 TEST INFRASTRUCTURE ONLY (imported by tests/ to check tb_obs_sparsegpt).
 
-PARITY UNPINNED: the reference has no implementation of this configuration
+PARITY UNPINNED: the reference has no implementation of this algorithm
 (docs/EHAP.md:248-250; its kBlockOBS, ehap.hpp:502-704, is a different
 algorithm).  This follows the published column-block formulation (Frantar &
 Alistarh 2023, "SparseGPT") with the reference's OBS saliency w^2/[H^-1]_qq

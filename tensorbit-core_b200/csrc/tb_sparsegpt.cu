@@ -1,6 +1,6 @@
 // Exact OBS pruning of one weight matrix against calibration activations, in
-// the column-block ("SparseGPT") formulation: BASELINE configuration 4, for
-// which the reference has no implementation (docs/EHAP.md:248-250).  It keeps
+// the column-block ("SparseGPT") formulation, for which the reference has no
+// implementation (docs/EHAP.md:248-250).  It keeps
 // the reference's OBS saliency w^2 / [H^-1]_qq and update
 // w -= (w_q / [H^-1]_qq) [H^-1]_{q,:} (ehap.hpp:683-691), taken along the
 // Cholesky factor of H^-1 so that each pruned column is eliminated once.

@@ -5,7 +5,7 @@
 Runs the reference's own CPU code (oracle/_ref, compiled from the reference
 sources) on the seeded inputs of tests/inputs.py and records its outputs:
 
-* golden.json - sha256 digests of every output array of the configuration-1
+* golden.json - sha256 digests of every output array of the small-tensor
   pass (weights 128x128 FP32, 8 gradient samples, OBD, 2:4) for each mask
   strategy, of the tb-prune mock run's .tb file, of the BF16/F16 decode of all
   65536 bit patterns, plus the documented pins (docs/TODO.md:101,
@@ -48,25 +48,25 @@ def main():
     R = Oracle("ref")
     out = {"generator": "tests/golden/make_golden.py (reference CPU code via oracle/_ref)"}
 
-    # Configuration 1: score+mask+pack without the EHAP pre-prune.
-    w, g = inputs.cfg1()
-    cfg1 = {"inputs": {"w": sha(w), "g": sha(g)}}
+    # The 128x128 tensor with 8 samples: score+mask+pack without the EHAP pre-prune.
+    w, g = inputs.tensor_128x128_s8()
+    small = {"inputs": {"w": sha(w), "g": sha(g)}}
     for strategy in ("topn", "optimal", "iterative"):
         rc, wp, mask, F, s, _, cp = R.pipeline(w, g, mode="obd", strategy=strategy, redist="proportional")
         assert rc == 0
-        cfg1[strategy] = {"w_out": sha(wp), "mask": sha(mask), "fisher": sha(F), "scores": sha(s),
+        small[strategy] = {"w_out": sha(wp), "mask": sha(mask), "fisher": sha(F), "scores": sha(s),
                           "tb": sha(R.tb_bytes(wp, mask, 2, 4)), "coring_pruned": cp,
                           "mask_head": mask[:16].tolist()}
     for mode in ("obs", "normalized"):
         rc, wp, mask, F, s, _, cp = R.pipeline(w, g, mode=mode, strategy="optimal", redist="proportional")
         assert rc == 0
-        cfg1["optimal_" + mode] = {"w_out": sha(wp), "mask": sha(mask), "scores": sha(s)}
+        small["optimal_" + mode] = {"w_out": sha(wp), "mask": sha(mask), "scores": sha(s)}
     # tb-prune mode: EHAP one-shot global pre-prune, then CORING top-N.
     rc, wp, mask, F, s, ep, cp = R.pipeline(w, g, mode="obd", ehap_strategy="oneshot", strategy="topn")
     assert rc == 0
-    cfg1["tbprune_oneshot_topn"] = {"w_out": sha(wp), "mask": sha(mask), "scores": sha(s),
+    small["tbprune_oneshot_topn"] = {"w_out": sha(wp), "mask": sha(mask), "scores": sha(s),
                                     "ehap_pruned": ep, "coring_pruned": cp}
-    out["cfg1"] = cfg1
+    out["tensor_128x128_s8"] = small
 
     # tb-prune --mock-size 16384 --sparsity 2:4 (docs/DOCUMENTATION.md:57-70).
     with tempfile.TemporaryDirectory() as d:

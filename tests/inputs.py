@@ -11,7 +11,7 @@ def normal(shape, sigma, seed):
     return (rng.standard_normal(shape, dtype=np.float32) * np.float32(sigma)).astype(np.float32)
 
 
-def cfg1():
+def tensor_128x128_s8():
     """128x128 FP32 weights ~ N(0, 0.02^2) seed 0; 8 FP32 gradient samples ~ N(0, 1e-3^2) seed 1."""
     w = normal(16384, 0.02, 0)
     g = normal((8, 16384), 1e-3, 1)

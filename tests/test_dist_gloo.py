@@ -72,7 +72,7 @@ def _worker(rank, world, port_no, tmpdir, results):
     dist.all_reduce(F)
     results[f"F{rank}"] = F.numpy().copy()
     # --- group sharding: each rank writes its slice of one .tb ---
-    w, gg = inp.cfg1()
+    w, gg = inp.tensor_128x128_s8()
     path = os.path.join(tmpdir, "sharded.tb")
     N2, m = w.size, 4
     e0, e1 = td.group_shard(N2, m, world, rank)
@@ -98,7 +98,7 @@ def test_two_gloo_ranks(port, tmp_path):
     assert np.array_equal(results["F0"], results["F1"])
     np.testing.assert_allclose(results["F0"], F, rtol=1e-5, atol=0)
     # the .tb assembled from two ranks' slices == the single-process file
-    w, gg = inputs.cfg1()
+    w, gg = inputs.tensor_128x128_s8()
     rc, wp, mk, *_ = port.pipeline(w, gg, strategy="optimal", redist="proportional")
     assert open(tmp_path / "sharded.tb", "rb").read() == port.tb_bytes(wp, mk, 2, 4)
 

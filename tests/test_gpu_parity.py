@@ -3,7 +3,7 @@
 Bar: bit-exact.  Scores, Fisher state and pruned weights are compared as raw
 FP32 bits, masks byte for byte (ties included), .tb images byte for byte.  The
 oracle is the CPU restatement (oracle/tb_oracle.cpp), itself pinned to the
-reference's outputs by tests/test_oracle.py; configuration-1 outputs are also
+reference's outputs by tests/test_oracle.py; the 128x128 tensor's outputs are also
 checked directly against the reference's golden digests.
 """
 import ctypes as C
@@ -91,13 +91,13 @@ def oracle_pass(port, w32, g32, **kw):
     return wp, mask, F, s
 
 
-# --- configuration 1 against the reference's golden digests -------------------
+# --- the 128x128 tensor against the reference's golden digests ---------------
 
 @pytest.mark.parametrize("strategy", ["topn", "optimal", "iterative"])
-def test_cfg1_matches_reference_golden(cuda, tblib, port, strategy):
-    w, g = inputs.cfg1()
+def test_128x128_matches_reference_golden(cuda, tblib, port, strategy):
+    w, g = inputs.tensor_128x128_s8()
     r = run_fused(cuda, tblib, w, g, strategy=strategy)
-    gold = GOLD["cfg1"][strategy]
+    gold = GOLD["tensor_128x128_s8"][strategy]
     assert sha(r["F"]) == gold["fisher"]
     assert sha(r["s"]) == gold["scores"]
     assert sha(r["mask"]) == gold["mask"]
@@ -106,10 +106,10 @@ def test_cfg1_matches_reference_golden(cuda, tblib, port, strategy):
 
 
 @pytest.mark.parametrize("mode", ["obs", "normalized"])
-def test_cfg1_modes_match_reference_golden(cuda, tblib, mode):
-    w, g = inputs.cfg1()
+def test_128x128_modes_match_reference_golden(cuda, tblib, mode):
+    w, g = inputs.tensor_128x128_s8()
     r = run_fused(cuda, tblib, w, g, strategy="optimal", mode=mode)
-    gold = GOLD["cfg1"]["optimal_" + mode]
+    gold = GOLD["tensor_128x128_s8"]["optimal_" + mode]
     assert sha(r["s"]) == gold["scores"] and sha(r["mask"]) == gold["mask"] and sha(r["w_out"]) == gold["w_out"]
 
 
@@ -396,8 +396,8 @@ def test_q_proj_shape_against_oracle(cuda, tblib, port):
 
 
 def test_gate_proj_full_size_properties(cuda, tblib, port):
-    """14336x4096 BF16 weights with 128 BF16 samples (the per-matrix size of the
-    one-layer configuration): generated on the device, checked by properties
+    """14336x4096 BF16 weights with 128 BF16 samples (the per-matrix size of a
+    7B-class decoder layer's gate_proj): generated on the device, checked by properties
     that do not depend on size, and on 4096 random groups against the oracle."""
     torch = cuda
     rows, cols, S = 14336, 4096, 128

@@ -32,16 +32,16 @@ def same(a, b):
 # --- golden fixtures --------------------------------------------------------
 
 def test_inputs_are_the_fixture_inputs():
-    w, g = inputs.cfg1()
-    assert sha(w) == GOLD["cfg1"]["inputs"]["w"]
-    assert sha(g) == GOLD["cfg1"]["inputs"]["g"]
+    w, g = inputs.tensor_128x128_s8()
+    assert sha(w) == GOLD["tensor_128x128_s8"]["inputs"]["w"]
+    assert sha(g) == GOLD["tensor_128x128_s8"]["inputs"]["g"]
 
 
 @pytest.mark.parametrize("strategy", ["topn", "optimal", "iterative"])
-def test_cfg1_pass_matches_golden(port, strategy):
-    w, g = inputs.cfg1()
+def test_128x128_pass_matches_golden(port, strategy):
+    w, g = inputs.tensor_128x128_s8()
     rc, wp, mask, F, s, _, cp = port.pipeline(w, g, mode="obd", strategy=strategy, redist="proportional")
-    gold = GOLD["cfg1"][strategy]
+    gold = GOLD["tensor_128x128_s8"][strategy]
     assert rc == 0
     assert sha(F) == gold["fisher"]
     assert sha(s) == gold["scores"]
@@ -52,17 +52,17 @@ def test_cfg1_pass_matches_golden(port, strategy):
 
 
 @pytest.mark.parametrize("mode", ["obs", "normalized"])
-def test_cfg1_modes_match_golden(port, mode):
-    w, g = inputs.cfg1()
+def test_128x128_modes_match_golden(port, mode):
+    w, g = inputs.tensor_128x128_s8()
     rc, wp, mask, F, s, _, _ = port.pipeline(w, g, mode=mode, strategy="optimal", redist="proportional")
-    gold = GOLD["cfg1"]["optimal_" + mode]
+    gold = GOLD["tensor_128x128_s8"]["optimal_" + mode]
     assert rc == 0 and sha(s) == gold["scores"] and sha(mask) == gold["mask"] and sha(wp) == gold["w_out"]
 
 
 def test_tbprune_oneshot_matches_golden(port):
-    w, g = inputs.cfg1()
+    w, g = inputs.tensor_128x128_s8()
     rc, wp, mask, F, s, ep, cp = port.pipeline(w, g, mode="obd", ehap_strategy="oneshot", strategy="topn")
-    gold = GOLD["cfg1"]["tbprune_oneshot_topn"]
+    gold = GOLD["tensor_128x128_s8"]["tbprune_oneshot_topn"]
     assert rc == 0 and ep == gold["ehap_pruned"] and cp == gold["coring_pruned"]
     assert sha(s) == gold["scores"] and sha(mask) == gold["mask"] and sha(wp) == gold["w_out"]
 
