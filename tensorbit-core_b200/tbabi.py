@@ -1,7 +1,7 @@
 """ctypes binding of the C ABI in include/tb_kernels.h.
 
-This is the same boundary a foreign host would bind (see INTEGRATION.md for the
-cgo/JNI equivalents): plain pointers, sizes and int status codes.  Device
+This is the same boundary a foreign host would bind through cgo or JNI: plain
+pointers, sizes and int status codes.  Device
 pointers are passed as integers (e.g. ``tensor.data_ptr()``), streams as
 ``torch.cuda.current_stream().cuda_stream``.
 
