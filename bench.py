@@ -1,98 +1,192 @@
-"""Throughput of the fused score -> 2:4 mask -> pack pass on B200.
+"""Throughput of the fused score -> N:M mask -> pack pass on B200.
 
-Workload (default): a 7B-class decoder - 32 layers of
-q/k/v/o (4096x4096, 1024x4096 x2, 4096x4096), gate/up (14336x4096) and down
-(4096x14336) BF16 matrices, 6,979,321,856 prunable parameters - each matrix
-with 64 BF16 gradient samples ~ N(0, 1e-3^2), weights ~ N(0, 0.02^2); Fisher EMA
-(alpha 0.01, beta 0.99), OBD scoring (lambda 0.01), optimal C(4,2) 2:4 mask,
-proportional redistribution, FP32 weights + packed mask bytes written.
+Headline workload: a 7B-class decoder - 32 layers of q/k/v/o (4096x4096,
+1024x4096 x2, 4096x4096), gate/up (14336x4096) and down (4096x14336) BF16
+matrices, 6,979,321,856 prunable parameters - each matrix with 64 BF16 gradient
+samples ~ N(0, 1e-3^2), weights ~ N(0, 0.02^2); Fisher EMA (alpha 0.01, beta
+0.99), OBD scoring (lambda 0.01), optimal C(4,2) 2:4 mask, proportional
+redistribution, FP32 weights + packed mask bytes written.
 
-One step = the whole 32-layer pass (224 fused launches).  Gradients for all 32
-layers do not fit in HBM (~0.9 TB), so two resident random-init layer sets (A,
-B; 29 GB each) alternate layer by layer; every launch streams 0.5-7.6 GB, far
-above the 126 MB L2, so no L2 flush is needed between launches.  Each rank runs
-the same per-rank job (weak scaling): the path has no cross-rank data
-dependency, only the timing barrier and max-over-ranks reduction.
+One step = one whole 7B pass.  With N ranks the model is split (strong
+scaling): the 224 tensors laid end to end are cut into N contiguous, balanced
+group ranges (tbdist.model_shard); each rank prunes its range and the step
+time is the maximum over ranks.  Gradients for all 32 layers do not fit in HBM
+(~0.9 TB), so two resident random-init layer sets (A, B; 29 GB each, the same
+seeded values on every rank) alternate layer by layer; every launch streams
+0.1-7.6 GB, far above the 126 MB L2, so no L2 flush is needed.  After the
+timed region the 14 distinct tensors are pruned again split evenly across all
+ranks, assembled into .tb images and hashed: the digest must equal a single
+rank's pass over the same tensors and the committed one-GPU digest, and the
+timed outputs must equal the assembled ones.
+
+Beside the headline the line carries: the configuration-2 decoder layer
+(128 gradients with outlier columns, Normalized), the configuration-5 70B
+sweep (32 gradients, OBS scores, iterative refine with 4 rounds, patterns
+2:4 / 1:4 / 2:8 / 4:8), each checked bit for bit on a sampled piece; the
+sample-split Fisher path with its exchange (N > 1); the end-to-end host-buffer
+pass; the column-block exact OBS; the reference-semantics block OBS; and the
+reference's own CPU code on the host cores.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 7b|layer|70b] [--replicas]
 """
 from __future__ import annotations
 
 import argparse
 import ctypes as C
 import datetime
+import hashlib
 import json
 import os
 import re
 import statistics
 import subprocess
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "tensorbit-core_b200"))
 
-LAYER = [("q_proj", 4096, 4096), ("k_proj", 1024, 4096), ("v_proj", 1024, 4096),
-         ("o_proj", 4096, 4096), ("gate_proj", 14336, 4096), ("up_proj", 14336, 4096),
-         ("down_proj", 4096, 14336)]
-LAYERS = 32
-S = 64
-PARAMS_PER_LAYER = sum(r * c for _, r, c in LAYER)          # 218,103,808
-PARAMS_PER_STEP = PARAMS_PER_LAYER * LAYERS                   # 6,979,321,856
-BYTES_PER_PARAM = 2 + 2 * S + 4 + 0.25                        # W bf16 + 64 grads bf16 + W' f32 + mask
+LAYER_7B = [("q_proj", 4096, 4096), ("k_proj", 1024, 4096), ("v_proj", 1024, 4096),
+            ("o_proj", 4096, 4096), ("gate_proj", 14336, 4096), ("up_proj", 14336, 4096),
+            ("down_proj", 4096, 14336)]
+LAYER_70B = [("q_proj", 8192, 8192), ("k_proj", 1024, 8192), ("v_proj", 1024, 8192),
+             ("o_proj", 8192, 8192), ("gate_proj", 28672, 8192), ("up_proj", 28672, 8192),
+             ("down_proj", 8192, 28672)]
 METRIC = "2:4 score+mask+pack Gparams/s at 1/2/4/8 B200; % HBM roofline; OBS TFLOP/s"
-WORKLOAD = "7B-class decoder (32 layers, hidden 4096, inter 14336, 32q/8kv heads x128), 64 BF16 grads/tensor, OBD, optimal 2:4 + proportional redistribution"
+
+# SHA-256 over the .tb images (header + FP32 weights + mask bytes) of the 14
+# distinct tensors of the headline pass (layer sets A and B, 7 matrices each),
+# as one B200 produced them; every N must reproduce it.
+EXPECTED_7B_DIGEST = None
+
+
+class Workload:
+    def __init__(self, name, layer, layers, S, mode, strategy, n, m, rounds=3, redist="proportional",
+                 outliers=False, sets=1, seed=1234):
+        self.name, self.layer, self.layers, self.S = name, layer, layers, S
+        self.mode, self.strategy, self.n, self.m, self.rounds = mode, strategy, n, m, rounds
+        self.redist, self.outliers, self.sets, self.seed = redist, outliers, sets, seed
+
+    @property
+    def sizes(self):
+        return [r * c for _ in range(self.layers) for _, r, c in self.layer]
+
+    @property
+    def params(self):
+        return sum(self.sizes)
+
+    @property
+    def bytes_per_param(self):
+        # W bf16 + S grads bf16 + W' f32 + mask byte per group
+        return 2 + 2 * self.S + 4 + 1 / self.m
+
+    def pattern(self, n, m):
+        return Workload(self.name, self.layer, self.layers, self.S, self.mode, self.strategy, n, m, self.rounds,
+                        self.redist, self.outliers, self.sets, self.seed)
+
+
+W7B = Workload("7B-class decoder (32 layers, hidden 4096, inter 14336, 32q/8kv heads x128), 64 BF16 grads/tensor, "
+               "OBD, optimal 2:4 + proportional redistribution", LAYER_7B, 32, 64, "obd", "optimal", 2, 4, sets=2)
+WLAYER = Workload("one 7B-class decoder layer (q/k/v/o 4096x4096, 1024x4096 x2, 4096x4096; gate/up 14336x4096; "
+                  "down 4096x14336), 128 BF16 grads/matrix with 5% of input columns x10, Normalized, optimal 2:4",
+                  LAYER_7B, 1, 128, "normalized", "optimal", 2, 4, outliers=True, seed=2024)
+W70B = Workload("70B-class decoder (80 layers, hidden 8192, inter 28672, 64q/8kv heads x128), 32 BF16 grads/tensor, "
+                "OBS scores, iterative swap-refine (4 rounds)", LAYER_70B, 80, 32, "obs", "iterative", 2, 4, rounds=4,
+                seed=7070)
+PATTERNS_70B = [(2, 4), (1, 4), (2, 8), (4, 8)]
 
 
 def parse():
-    global LAYER, LAYERS, PARAMS_PER_LAYER, PARAMS_PER_STEP
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["7b", "layer", "70b"], default="7b",
+                    help="7b: the headline line with every sub-measurement; layer / 70b: only that workload, "
+                         "one line (per N:M pattern for 70b)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="each rank prunes its own whole model (weak scaling) instead of a share of one")
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-obs", action="store_true", help="skip the column-block exact OBS measurement")
-    ap.add_argument("--no-block-obs", action="store_true", help="skip the reference-semantics block OBS timing")
-    ap.add_argument("--no-ties", action="store_true", help="skip the untimed near-tie counting pass")
+    ap.add_argument("--sweep-steps", type=int, default=2, help="timed steps per pattern of the 70B sweep")
+    ap.add_argument("--split-steps", type=int, default=3, help="timed steps of each sample-split variant")
+    for k in ("e2e", "cpu", "obs", "block-obs", "ties", "layer", "sweep", "split", "digest", "verify"):
+        ap.add_argument(f"--no-{k}", action="store_true")
     ap.add_argument("--obs-only", action="store_true", help="only the column-block exact OBS measurement")
     ap.add_argument("--block-obs-only", action="store_true", help="only the reference-semantics block OBS timing")
     ap.add_argument("--block-obs-size", type=int, default=4096 * 4096,
                     help="weights of the block OBS tensor (default one 4096 x 4096 q_proj)")
+    ap.add_argument("--block-obs-passes", type=int, default=10)
     ap.add_argument("--obs-steps", type=int, default=3)
     ap.add_argument("--obs-shape", type=int, nargs=3, metavar=("R", "D", "N"),
                     help="rows, columns and tokens of the exact-OBS pass (default: the 4096 x 14336, 2048-token down_proj)")
     ap.add_argument("--gemm-probe", type=int, nargs=3, metavar=("M", "N", "K"),
                     help="time the tcgen05 NT GEMM (3xTF32 and BF16) at one shape and exit")
-    ap.add_argument("--layers", type=int, default=LAYERS,
-                    help="decoder layers per step (profiling a smaller case only; default 32)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder layers of the headline model (profiling a smaller case only; default 32)")
     ap.add_argument("--matrices", default="",
                     help="comma list restricting the per-layer matrices (profiling only), e.g. q_proj")
     a = ap.parse_args()
     if a.matrices:
         keep = set(a.matrices.split(","))
-        LAYER = [x for x in LAYER if x[0] in keep]
-    LAYERS = a.layers
-    PARAMS_PER_LAYER = sum(r * c for _, r, c in LAYER)
-    PARAMS_PER_STEP = PARAMS_PER_LAYER * LAYERS
+        W7B.layer = [x for x in W7B.layer if x[0] in keep]
+    if a.layers:
+        W7B.layers = a.layers
     return a
 
 
 # ---------------------------------------------------------------------------
-# clocks sampled during the timed region
+# ranks, clocks, roofline denominators
 # ---------------------------------------------------------------------------
+class Ranks:
+    """One process per GPU (torchrun environment); NCCL for the plumbing."""
+
+    def __init__(self, torch):
+        import torch.distributed as dist
+        self.torch = torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.dist = dist if self.world > 1 else None
+        if self.dist:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier(device_ids=[self.local])
+
+    def gather(self, values):
+        """[world][len(values)] float64 lists, every rank's values."""
+        t = self.torch.tensor(values, dtype=self.torch.float64, device=self.dev)
+        if not self.dist:
+            return [t.tolist()]
+        out = self.torch.empty(self.world * len(values), dtype=self.torch.float64, device=self.dev)
+        self.dist.all_gather_into_tensor(out, t)
+        return out.view(self.world, len(values)).tolist()
+
+    def sum(self, values):
+        return [sum(col) for col in zip(*self.gather(values))]
+
+    def close(self):
+        if self.dist:
+            self.barrier()
+            self.dist.destroy_process_group()
+
+
 class Clocks:
-    """nvidia-smi samples (200 ms) of this rank's GPU while the timed region runs."""
+    """nvidia-smi samples (200 ms) of this rank's GPU while a timed region runs."""
     FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
     NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, uuid: str, index: str):
-        self.uuid, self.index = uuid.lower(), str(index)
+    def __init__(self, torch, local):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        self.index = vis.split(",")[local] if vis and len(vis.split(",")) > local else str(local)
+        self.uuid = str(getattr(torch.cuda.get_device_properties(local), "uuid", "")).lower()
         self.proc = None
 
     def start(self):
@@ -102,6 +196,7 @@ class Clocks:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+        return self
 
     def stop(self):
         if not self.proc:
@@ -134,14 +229,12 @@ class Clocks:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
-# ---------------------------------------------------------------------------
-# roofline denominators and ncu traffic
-# ---------------------------------------------------------------------------
-def hbm_peak():
+def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        return float(json.load(open(p))["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
 
 
 def ncu_traffic_per_param():
@@ -155,219 +248,586 @@ def ncu_traffic_per_param():
 
 
 # ---------------------------------------------------------------------------
-# our arm
+# resident inputs and launch plans
 # ---------------------------------------------------------------------------
-def make_layer_set(torch, gen, dev):
-    tensors = []
-    for name, r, c in LAYER:
-        n = r * c
-        w = (torch.randn(n, device=dev, generator=gen, dtype=torch.bfloat16) * 0.02)
-        g = (torch.randn(S, n, device=dev, generator=gen, dtype=torch.bfloat16) * 1e-3)
-        w_out = torch.empty(n, device=dev, dtype=torch.float32)
-        mask = torch.empty(n // 4, device=dev, dtype=torch.uint8)
-        tensors.append((name, n, w, g, w_out, mask))
-    return tensors
+class Tensor:
+    def __init__(self, name, rows, cols, w, g, w_out, mask):
+        self.name, self.rows, self.cols, self.n = name, rows, cols, rows * cols
+        self.w, self.g, self.w_out, self.mask = w, g, w_out, mask
 
 
-def prune_args_for(tb, n, w_ptr, g_ptr, w_out_ptr, mask_ptr, g_stride=0):
-    return tb.prune_args(weights=w_ptr, w_dtype=tb.BF16, grads=g_ptr, g_dtype=tb.BF16, S=S, N=n,
-                         g_stride=g_stride, alpha=0.01, beta=0.99, damping=0.01, mode="obd",
-                         use_fisher=True, n=2, m=4, strategy="optimal", redist="proportional",
-                         w_out=w_out_ptr, mask_out=mask_ptr)
+def make_sets(torch, dev, wl):
+    """wl.sets layer sets of random-init BF16 weights and gradients.  The seed is
+    fixed, so every rank holds the same model."""
+    gen = torch.Generator(device=dev).manual_seed(wl.seed)
+    sets = []
+    for _ in range(wl.sets):
+        ts = []
+        for name, r, c in wl.layer:
+            n = r * c
+            w = torch.randn(n, device=dev, generator=gen, dtype=torch.bfloat16).mul_(0.02)
+            g = torch.randn(wl.S, n, device=dev, generator=gen, dtype=torch.bfloat16).mul_(1e-3)
+            if wl.outliers:  # 5% of the input columns (the second index of [out, in]) x10
+                hot = torch.randperm(c, device=dev, generator=gen)[: c // 20]
+                g.view(wl.S, r, c)[:, :, hot] *= 10
+            ts.append(Tensor(name, r, c, w, g, torch.empty(n, device=dev, dtype=torch.float32),
+                             torch.empty(n // 2, device=dev, dtype=torch.uint8)))
+        sets.append(ts)
+    return sets
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-    import tbabi as tb
+def args_for(tb, wl, T, e0, e1, n, m, w_out=None, mask=None, **extra):
+    """tb_prune_args for elements [e0, e1) of tensor T (outputs at the same
+    offsets of T's output buffers unless others are given)."""
+    wo = w_out if w_out is not None else T.w_out.data_ptr() + 4 * e0
+    mo = mask if mask is not None else T.mask.data_ptr() + e0 // m
+    return tb.prune_args(weights=T.w.data_ptr() + 2 * e0, w_dtype=tb.BF16, grads=T.g.data_ptr() + 2 * e0,
+                         g_dtype=tb.BF16, S=wl.S, N=e1 - e0, g_stride=T.n, alpha=0.01, beta=0.99, damping=0.01,
+                         mode=wl.mode, use_fisher=True, n=n, m=m, strategy=wl.strategy, rounds=wl.rounds,
+                         redist=wl.redist, w_out=wo, mask_out=mo, **extra)
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    tb.lib()
+
+def shard_plan(tb, wl, sets, ranks, replicas=False):
+    """This rank's launches: [(tensor, e0, e1, args)] in model order."""
+    import tbdist as td
+    world, rank = (1, 0) if replicas else (ranks.world, ranks.rank)
+    plan = []
+    for t, e0, e1 in td.model_shard(wl.sizes, wl.m, world, rank):
+        layer, j = divmod(t, len(wl.layer))
+        T = sets[layer % len(sets)][j]
+        plan.append((T, e0, e1, args_for(tb, wl, T, e0, e1, wl.n, wl.m)))
+    return plan
+
+
+def time_plan(torch, tb, ranks, plan, steps, warmup, clocks=None):
+    """Runs the plan `warmup` times untimed, then `steps` times between CUDA
+    events (per launch and for the whole region) with a barrier and a
+    synchronise on both sides.  Returns per-rank figures."""
+    L = tb.lib()
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
-    if args.gemm_probe:
-        if rank == 0:
-            print(json.dumps({"gemm_probe": gemm_probe(torch, tb, dev, *args.gemm_probe)}), flush=True)
-        return
-    if args.block_obs_only:
-        if rank == 0:
-            print(json.dumps({"block_obs": run_block_obs(torch, tb, dev, n=args.block_obs_size,
-                                                         cpu=not args.no_cpu)}), flush=True)
-        if world > 1:
-            dist.destroy_process_group()
-        return
-    if args.obs_only:
-        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape, dist if world > 1 else None)
-        if rank == 0:
-            print(json.dumps({"metric": METRIC, "obs": obs, "n_gpus": world}), flush=True)
-        if world > 1:
-            dist.barrier(device_ids=[local])
-            dist.destroy_process_group()
-        return
-
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    sets = [make_layer_set(torch, gen, dev), make_layer_set(torch, gen, dev)]
-    plan = []
-    for layer in range(LAYERS):
-        for (name, n, w, g, w_out, mask) in sets[layer % 2]:
-            plan.append((n, prune_args_for(tb, n, w.data_ptr(), g.data_ptr(), w_out.data_ptr(), mask.data_ptr())))
-    torch.cuda.synchronize()
 
     def step(events=None):
-        for i, (n, a) in enumerate(plan):
+        for i, (_, _, _, a) in enumerate(plan):
             if events is not None:
                 events[i][0].record(stream)
-            rc = tb.lib().tb_score_mask_pack(C.byref(a), sptr)
+            rc = L.tb_score_mask_pack(C.byref(a), sptr)
             if rc:
                 tb.check(rc)
             if events is not None:
                 events[i][1].record(stream)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-
     events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in plan]
-              for _ in range(args.steps)]
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    phys = vis.split(",")[local] if vis and len(vis.split(",")) > local else str(local)
-    clocks = Clocks(str(getattr(torch.cuda.get_device_properties(dev), "uuid", "")), phys)
-    if world > 1:
-        dist.barrier(device_ids=[local])
+              for _ in range(steps)]
+    ranks.barrier()
     torch.cuda.synchronize()
-    clocks.start()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for k in range(args.steps):
+    for k in range(steps):
         step(events[k])
     t1.record(stream)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier(device_ids=[local])
+    ranks.barrier()
     torch.cuda.synchronize()
-    clk = clocks.stop()
-    elapsed_ms = t0.elapsed_time(t1)
-    kernel_ms = sum(a.elapsed_time(b) for ev in events for a, b in ev)
-    launches = args.steps * len(plan)
-    t = torch.tensor([elapsed_ms, kernel_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, kernel_ms = t.tolist()
+    clk = clocks.stop() if clocks else None
+    elapsed = t0.elapsed_time(t1)
+    kernel = sum(a.elapsed_time(b) for ev in events for a, b in ev)
+    params = sum(e1 - e0 for _, e0, e1, _ in plan)
+    per = ranks.gather([elapsed, kernel, params, len(plan)])
+    return {"per_rank": per, "clocks": clk, "steps": steps}
 
-    params_total = PARAMS_PER_STEP * args.steps * world
-    value = params_total / (elapsed_ms / 1e3) / 1e9
-    peak, peak_kind = hbm_peak()
-    per_launch_bytes = PARAMS_PER_STEP * BYTES_PER_PARAM / len(plan)
-    achieved = per_launch_bytes / (kernel_ms / launches / 1e3) / 1e9
+
+def summarize(wl, timing, world, hbm, replicas=False):
+    per = timing["per_rank"]
+    steps = timing["steps"]
+    elapsed = max(r[0] for r in per)
+    slow = max(range(len(per)), key=lambda i: per[i][0])
+    mean = sum(r[0] for r in per) / len(per)
+    params = sum(r[2] for r in per)          # per step, all ranks
+    value = params * steps / (elapsed / 1e3) / 1e9
+    bpp = wl.bytes_per_param
+    # achieved HBM bandwidth of each rank's fused launches: algorithmic bytes / launch time
+    ach = [r[2] * bpp * steps / (r[1] / 1e3) / 1e9 for r in per if r[1] > 0]
+    launches = int(sum(r[3] for r in per) * steps)
+    return {
+        "value": round(value, 3), "unit": "Gparams/s", "ms_per_step": round(elapsed / steps, 3),
+        "params_per_step": int(params), "gpu_launches": launches,
+        "ranks": {"ms_per_step": [round(r[0] / steps, 3) for r in per], "params_per_step": [int(r[2]) for r in per],
+                  "launches_per_step": [int(r[3]) for r in per], "slowest_rank": slow,
+                  "imbalance": round(elapsed / mean - 1, 4)},
+        "roofline": {"bound": "hbm", "achieved": round(min(ach), 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(min(ach) / hbm, 4), "achieved_per_rank": [round(x, 1) for x in ach],
+                     "algorithmic_bytes_per_param": round(bpp, 4),
+                     "kernel_ms_total_per_rank": [round(r[1], 3) for r in per]},
+    }
+
+
+def count_near_ties(torch, tb, ranks, plan):
+    """Near-tie groups of the pass (one extra, untimed pass with the kernel's counter)."""
+    cnt = torch.zeros(1, dtype=torch.int64, device=ranks.dev)
+    sptr = torch.cuda.current_stream().cuda_stream
+    for _, _, _, a in plan:
+        a.near_ties = cnt.data_ptr()
+        rc = tb.lib().tb_score_mask_pack(C.byref(a), sptr)
+        a.near_ties = None
+        tb.check(rc)
+    torch.cuda.synchronize()
+    return int(ranks.sum([float(cnt.item())])[0])
+
+
+# ---------------------------------------------------------------------------
+# checks inside the bench (untimed): torch recomputation on the device
+# ---------------------------------------------------------------------------
+def verify_piece(torch, tb, wl, T, e0, e1, n, m, limit=1 << 22):
+    """Prunes elements [e0, e0 + L) of T again with the Fisher state and scores
+    written out and checks them: F and the scores bit for bit against the
+    reference's expression trees evaluated op by op in torch (ehap.hpp:190-197,
+    260-282), every group keeps exactly n, pruned weights are +0 and kept
+    ones the widened input; optimal masks equal the first maximum of the
+    C(m,n) subset sums in ascending subset order (coring.hpp:397-422), top-N
+    and iterative masks keep a top-n set (min kept >= max pruned)."""
+    import numpy as np
+    dev = T.w.device
+    L = min(e1 - e0, limit) // m * m
+    F = torch.empty(L, device=dev, dtype=torch.float32)
+    s = torch.empty(L, device=dev, dtype=torch.float32)
+    wo = torch.empty(L, device=dev, dtype=torch.float32)
+    mk = torch.empty(L // m, device=dev, dtype=torch.uint8)
+    a = args_for(tb, wl, T, e0, e0 + L, n, m, w_out=wo.data_ptr(), mask=mk.data_ptr(), fisher_out=F.data_ptr(),
+                 scores_out=s.data_ptr())
+    tb.check(tb.score_mask_pack(a, torch.cuda.current_stream().cuda_stream))
+    f32 = lambda v: torch.tensor(np.float32(v), device=dev)
+    alpha, beta, damp = f32(0.01), f32(0.99), f32(0.01)
+    contrib = f32(np.float32(0.01) * (np.float32(1.0) - np.float32(0.99)))
+    g = T.g[:, e0:e0 + L]
+    Fr = (alpha * g[0].float()) * g[0].float()
+    for k in range(1, wl.S):
+        gk = g[k].float()
+        Fr = (beta * Fr) + ((contrib * gk) * gk)
+    w = T.w[e0:e0 + L].float()
+    w2 = w * w
+    fd = Fr + damp
+    if wl.mode == "obd":
+        sr = w2 * fd
+    elif wl.mode == "obs":
+        sr = w2 / fd
+    else:
+        sr = (w2 * fd) / (1.0 + w2)
+    out = {"elements": L, "groups": L // m,
+           "fisher_bit_exact": bool(torch.equal(F.view(torch.int32), Fr.view(torch.int32))),
+           "scores_bit_exact": bool(torch.equal(s.view(torch.int32), sr.view(torch.int32)))}
+    bits = torch.stack([(mk >> b) & 1 for b in range(m)], 1).bool()          # [G, m]
+    keep = bits.reshape(-1)
+    out["groups_not_keeping_n"] = int((bits.sum(1) != n).sum().item())
+    wexp = torch.where(keep, w, torch.zeros_like(w))
+    out["weights_bit_exact"] = bool(torch.equal(wo.view(torch.int32), wexp.view(torch.int32)))
+    sg = sr.view(-1, m)
+    if wl.strategy == "optimal":
+        best = torch.full((sg.shape[0],), -float("inf"), device=dev)
+        bmask = torch.zeros(sg.shape[0], dtype=torch.int32, device=dev)
+        for sub in range(1 << m):  # ascending numeric order = Gosper order among popcount-n masks
+            if bin(sub).count("1") != n:
+                continue
+            tot = torch.zeros(sg.shape[0], device=dev)
+            for i in range(m):
+                if sub >> i & 1:
+                    tot = tot + sg[:, i]
+            better = tot > best
+            best = torch.where(better, tot, best)
+            bmask = torch.where(better, torch.full_like(bmask, sub), bmask)
+        out["mask_check"] = "exact: first strict maximum of the subset sums"
+        out["mask_mismatches"] = int((bmask != mk.int()).sum().item())
+    else:
+        kept_min = torch.where(bits, sg, torch.full_like(sg, float("inf"))).min(1).values
+        pruned_max = torch.where(bits, torch.full_like(sg, -float("inf")), sg).max(1).values
+        out["mask_check"] = "top-n property: min kept score >= max pruned score"
+        out["mask_mismatches"] = int((kept_min < pruned_max).sum().item())
+    out["ok"] = (out["fisher_bit_exact"] and out["scores_bit_exact"] and out["weights_bit_exact"]
+                 and out["groups_not_keeping_n"] == 0 and out["mask_mismatches"] == 0)
+    return out
+
+
+def verify_plan(torch, tb, ranks, wl, plan, n, m):
+    """verify_piece on this rank's first and last pieces; all ranks' results."""
+    res = []
+    for T, e0, e1, _ in ([plan[0], plan[-1]] if len(plan) > 1 else plan):
+        r = verify_piece(torch, tb, wl, T, e0, e1, n, m)
+        r["tensor"] = T.name
+        res.append(r)
+    ok = ranks.sum([float(all(r["ok"] for r in res))])[0] == ranks.world
+    checked = int(ranks.sum([float(sum(r["groups"] for r in res))])[0])
+    return {"ok": bool(ok), "groups_checked_all_ranks": checked, "rank0": res}
+
+
+def digest_check(torch, tb, ranks, wl, sets, plan):
+    """The 14 distinct tensors of the pass (two layer sets x 7 matrices), each
+    pruned split evenly across all ranks (tbdist.group_shard), assembled on
+    every rank (an all-reduce sum over disjoint ranges of zeros is an exact
+    gather), written as .tb images (header + FP32 weights + mask) and hashed
+    on rank 0.  Rank 0 also prunes each tensor whole and compares; every rank
+    compares the outputs of its timed pieces with the assembled ones."""
+    import numpy as np
+    import tbdist as td
+    dev, m, n = ranks.dev, wl.m, wl.n
+    sptr = torch.cuda.current_stream().cuda_stream
+    h = hashlib.sha256()
+    bad_unsharded = bad_timed = 0
+    for si, ts in enumerate(sets):
+        for j, T in enumerate(ts):
+            e0, e1 = td.group_shard(T.n, m, ranks.world, ranks.rank)
+            Wa = torch.zeros(T.n, dtype=torch.float32, device=dev)
+            Ma = torch.zeros(T.n // m, dtype=torch.uint8, device=dev)
+            if e1 > e0:
+                a = args_for(tb, wl, T, e0, e1, n, m, w_out=Wa.data_ptr() + 4 * e0, mask=Ma.data_ptr() + e0 // m)
+                tb.check(tb.score_mask_pack(a, sptr))
+            if ranks.dist:
+                ranks.dist.all_reduce(Wa.view(torch.int32))
+                ranks.dist.all_reduce(Ma)
+            for T2, p0, p1, _ in plan:
+                if T2 is T:
+                    bad_timed += int((T.w_out[p0:p1].view(torch.int32) != Wa[p0:p1].view(torch.int32)).sum().item())
+                    bad_timed += int((T.mask[p0 // m:p1 // m] != Ma[p0 // m:p1 // m]).sum().item())
+            if ranks.rank == 0:
+                if ranks.world > 1:
+                    Wu = torch.empty_like(Wa)
+                    Mu = torch.empty_like(Ma)
+                    tb.check(tb.score_mask_pack(args_for(tb, wl, T, 0, T.n, n, m, w_out=Wu.data_ptr(),
+                                                         mask=Mu.data_ptr()), sptr))
+                    bad_unsharded += int((Wu.view(torch.int32) != Wa.view(torch.int32)).sum().item())
+                    bad_unsharded += int((Mu != Ma).sum().item())
+                h.update(td.tb_header(n, m, T.n))
+                h.update(Wa.cpu().numpy())
+                h.update(Ma.cpu().numpy())
+    bad_timed = int(ranks.sum([float(bad_timed)])[0])
+    bad_unsharded = int(ranks.sum([float(bad_unsharded)])[0])
+    dig = h.hexdigest() if ranks.rank == 0 else None
+    return {"tb_images": 2 * len(sets[0]) if len(sets) > 1 else len(sets[0]),
+            "sha256": dig, "assembled_from_ranks": ranks.world,
+            "differs_from_one_rank_pass": bad_unsharded, "timed_outputs_differ": bad_timed,
+            "expected_sha256": EXPECTED_7B_DIGEST,
+            "matches_expected": (dig == EXPECTED_7B_DIGEST) if (EXPECTED_7B_DIGEST and dig) else None,
+            "ok": bad_unsharded == 0 and bad_timed == 0 and (EXPECTED_7B_DIGEST is None or dig is None
+                                                             or dig == EXPECTED_7B_DIGEST)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def run_workload(torch, tb, ranks, wl, steps, warmup, args, hbm, sets=None, patterns=None, clocks=None):
+    """Times one workload (each N:M pattern of it) split across the ranks."""
+    own = sets is None
+    if own:
+        sets = make_sets(torch, ranks.dev, wl)
+    out = {}
+    for (n, m) in (patterns or [(wl.n, wl.m)]):
+        w = wl.pattern(n, m)
+        if w.strategy != "optimal":
+            tb.check(tb.lib().tb_prepare_nm(n, m))
+        plan = shard_plan(tb, w, sets, ranks, replicas=args.replicas)
+        timing = time_plan(torch, tb, ranks, plan, steps, warmup, clocks)
+        res = summarize(w, timing, ranks.world, hbm, args.replicas)
+        res["clocks"] = timing["clocks"]
+        if not args.no_ties:
+            res["near_tie_groups"] = count_near_ties(torch, tb, ranks, plan)
+            res["groups"] = w.params // m
+        if not args.no_verify:
+            res["check"] = verify_plan(torch, tb, ranks, w, plan, n, m)
+        out[f"{n}:{m}"] = (res, plan)
+    return out, sets
+
+
+def line_base(args, world, wl, res, extra_config):
+    return {
+        "metric": METRIC, "value": res["value"], "unit": "Gparams/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak" if args.replicas else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded torch Philox; random-init BF16 weights and gradients of the model's shapes, "
+                "the same values on every rank)",
+        "config": dict({"workload": wl.name, "params_per_step": wl.params, "grad_samples": wl.S, "weights": "bf16",
+                        "grads": "bf16", "outputs": "fp32 weights + u8 mask",
+                        "l2": "no flush: every launch streams >= 0.1 GB of inputs, far above the 126 MB L2",
+                        "parallelism": (f"replicas: {world} rank(s), each its own whole model" if args.replicas else
+                                        f"strong: one model per step split over {world} rank(s) by contiguous "
+                                        f"group ranges (tbdist.model_shard), no data-path collective")},
+                       **extra_config),
+    }
+
+
+def run_ours(args):
+    import torch
+    import tbabi as tb
+    ranks = Ranks(torch)
+    tb.lib()
+    hbm, bf16_peak, peak_kind = peaks()
+    if args.gemm_probe:
+        if ranks.rank == 0:
+            print(json.dumps({"gemm_probe": gemm_probe(torch, tb, ranks.dev, *args.gemm_probe)}), flush=True)
+        ranks.close()
+        return
+    if args.block_obs_only:
+        if ranks.rank == 0:
+            print(json.dumps({"block_obs": run_block_obs(torch, tb, ranks, n=args.block_obs_size,
+                                                         passes=args.block_obs_passes, cpu=not args.no_cpu)}),
+                  flush=True)
+        ranks.close()
+        return
+    if args.obs_only:
+        obs = run_obs(torch, tb, ranks.dev, args.obs_steps, args.obs_shape, ranks.dist, bf16_peak)
+        if ranks.rank == 0:
+            print(json.dumps({"metric": METRIC, "obs": obs, "n_gpus": ranks.world}), flush=True)
+        ranks.close()
+        return
+    if args.config == "layer":
+        out, _ = run_workload(torch, tb, ranks, WLAYER, args.steps, args.warmup, args, hbm,
+                              clocks=Clocks(torch, ranks.local))
+        res, _ = out["2:4"]
+        if ranks.rank == 0:
+            line = line_base(args, ranks.world, WLAYER, res, {"config_id": "decoder layer, configuration 2"})
+            line.update({k: res[k] for k in ("roofline", "ranks", "gpu_launches", "clocks") if k in res})
+            line["roofline"]["peak_kind"] = f"{peak_kind} hbm_gbs"
+            line.update({k: res.get(k) for k in ("near_tie_groups", "groups", "check")})
+            print(json.dumps(line), flush=True)
+        ranks.close()
+        return
+    if args.config == "70b":
+        out, _ = run_workload(torch, tb, ranks, W70B, args.sweep_steps, 1, args, hbm, patterns=PATTERNS_70B,
+                              clocks=Clocks(torch, ranks.local))
+        if ranks.rank == 0:
+            for pat, (res, _) in out.items():
+                line = line_base(args, ranks.world, W70B, res, {"config_id": "70B sweep, configuration 5",
+                                                                "pattern": pat})
+                line["metric"] = f"{pat} score+mask+pack Gparams/s (70B sweep); % HBM roofline"
+                line["steps"], line["warmup"] = args.sweep_steps, 1
+                line.update({k: res[k] for k in ("roofline", "ranks", "gpu_launches", "clocks") if k in res})
+                line["roofline"]["peak_kind"] = f"{peak_kind} hbm_gbs"
+                line.update({k: res.get(k) for k in ("near_tie_groups", "groups", "check")})
+                print(json.dumps(line), flush=True)
+        ranks.close()
+        return
+
+    # ---- headline: the 7B pass, split over the ranks ------------------------
+    out, sets = run_workload(torch, tb, ranks, W7B, args.steps, args.warmup, args, hbm,
+                             clocks=Clocks(torch, ranks.local))
+    res, plan = out["2:4"]
     traffic_pp = ncu_traffic_per_param()
+    digest = None
+    if not args.no_digest and not args.replicas:
+        digest = digest_check(torch, tb, ranks, W7B, sets, plan)
 
-    # ---- near-tie groups of the pass (one extra, untimed pass with the counter) --
-    ties = None
-    if not args.no_ties:
-        cnt = torch.zeros(1, dtype=torch.int64, device=dev)
-        for _, a in plan:
-            a.near_ties = cnt.data_ptr()
-            rc = tb.lib().tb_score_mask_pack(C.byref(a), sptr)
-            a.near_ties = None
-            if rc:
-                raise tb.TbError(rc, tb.lib().tb_last_error().decode())
-        torch.cuda.synchronize()
-        groups = PARAMS_PER_STEP // 4
-        ties = {"groups": groups, "near_tie_groups": int(cnt.item()),
-                "rule": "|s(N) - s(N+1)| <= 1e-6 max(|s(N)|, FLT_MIN) among a group's sorted scores; the masks of "
-                        "these groups are bit-exact too (the reference's selection and tie order are reproduced, "
-                        "for top-N through its nth_element tie tables)"}
-
-    # ---- end to end through the host-buffer entry point --------------------
-    e2e = None
-    del sets
+    # ---- sample-split Fisher with the exchange (N > 1) ----------------------
+    split = None
+    if ranks.world > 1 and not args.no_split and not args.replicas:
+        split = run_sample_split(torch, tb, ranks, W7B, sets, args.split_steps, hbm)
+    del sets, plan, out
     torch.cuda.empty_cache()
-    if not args.no_e2e:
-        e2e = run_e2e(torch, tb, dev, gen, args, world, rank, local)
 
-    # ---- column-block exact OBS on tensor cores ------------------------------
+    # ---- configuration 2 (one decoder layer) and 5 (70B sweep) --------------
+    layer = sweep = None
+    if not args.no_layer:
+        o, _ = run_workload(torch, tb, ranks, WLAYER, args.steps, args.warmup, args, hbm)
+        layer = dict(o["2:4"][0], workload=WLAYER.name)
+        del o
+        torch.cuda.empty_cache()
+    if not args.no_sweep:
+        o, _ = run_workload(torch, tb, ranks, W70B, args.sweep_steps, 1, args, hbm, patterns=PATTERNS_70B)
+        sweep = {"workload": W70B.name, "params_per_step": W70B.params, "steps": args.sweep_steps, "warmup": 1,
+                 "patterns": {p: r for p, (r, _) in o.items()}}
+        del o
+        torch.cuda.empty_cache()
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(torch, tb, ranks, args)
     obs = None
     if not args.no_obs:
-        obs = run_obs(torch, tb, dev, args.obs_steps, args.obs_shape, dist if world > 1 else None)
-
-    # ---- reference-semantics block OBS (wall time; rank 0, single GPU) ------
+        obs = run_obs(torch, tb, ranks.dev, args.obs_steps, args.obs_shape, ranks.dist, bf16_peak)
     block_obs = None
-    if rank == 0 and world == 1 and not args.no_block_obs:
-        block_obs = run_block_obs(torch, tb, dev, cpu=not args.no_cpu)
-
-    # ---- CPU baseline (rank 0, single GPU only) ----------------------------
+    if ranks.rank == 0 and ranks.world == 1 and not args.no_block_obs:
+        block_obs = run_block_obs(torch, tb, ranks, passes=args.block_obs_passes, cpu=not args.no_cpu)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(torch, dev, threads=os.cpu_count() or 1, seconds=4.0)
+    if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(torch, ranks.dev, threads=os.cpu_count() or 1, seconds=4.0)
 
-    if rank == 0:
-        line = {
-            "metric": METRIC,
-            "value": round(value, 3),
-            "unit": "Gparams/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(elapsed_ms / args.steps, 3),
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "f32",
-            "data": "synthetic (seeded torch Philox; random-init weights and gradients of the 7B shapes)",
-            "config": {"workload": WORKLOAD, "params_per_rank_step": PARAMS_PER_STEP, "grad_samples": S,
-                       "weights": "bf16", "grads": "bf16", "outputs": "fp32 weights + u8 mask",
-                       "layer_sets_resident": 2,
-                       "l2": "no flush: every launch streams 0.5-7.6 GB >> 126 MB L2",
-                       "parallelism": f"weak: {world} rank(s), each its own 32-layer pass, no data-path collective"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
-                         "algorithmic_bytes_per_param": BYTES_PER_PARAM,
-                         "traffic": (round(traffic_pp * PARAMS_PER_STEP / len(plan)) if traffic_pp else None),
-                         "traffic_per_param": traffic_pp,
-                         "kernel": "fused_vec_kernel<BF16,BF16,M=4>",
-                         "kernel_ms_total": round(kernel_ms, 3)},
-            "gpu_launches": launches,
-            "near_ties": ties,
-            "clocks": clk,
-            "e2e": e2e,
-            "obs": obs,
-            "block_obs": block_obs,
-            "cpu_baseline": cpu,
-        }
+    if ranks.rank == 0:
+        line = line_base(args, ranks.world, W7B, res, {"layer_sets_resident": 2})
+        rl = res["roofline"]
+        rl.update({"peak_kind": f"{peak_kind} hbm_gbs", "kernel": "fused_vec_kernel<BF16,BF16,M=4>",
+                   "traffic": (round(traffic_pp * res["params_per_step"] / res["gpu_launches"] * args.steps)
+                               if traffic_pp else None),
+                   "traffic_per_param": traffic_pp})
+        line.update({"roofline": rl, "gpu_launches": res["gpu_launches"], "ranks": res["ranks"],
+                     "clocks": res["clocks"], "check": res.get("check"), "tb_digest": digest,
+                     "near_ties": ({"groups": res["groups"], "near_tie_groups": res["near_tie_groups"],
+                                    "rule": "|s(N) - s(N+1)| <= 1e-6 max(|s(N)|, FLT_MIN) among a group's sorted "
+                                            "scores; their masks are bit-exact too (the reference's selection and "
+                                            "tie order are reproduced)"} if "groups" in res else None),
+                     "sample_split": split, "layer": layer, "sweep70b": sweep, "e2e": e2e, "obs": obs,
+                     "block_obs": block_obs, "cpu_baseline": cpu})
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
+    ranks.close()
 
 
-def run_e2e(torch, tb, dev, gen, args, world, rank, local):
+# ---------------------------------------------------------------------------
+# sample split: calibration samples split across ranks, one exchange per tensor
+# ---------------------------------------------------------------------------
+def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
+    """Each rank holds samples [s0, s1) of every tensor.  Per tensor: the rank's
+    partial Fisher sum_t c_t g_t^2 over its samples (tb_fisher_weighted_sum),
+    an NCCL all-reduce of the N-float partials, and the fused pass over the
+    rank's group range from the summed Fisher (stateful entry, no samples).
+    Timed over one whole 7B pass; masks compared with the exact row-sharded
+    pass (the serial recurrence) on this rank's ranges."""
+    import tbdist as td
+    dist, dev, m = ranks.dist, ranks.dev, wl.m
+    s0, s1 = td.sample_shard(wl.S, ranks.world, ranks.rank)
+    c = td.ema_weights(wl.S, 0.01, 0.99)[s0:s1].copy()
+    nmax = max(T.n for ts in sets for T in ts)
+    F = torch.empty(nmax, dtype=torch.float32, device=dev)
+    sptr = torch.cuda.current_stream().cuda_stream
+    L = tb.lib()
+    items = []
+    for layer in range(wl.layers):
+        for j in range(len(wl.layer)):
+            T = sets[layer % len(sets)][j]
+            e0, e1 = td.group_shard(T.n, m, ranks.world, ranks.rank)
+            wo = torch.empty(max(1, e1 - e0), dtype=torch.float32, device=dev)
+            items.append((T, e0, e1, wo))
+    outs = {}
+    masks = {}
+    for si, ts in enumerate(sets):
+        for T in ts:
+            e0, e1 = td.group_shard(T.n, m, ranks.world, ranks.rank)
+            masks[id(T)] = torch.zeros(max(1, (e1 - e0) // m), dtype=torch.uint8, device=dev)
+            outs[id(T)] = torch.empty(max(1, e1 - e0), dtype=torch.float32, device=dev)
+    ties = torch.zeros(1, dtype=torch.int64, device=dev)
+    ev = {}
+
+    def one_pass(record=False, count=False):
+        for i, (T, e0, e1, _) in enumerate(items):
+            if record:
+                ev[i][0].record()
+            tb.check(L.tb_fisher_weighted_sum(F.data_ptr(), T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n,
+                                              T.n, c.ctypes.data, 0, sptr))
+            if record:
+                ev[i][1].record()
+            dist.all_reduce(F[:T.n])
+            if record:
+                ev[i][2].record()
+            if e1 > e0:
+                a = tb.prune_args(weights=T.w.data_ptr() + 2 * e0, w_dtype=tb.BF16, grads=None, g_dtype=tb.BF16,
+                                  S=0, N=e1 - e0, fisher_in=F.data_ptr() + 4 * e0, fisher_steps_in=wl.S,
+                                  alpha=0.01, beta=0.99, damping=0.01, mode=wl.mode, n=wl.n, m=m,
+                                  strategy=wl.strategy, redist=wl.redist, w_out=outs[id(T)].data_ptr(),
+                                  mask_out=masks[id(T)].data_ptr(), near_ties=ties.data_ptr() if count else None)
+                tb.check(L.tb_score_mask_pack(C.byref(a), sptr))
+            if record:
+                ev[i][3].record()
+
+    one_pass()  # warm-up
+    torch.cuda.synchronize()
+    ev = {i: [torch.cuda.Event(enable_timing=True) for _ in range(4)] for i in range(len(items))}
+    ph = [0.0, 0.0, 0.0]
+    ranks.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        one_pass(record=True)
+        torch.cuda.synchronize()
+        for i in range(len(items)):
+            for k in range(3):
+                ph[k] += ev[i][k].elapsed_time(ev[i][k + 1])
+    t1.record()
+    torch.cuda.synchronize()
+    ranks.barrier()
+    el = t0.elapsed_time(t1)
+    one_pass(count=True)
+    torch.cuda.synchronize()
+    # masks against the exact pass: this rank's ranges of the 14 distinct tensors
+    differ = 0
+    for ts in sets:
+        for T in ts:
+            e0, e1 = td.group_shard(T.n, m, ranks.world, ranks.rank)
+            if e1 > e0:
+                Me = torch.empty((e1 - e0) // m, dtype=torch.uint8, device=dev)
+                We = torch.empty(e1 - e0, dtype=torch.float32, device=dev)
+                tb.check(tb.score_mask_pack(args_for(tb, wl, T, e0, e1, wl.n, m, w_out=We.data_ptr(),
+                                                     mask=Me.data_ptr()), sptr))
+                differ += int((Me != masks[id(T)][:(e1 - e0) // m]).sum().item())
+    tot = ranks.gather([el, ph[0], ph[1], ph[2], float(ties.item()), float(differ)])
+    elapsed = max(r[0] for r in tot)
+    bytes_reduced = sum(T.n for T, *_ in items) * 4
+    return {
+        "workload": "the headline 7B pass with each tensor's 64 samples split over the ranks",
+        "exchange": "NCCL all-reduce (sum, FP32) of each tensor's partial Fisher",
+        "value": round(wl.params * steps / (elapsed / 1e3) / 1e9, 3), "unit": "Gparams/s",
+        "ms_per_step": round(elapsed / steps, 3), "steps": steps,
+        "phase_ms_per_step_rank0": {"partial_fisher": round(tot[0][1] / steps, 3),
+                                    "all_reduce": round(tot[0][2] / steps, 3),
+                                    "score_mask_pack": round(tot[0][3] / steps, 3)},
+        "all_reduce_bytes_per_step": bytes_reduced,
+        "all_reduce_algbw_gbs_rank0": round(bytes_reduced / (tot[0][2] / steps / 1e3) / 1e9, 1),
+        "near_tie_groups": int(sum(r[4] for r in tot)),
+        "mask_bytes_differing_from_exact_pass": int(sum(r[5] for r in tot)),
+        "mask_bytes_compared": sum(T.n // m for ts in sets for T in ts),
+    }
+
+
+# ---------------------------------------------------------------------------
+# end to end through the host-buffer entry point
+# ---------------------------------------------------------------------------
+def pcie_peak(torch, ranks, nbytes=1 << 30, reps=5):
+    """Pinned host <-> device copy bandwidth of this rank (all ranks at once)."""
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=ranks.dev)
+    out = []
+    for direction in ("h2d", "d2h"):
+        src, dst = (h, d) if direction == "h2d" else (d, h)
+        dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize()
+        ranks.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            dst.copy_(src, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        out.append(nbytes * reps / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    del h, d
+    return out
+
+
+def run_e2e(torch, tb, ranks, args):
     """Same metric through tb_score_mask_pack_host with pinned host buffers: every
     step copies that step's inputs host->device and the results back inside the
-    timed region.  One step = one decoder layer (7 matrices, 218,103,808 params);
-    the 7B pass is 32 identical layers."""
-    import torch.distributed as dist
-    nmax = max(r * c for _, r, c in LAYER)
+    timed region.  One step = one decoder layer (7 matrices, 218,103,808
+    params), split over the ranks like the headline pass."""
+    import tbdist as td
+    wl = W7B
+    S = wl.S
+    nmax = max(r * c for _, r, c in wl.layer)
+    gen = torch.Generator(device=ranks.dev).manual_seed(99)
     hw = torch.empty(nmax, dtype=torch.bfloat16, pin_memory=True)
     hg = torch.empty(S, nmax, dtype=torch.bfloat16, pin_memory=True)
     hwo = torch.empty(nmax, dtype=torch.float32, pin_memory=True)
     hm = torch.empty(nmax // 4, dtype=torch.uint8, pin_memory=True)
-    hw.copy_((torch.randn(nmax, device=dev, generator=gen) * 0.02).to(torch.bfloat16))
+    hw.copy_(torch.randn(nmax, device=ranks.dev, generator=gen, dtype=torch.bfloat16).mul_(0.02))
     for s0 in range(0, S, 8):
-        hg[s0:s0 + 8].copy_((torch.randn(8, nmax, device=dev, generator=gen) * 1e-3).to(torch.bfloat16))
+        hg[s0:s0 + 8].copy_(torch.randn(8, nmax, device=ranks.dev, generator=gen, dtype=torch.bfloat16).mul_(1e-3))
     torch.cuda.synchronize()
+    sizes = [r * c for _, r, c in wl.layer]
     calls = []
     h2d = d2h = 0
-    for name, r, c in LAYER:
-        n = r * c
-        # All matrices read the leading n columns of the shared pinned buffers.
-        calls.append(prune_args_for(tb, n, hw.data_ptr(), hg.data_ptr(), hwo.data_ptr(), hm.data_ptr(), g_stride=nmax))
+    for t, e0, e1 in td.model_shard(sizes, 4, 1 if args.replicas else ranks.world, 0 if args.replicas else ranks.rank):
+        n = e1 - e0  # every matrix reads the leading columns of the shared pinned buffers
+        calls.append(tb.prune_args(weights=hw.data_ptr() + 2 * e0, w_dtype=tb.BF16, grads=hg.data_ptr() + 2 * e0,
+                                   g_dtype=tb.BF16, S=S, N=n, g_stride=nmax, mode=wl.mode, strategy=wl.strategy,
+                                   redist=wl.redist, w_out=hwo.data_ptr() + 4 * e0, mask_out=hm.data_ptr() + e0 // 4))
         h2d += n * 2 + S * n * 2
         d2h += n * 4 + n // 4
 
@@ -376,20 +836,25 @@ def run_e2e(torch, tb, dev, gen, args, world, rank, local):
             tb.check(tb.lib().tb_score_mask_pack_host(C.byref(a)))
 
     layer()  # warm-up: staging buffers, streams
-    if world > 1:
-        dist.barrier(device_ids=[local])
+    ranks.barrier()
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
         layer()
     el = time.perf_counter() - t0
-    t = torch.tensor([el], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    el = t.item()
-    value = PARAMS_PER_LAYER * args.e2e_steps * world / el / 1e9
-    return {"value": round(value, 4), "unit": "Gparams/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": args.e2e_steps, "step": "one decoder layer (7 matrices) via tb_score_mask_pack_host, pinned host memory",
-            "s_per_step": round(el / args.e2e_steps, 4)}
+    per = ranks.gather([el, h2d, d2h])
+    del hw, hg, hwo, hm
+    peak = ranks.gather(pcie_peak(torch, ranks))
+    el = max(r[0] for r in per)
+    params = sum(sizes) * (ranks.world if args.replicas else 1)
+    return {"value": round(params * args.e2e_steps / el / 1e9, 4), "unit": "Gparams/s",
+            "h2d_bytes_per_step": int(sum(r[1] for r in per)), "d2h_bytes_per_step": int(sum(r[2] for r in per)),
+            "steps": args.e2e_steps, "s_per_step": round(el / args.e2e_steps, 4),
+            "step": "one decoder layer (7 matrices) via tb_score_mask_pack_host from pinned host memory, split "
+                    "over the ranks like the headline pass",
+            "h2d_gbs_per_rank": [round(r[1] * args.e2e_steps / r[0] / 1e9, 1) for r in per],
+            "pinned_copy_peak_gbs_per_rank": {"h2d": [round(p[0], 1) for p in peak],
+                                              "d2h": [round(p[1], 1) for p in peak]},
+            "bound": "host-to-device copies (PCIe): compare h2d_gbs_per_rank with the pinned copy peak"}
 
 
 # ---------------------------------------------------------------------------
@@ -413,7 +878,7 @@ def gemm_probe(torch, tb, dev, M, N, K, reps=5):
     sptr = torch.cuda.current_stream().cuda_stream
     A = torch.randn(M, K, device=dev)
     B = torch.randn(N, K, device=dev)
-    C = torch.empty(M, N, device=dev)
+    Cm = torch.empty(M, N, device=dev)
     ah, al, bh, bl = (torch.empty_like(A), torch.empty_like(A), torch.empty_like(B), torch.empty_like(B))
     tb.check(L.tb_split_tf32(A.data_ptr(), ah.data_ptr(), al.data_ptr(), A.numel(), sptr))
     tb.check(L.tb_split_tf32(B.data_ptr(), bh.data_ptr(), bl.data_ptr(), B.numel(), sptr))
@@ -423,8 +888,8 @@ def gemm_probe(torch, tb, dev, M, N, K, reps=5):
         def once():
             if kind == "tf32x3":
                 return L.tb_gemm_nt_tf32x3(ah.data_ptr(), al.data_ptr(), K, bh.data_ptr(), bl.data_ptr(), K, M, N, K,
-                                           1.0, 0.0, None, N, C.data_ptr(), N, 0, sptr)
-            return L.tb_gemm_nt_bf16(Ab.data_ptr(), K, Bb.data_ptr(), K, M, N, K, 1.0, 0.0, None, N, C.data_ptr(), N,
+                                           1.0, 0.0, None, N, Cm.data_ptr(), N, 0, sptr)
+            return L.tb_gemm_nt_bf16(Ab.data_ptr(), K, Bb.data_ptr(), K, M, N, K, 1.0, 0.0, None, N, Cm.data_ptr(), N,
                                      0, sptr)
         tb.check(once())
         torch.cuda.synchronize()
@@ -447,27 +912,27 @@ def sparsegpt_flops(d, r, n):
     return 2 * n * d * d + d ** 3 // 3 + 2 * d ** 3 // 3 + d ** 3 // 3 + r * d * d + r * d * 128
 
 
-def run_obs(torch, tb, dev, steps, shape=None, dist=None):
+def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1683.6):
     """Column-block exact OBS of one down_proj on tensor cores.  With several ranks the tokens are
     split for X^T X (one NCCL all-reduce of H) and the rows of W for the sweep;
     the factorisation of H is replicated on every rank.  Time per pass is the
     maximum over ranks."""
     import tbdist as td
-    OBS_R, OBS_D, OBS_N = shape or (globals()["OBS_R"], globals()["OBS_D"], globals()["OBS_N"])
+    R, D, NT = shape or (OBS_R, OBS_D, OBS_N)
     world = dist.get_world_size() if dist is not None else 1
     rank = dist.get_rank() if dist is not None else 0
     gen = torch.Generator(device=dev).manual_seed(4)
-    X = torch.randn(OBS_N, OBS_D, device=dev, generator=gen)
-    hot = torch.randperm(OBS_D, device=dev, generator=gen)[: OBS_D // 100]
+    X = torch.randn(NT, D, device=dev, generator=gen)
+    hot = torch.randperm(D, device=dev, generator=gen)[: D // 100]
     X[:, hot] *= 20
-    t0, t1 = td.token_shard(OBS_N, world, rank)
+    t0, t1 = td.token_shard(NT, world, rank)
     xt = X[t0:t1].t().contiguous().to(torch.bfloat16)
     del X
-    r0, r1 = td.obs_row_shard(OBS_R, world, rank)
-    W0 = (torch.randn(OBS_R, OBS_D, device=dev, generator=gen) * 0.02).to(torch.bfloat16).float()[r0:r1].contiguous()
+    r0, r1 = td.obs_row_shard(R, world, rank)
+    W0 = (torch.randn(R, D, device=dev, generator=gen) * 0.02).to(torch.bfloat16).float()[r0:r1].contiguous()
     W = torch.empty_like(W0)
-    H = torch.zeros(OBS_D, OBS_D, device=dev)
-    mask = torch.empty(max(1, (r1 - r0) * OBS_D // 4), dtype=torch.uint8, device=dev)
+    H = torch.zeros(D, D, device=dev)
+    mask = torch.empty(max(1, (r1 - r0) * D // 4), dtype=torch.uint8, device=dev)
     L = tb.lib()
     sptr = torch.cuda.current_stream().cuda_stream
     ms = []
@@ -479,12 +944,11 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         if world > 1:
-            td.obs_hessian_token_split(dist, torch, xt, OBS_D, OBS_N, H)
+            td.obs_hessian_token_split(dist, torch, xt, D, NT, H)
             td.prune_obs_row_split(dist, torch, W, H, mask)
         else:
-            tb.check(L.tb_obs_hessian(xt.data_ptr(), OBS_D, OBS_N, H.data_ptr(), sptr))
-            tb.check(L.tb_obs_sparsegpt(W.data_ptr(), OBS_R, OBS_D, H.data_ptr(), 0.01, 2, 4, mask.data_ptr(),
-                                        None, sptr))
+            tb.check(L.tb_obs_hessian(xt.data_ptr(), D, NT, H.data_ptr(), sptr))
+            tb.check(L.tb_obs_sparsegpt(W.data_ptr(), R, D, H.data_ptr(), 0.01, 2, 4, mask.data_ptr(), None, sptr))
         e1.record()
         torch.cuda.synchronize()
         if k:
@@ -495,13 +959,11 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t = float(t.item())
-    f = obs_flops(OBS_D, OBS_R, OBS_N)
-    fs = sparsegpt_flops(OBS_D, OBS_R, OBS_N)
-    bf16_peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
-        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+    f = obs_flops(D, R, NT)
+    fs = sparsegpt_flops(D, R, NT)
     tflops = f / (t / 1e3) / 1e12
-    return {"workload": f"column-block exact OBS: {OBS_R}x{OBS_D} down_proj (BF16 -> FP32), X {OBS_N}x{OBS_D} BF16 N(0,1) with 1% columns x20, "
-                        "damp 0.01 mean(diag), 128-column blocks, 2:4",
+    return {"workload": f"column-block exact OBS: {R}x{D} down_proj (BF16 -> FP32), X {NT}x{D} BF16 N(0,1) with 1% "
+                        "columns x20, damp 0.01 mean(diag), 128-column blocks, 2:4",
             "ms_per_pass": round(t, 2), "passes": steps, "flops_per_pass": f, "tflops": round(tflops, 1),
             "unit": "TFLOP/s", "flop_count": "algorithmic for this route: d(d+1)n + 2d^3/3 + r d^2 (bench.obs_flops)",
             "sparsegpt_flops_per_pass": fs,
@@ -514,15 +976,18 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None):
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the reference's own CPU code (oracle/_ref) or the port
+# reference-semantics block OBS
 # ---------------------------------------------------------------------------
-def run_block_obs(torch, tb, dev, passes=3, n=4096 * 4096, cpu=True):
+def run_block_obs(torch, tb, ranks, passes=10, n=4096 * 4096, cpu=True):
     """tb-prune --strategy BlockOBS on one 4096 x 4096 q_proj (n weights; the reference's
     prune_block_obs semantics: 128-element blocks, Fisher from one gradient
-    sample, four scaled snapshots of it, sparsity 0.5): wall time per tensor,
-    and the reference's own CPU code (one thread, as it runs) on a bounded
-    sample of the same tensor's blocks, per block."""
+    sample, four scaled snapshots of it, sparsity 0.5): per pass the wall time
+    of the call and its phases (tb_block_obs_phase_times: device importance,
+    host targets, device greedy kernels), SM clocks sampled meanwhile; and the
+    reference's own CPU code (one thread, as it runs) on a bounded sample of
+    the same tensor's blocks."""
     import numpy as np
+    dev = ranks.dev
     block, K = 128, 4
     gen = torch.Generator(device=dev).manual_seed(77)
     w0 = torch.randn(n, device=dev, generator=gen) * 0.02
@@ -532,9 +997,13 @@ def run_block_obs(torch, tb, dev, passes=3, n=4096 * 4096, cpu=True):
     ptrs = (C.c_void_p * K)(*[h.data_ptr() for h in hist])
     w = torch.empty_like(w0)
     L = tb.lib()
-    ms = []
+    walls, phases = [], []
     pruned = C.c_uint64()
+    ph = (C.c_float * 4)()
+    clocks = Clocks(torch, ranks.local)
     for k in range(passes + 1):  # the first pass warms up
+        if k == 1:
+            clocks.start()
         w.copy_(w0)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -542,12 +1011,22 @@ def run_block_obs(torch, tb, dev, passes=3, n=4096 * 4096, cpu=True):
                                 torch.cuda.current_stream().cuda_stream))
         torch.cuda.synchronize()
         if k:
-            ms.append((time.perf_counter() - t0) * 1e3)
-    t = statistics.median(ms)
+            walls.append((time.perf_counter() - t0) * 1e3)
+            tb.check(L.tb_block_obs_phase_times(ph, 4))
+            phases.append(list(ph))
+    clk = clocks.stop()
+    kern = [p[2] for p in phases]
+    t = statistics.median(walls)
     shape = "one 4096x4096 q_proj" if n == 4096 * 4096 else f"{n} weights"
     out = {"workload": f"tb-prune BlockOBS on {shape} (FP32 weights), 128-element blocks, Fisher from "
                        "one gradient sample, 4 scaled snapshots, sparsity 0.5, damping 0.01",
-           "ms_per_tensor": round(t, 2), "passes": passes, "blocks": n // block,
+           "ms_per_tensor": round(t, 2), "passes": passes,
+           "wall_ms": {"min": round(min(walls), 2), "median": round(t, 2), "max": round(max(walls), 2)},
+           "greedy_kernels_ms": {"min": round(min(kern), 2), "median": round(statistics.median(kern), 2),
+                                 "max": round(max(kern), 2)},
+           "importance_device_ms_median": round(statistics.median(p[0] for p in phases), 3),
+           "host_targets_ms_median": round(statistics.median(p[1] for p in phases), 3),
+           "clocks": clk, "blocks": n // block,
            "blocks_per_s": round(n / block / (t / 1e3)), "gparams_per_s": round(n / (t / 1e3) / 1e9, 4),
            "pruned": pruned.value}
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -569,9 +1048,13 @@ def run_block_obs(torch, tb, dev, passes=3, n=4096 * 4096, cpu=True):
     return out
 
 
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own CPU code (oracle/_ref) or the port
+# ---------------------------------------------------------------------------
 def cpu_sample(torch, dev):
     import numpy as np
     n = 4096 * 4096
+    S = W7B.S
     gen = torch.Generator(device=dev).manual_seed(99)
     w = (torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16).float().cpu().numpy()
     g = (torch.randn(S, n, device=dev, generator=gen) * 1e-3).to(torch.bfloat16).float().cpu().numpy()
@@ -626,7 +1109,7 @@ def run_reference(args):
         n = 4096 * 4096
         rng = np.random.default_rng(99)
         w = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.02))
-        g = (rng.standard_normal((S, n), dtype=np.float32) * np.float32(1e-3))
+        g = (rng.standard_normal((W7B.S, n), dtype=np.float32) * np.float32(1e-3))
     o = Oracle("ref" if kind == "reference" else "port")
 
     def one():
@@ -648,9 +1131,9 @@ def run_reference(args):
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "Gparams/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_per_step": "one 4096x4096 matrix, 64 FP32-widened BF16 gradient samples"},
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak" if args.replicas else "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": W7B.name, "sample_per_step": "one 4096x4096 matrix, 64 FP32-widened BF16 gradient samples"},
         "cpu_baseline": {"value": round(value, 5), "unit": "Gparams/s", "cores": cores, "kind": kind,
                          "sample": f"per step one 4096x4096 matrix (16,777,216 params) x 64 samples, {cores} shard(s) on {cores} thread(s)"},
         "e2e": {"value": round(value, 5), "unit": "Gparams/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -161,6 +161,13 @@ int tb_compensate(float* weights, const uint8_t* mask, const float* importance, 
 int tb_block_obs(float* weights, const float* fisher, const float* const* hist, int K, size_t N,
                  size_t block, float sparsity, float damping, float off_diag_alpha, uint64_t* pruned_out,
                  void* stream);
+/* Diagnostics, no reference counterpart: the phase times (milliseconds) of
+ * this host thread's last tb_block_obs call.  ms_out[0] = block importance on
+ * the device and its copy to the host (CUDA events), [1] = host target
+ * allocation and launch planning (host clock; the stream is idle meanwhile),
+ * [2] = target upload and the greedy kernels (CUDA events), [3] = the whole
+ * call (host clock).  Writes min(n, 4) values. */
+int tb_block_obs_phase_times(float* ms_out, int n);
 
 /* ---- stage 3 building blocks: tcgen05 tensor-core GEMM (sm_100a) --------- */
 /* Splits x into hi = tf32(x) (round to nearest) and lo = x - hi, the operand
@@ -210,7 +217,7 @@ int tb_obs_hessian_scaled(const void* xt_bf16, int d, int n, float scale, float*
  * r*d/4 bytes (bit k = keep column 4g+k, the .tb convention).  ut_out (d x d,
  * may be NULL) receives U^T.  A workspace of 7.5 d^2 + 3 r d floats is
  * allocated on first use and kept per device for later calls (grow-only;
- * ~8.3 GB at d = 14336, r = 4096), so calls on one device must not overlap;
+ * ~6.9 GB at d = 14336, r = 4096), so calls on one device must not overlap;
  * two internal streams per device carry the parts of the factorisation and
  * the sweep that run beside the caller's stream.  Synchronises the stream.
  * TB_ERR_CONFIG if H + lambda I is not positive definite in FP32;
@@ -260,9 +267,12 @@ typedef struct tb_prune_args {
 int tb_score_mask_pack(const tb_prune_args* args, void* stream);
 
 /* Same pass with every pointer in args a HOST pointer (pinned memory is
- * fastest).  The library stages chunks through device buffers it allocates,
- * overlapping host->device copies, the kernel and device->host copies on
- * several streams, and returns when the outputs are in host memory. */
+ * fastest).  The library stages chunks through device buffers it allocates
+ * (kept per device and grown on demand), overlapping host->device copies, the
+ * kernel and device->host copies on several internal streams, and returns when
+ * the outputs are in host memory.  Safe to call from several host threads:
+ * calls on one device are serialised by a per-device lock held for the whole
+ * call (a second caller waits), calls on different devices run in parallel. */
 int tb_score_mask_pack_host(const tb_prune_args* args);
 
 /* tb_score_mask_pack_host for callers that cannot allocate device memory.

@@ -391,7 +391,11 @@ int launch_fused(FusedParams p, int m, cudaStream_t st) {
 // ---- host-buffer pipeline ----------------------------------------------------
 // Per-device staging for tb_score_mask_pack_host: kSlots independent
 // (stream, buffers) slots; chunk k goes to slot k % kSlots, so the H2D copy of
-// one chunk, the kernel of another and the D2H copy of a third overlap.
+// one chunk, the kernel of another and the D2H copy of a third overlap.  A call
+// holds its device's call lock from the first copy until its outputs are in
+// host memory, so calls from several host threads on one device run one after
+// another and never share the slots or the tie counter; calls on different
+// devices run in parallel.
 constexpr int kSlots = 3;
 
 struct Slot {
@@ -402,6 +406,7 @@ struct Slot {
 
 struct HostPipe {
     int dev = -1;
+    std::mutex call_mu;  // held for a whole tb_score_mask_pack_host call
     Slot slot[kSlots];
     unsigned long long* ties = nullptr;
 };
@@ -409,22 +414,31 @@ struct HostPipe {
 std::mutex g_pipe_mu;
 std::vector<HostPipe*> g_pipes;
 
-int get_pipe(int dev, size_t need, HostPipe** out) {
+// The device's pipe (streams and tie counter created on first use).
+int get_pipe(int dev, HostPipe** out) {
     std::lock_guard<std::mutex> lk(g_pipe_mu);
-    HostPipe* hp = nullptr;
     for (auto* x : g_pipes)
-        if (x->dev == dev) hp = x;
-    if (!hp) {
-        hp = new HostPipe;
-        hp->dev = dev;
-        for (auto& s : hp->slot) {
-            cudaError_t e = cudaStreamCreateWithFlags(&s.st, cudaStreamNonBlocking);
-            if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+        if (x->dev == dev) {
+            *out = x;
+            return TB_OK;
         }
-        cudaError_t e = cudaMalloc(&hp->ties, sizeof(unsigned long long));
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(tie counter)");
-        g_pipes.push_back(hp);
+    auto* hp = new HostPipe;
+    hp->dev = dev;
+    for (auto& s : hp->slot) {
+        cudaError_t e = cudaStreamCreateWithFlags(&s.st, cudaStreamNonBlocking);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
     }
+    cudaError_t e = cudaMalloc(&hp->ties, sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(tie counter)");
+    g_pipes.push_back(hp);
+    *out = hp;
+    return TB_OK;
+}
+
+// Grows every slot to `need` bytes.  Called with hp->call_mu held, after the
+// previous call drained the slot streams, so no copy or kernel uses a buffer
+// that is freed here.
+int grow_slots(HostPipe* hp, size_t need) {
     for (auto& s : hp->slot) {
         if (s.cap >= need) continue;
         if (s.dbuf) {
@@ -437,9 +451,17 @@ int get_pipe(int dev, size_t need, HostPipe** out) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(host-path staging)");
         s.cap = need;
     }
-    *out = hp;
     return TB_OK;
 }
+
+// Waits for every slot stream when a call returns, also on an error path, so
+// no copy into or out of the caller's host buffers is left in flight.
+struct DrainSlots {
+    HostPipe* hp;
+    ~DrainSlots() {
+        for (auto& s : hp->slot) cudaStreamSynchronize(s.st);
+    }
+};
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -480,7 +502,10 @@ int tb_score_mask_pack_host(const tb_prune_args* a) {
     const size_t o_so = round_up(o_fo + (p.fout ? chunk * 4 : 0), 256);
     const size_t need = round_up(o_so + (p.sout ? chunk * 4 : 0), 256);
     HostPipe* hp = nullptr;
-    if ((rc = get_pipe(dev, need, &hp))) return rc;
+    if ((rc = get_pipe(dev, &hp))) return rc;
+    std::lock_guard<std::mutex> call_lock(hp->call_mu);
+    DrainSlots drain{hp};
+    if ((rc = grow_slots(hp, need))) return rc;
     if (p.ties) {
         cudaError_t e = cudaMemsetAsync(hp->ties, 0, sizeof(unsigned long long), hp->slot[0].st);
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");

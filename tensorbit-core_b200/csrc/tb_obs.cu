@@ -22,6 +22,7 @@
 // divisions); there is no tensor-core formulation of its serial greedy.
 #include <algorithm>
 #include <cfloat>
+#include <chrono>
 #include <cmath>
 #include <vector>
 
@@ -254,6 +255,34 @@ static_assert(obs_smem_bytes(kMaxBlock, kMaxK, kMaxBlock - 1) <= 227 * 1024,
 
 using namespace tb;
 
+namespace tb {
+namespace {
+// Phase times of the calling thread's last tb_block_obs call (milliseconds):
+// [0] block importance + its copy to the host, [1] host target allocation,
+// [2] target/order upload and the greedy kernels, [3] the whole call.
+thread_local float g_obs_phase_ms[4] = {0, 0, 0, 0};
+
+struct PhaseEvents {
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    bool ok = false;
+    PhaseEvents() {
+        ok = true;
+        for (auto& e : ev) ok = ok && cudaEventCreate(&e) == cudaSuccess;
+    }
+    ~PhaseEvents() {
+        for (auto& e : ev)
+            if (e) cudaEventDestroy(e);
+    }
+};
+}  // namespace
+}  // namespace tb
+
+extern "C" int tb_block_obs_phase_times(float* ms_out, int n) {
+    if (!ms_out || n < 1) return fail(TB_ERR_ARG, "tb_block_obs_phase_times: null or empty output");
+    for (int i = 0; i < n && i < 4; ++i) ms_out[i] = g_obs_phase_ms[i];
+    return TB_OK;
+}
+
 extern "C" int tb_block_obs(float* weights, const float* fisher, const float* const* hist, int K, size_t N,
                             size_t block, float sparsity, float damping, float off_diag_alpha, uint64_t* pruned_out,
                             void* stream) {
@@ -276,6 +305,9 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
         return TB_OK;
     }
     // Phase 1: block importance on the device.
+    const auto t_call = std::chrono::steady_clock::now();
+    PhaseEvents pe;
+    if (pe.ok) cudaEventRecord(pe.ev[0], st);
     float* d_imp = nullptr;
     uint32_t* d_tgt = nullptr;
     unsigned long long* d_cnt = nullptr;
@@ -295,6 +327,8 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
     e = cudaMemcpyAsync(imp.data(), d_imp, nb * sizeof(float), cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) { release(); return cuda_fail(e, "tb_block_obs block importance"); }
+    if (pe.ok) cudaEventRecord(pe.ev[1], st);
+    const auto t_host = std::chrono::steady_clock::now();
     // Phase 2: targets (ehap.hpp:538-577), host scalars.
     float mx = 0.0f;
     for (float v : imp) if (v > mx) mx = v;
@@ -389,6 +423,8 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
             first += c;
         }
     }
+    const auto t_host_end = std::chrono::steady_clock::now();
+    if (pe.ok) cudaEventRecord(pe.ev[2], st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_tgt, tgt.data(), nb * sizeof(uint32_t), cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(d_tgt + nb, order.data(), nb * sizeof(uint32_t), cudaMemcpyHostToDevice, st);
@@ -406,11 +442,19 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
         block_obs_kernel<<<static_cast<unsigned>(l.count), threads, obs_smem_bytes(B, K ? K : 1, l.tcap), st>>>(q);
     }
     if ((rc = check_launch("block_obs_kernel"))) { release(); return rc; }
+    if (pe.ok) cudaEventRecord(pe.ev[3], st);
     unsigned long long cnt = 0;
     e = cudaMemcpyAsync(&cnt, d_cnt, sizeof(cnt), cudaMemcpyDeviceToHost, st);
     release();
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_fail(e, "tb_block_obs result");
     if (pruned_out) *pruned_out = cnt;
+    using ms = std::chrono::duration<float, std::milli>;
+    g_obs_phase_ms[1] = ms(t_host_end - t_host).count();
+    g_obs_phase_ms[3] = ms(std::chrono::steady_clock::now() - t_call).count();
+    if (pe.ok) {
+        cudaEventElapsedTime(&g_obs_phase_ms[0], pe.ev[0], pe.ev[1]);
+        cudaEventElapsedTime(&g_obs_phase_ms[2], pe.ev[2], pe.ev[3]);
+    }
     return TB_OK;
 }

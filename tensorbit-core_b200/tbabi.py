@@ -113,6 +113,7 @@ def lib() -> C.CDLL:
             "tb_fisher_normalize": ([vp, sz, vp], i32),
             "tb_compensate": ([vp, vp, vp, sz, i32, vp], i32),
             "tb_block_obs": ([vp, vp, C.POINTER(vp), i32, sz, sz, f32, f32, f32, C.POINTER(C.c_uint64), vp], i32),
+            "tb_block_obs_phase_times": ([C.POINTER(C.c_float), i32], i32),
             "tb_split_tf32": ([vp, vp, vp, sz, vp], i32),
             "tb_gemm_nt_tf32x3": ([vp, vp, C.c_longlong, vp, vp, C.c_longlong, i32, i32, i32, f32, f32, vp,
                                    C.c_longlong, vp, C.c_longlong, i32, vp], i32),

@@ -27,6 +27,7 @@ Ranks read RANK / WORLD_SIZE / LOCAL_RANK from the environment like torchrun.
 """
 from __future__ import annotations
 
+import bisect
 import ctypes as C
 import math
 import os
@@ -49,6 +50,45 @@ def group_shard(N: int, m: int, world: int, rank: int) -> tuple[int, int]:
     e0 = units * rank // world * unit
     e1 = units * (rank + 1) // world * unit if rank < world - 1 else N
     return e0, e1
+
+
+def model_shard(sizes: list[int], m: int, world: int, rank: int) -> list[tuple[int, int, int]]:
+    """This rank's share of a whole model's pass.  The tensors (element counts
+    `sizes`, each a multiple of M) are laid end to end as one range of N:M
+    groups and cut into `world` contiguous parts of equal size, each cut moved
+    down to a multiple of lcm(M, 16) elements inside the tensor it falls in (so
+    every piece but a tensor's last keeps the 16-element vector path aligned).
+    Returns [(tensor index, e0, e1)]: element ranges inside the tensors, in
+    model order.  Ranks differ by at most one alignment unit per cut, however
+    unequal the tensors are; whole tensors stay whole unless a cut falls inside
+    one."""
+    for t, n in enumerate(sizes):
+        if n % m:
+            raise ValueError(f"tensor {t}: numel {n} not divisible by M={m}")
+    unit = m * 16 // math.gcd(m, 16)
+    starts = [0]
+    for n in sizes:
+        starts.append(starts[-1] + n)
+    total = starts[-1]
+
+    def cut(k):  # (tensor index, element offset in it) of cut k
+        if k <= 0:
+            return 0, 0
+        if k >= world:
+            return len(sizes), 0
+        pos = total * k // world
+        t = bisect.bisect_right(starts, pos) - 1
+        return t, (pos - starts[t]) // unit * unit
+
+    (t0, l0), (t1, l1) = cut(rank), cut(rank + 1)
+    pieces = []
+    t, lo = t0, l0
+    while t < len(sizes) and (t, lo) < (t1, l1):
+        hi = l1 if t == t1 else sizes[t]
+        if hi > lo:
+            pieces.append((t, lo, hi))
+        t, lo = t + 1, 0
+    return pieces
 
 
 def sample_shard(S: int, world: int, rank: int) -> tuple[int, int]:

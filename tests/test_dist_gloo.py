@@ -32,6 +32,46 @@ def test_group_shards_cover_and_align(N, m, world):
             assert e1 % unit == 0
 
 
+LAYER_7B = [4096 * 4096, 1024 * 4096, 1024 * 4096, 4096 * 4096, 14336 * 4096, 14336 * 4096, 4096 * 14336]
+LAYER_70B = [8192 * 8192, 1024 * 8192, 1024 * 8192, 8192 * 8192, 28672 * 8192, 28672 * 8192, 8192 * 28672]
+
+
+@pytest.mark.parametrize("sizes,m", [(LAYER_7B * 32, 4), (LAYER_70B * 80, 8), (LAYER_70B * 80, 4),
+                                     ([64, 4096, 8, 100_000, 12, 16, 48], 4), ([24, 24, 8], 8), ([4], 4),
+                                     (LAYER_7B, 4)])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 5, 7, 8])
+def test_model_shards_cover_align_and_balance(sizes, m, world):
+    unit = m * 16 // np.gcd(m, 16)
+    seen = {t: [] for t in range(len(sizes))}
+    per_rank = []
+    for r in range(world):
+        pieces = tbdist.model_shard(sizes, m, world, r)
+        per_rank.append(sum(e1 - e0 for _, e0, e1 in pieces))
+        prev = None
+        for t, e0, e1 in pieces:
+            assert 0 <= e0 < e1 <= sizes[t] and e0 % m == 0 and e1 % m == 0
+            assert e0 % unit == 0 and (e1 == sizes[t] or e1 % unit == 0)
+            assert prev is None or (t, e0) > prev  # model order
+            prev = (t, e1)
+            seen[t].append((e0, e1))
+    for t, ranges in seen.items():  # every tensor exactly covered once
+        ranges.sort()
+        assert ranges and ranges[0][0] == 0 and ranges[-1][1] == sizes[t]
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+    total = sum(sizes)
+    # each cut moves down by less than one alignment unit from its even share
+    assert all(abs(p - total / world) < unit + 1 for p in per_rank), per_rank
+
+
+def test_model_shards_keep_whole_tensors_when_layers_divide():
+    # 32 equal layers over 1/2/4/8 ranks: every cut lands on a layer boundary
+    for world in (1, 2, 4, 8):
+        for r in range(world):
+            pieces = tbdist.model_shard(LAYER_7B * 32, 4, world, r)
+            assert len(pieces) == 224 // world
+            assert all(e0 == 0 and e1 == (LAYER_7B * 32)[t] for t, e0, e1 in pieces)
+
+
 def test_ema_weights_equal_the_recurrence(port):
     g = inputs.normal((64, 5000), 1e-3, 3)
     rc, F = port.fisher(g, alpha=0.01, beta=0.99)
