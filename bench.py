@@ -124,15 +124,20 @@ def parse():
     ap.add_argument("--gemm-probe", type=int, nargs=3, metavar=("M", "N", "K"),
                     help="time the tcgen05 NT GEMM (3xTF32 and BF16) at one shape and exit")
     ap.add_argument("--layers", type=int, default=0,
-                    help="decoder layers of the headline model (profiling a smaller case only; default 32)")
+                    help="decoder layers of the selected config's model (profiling a smaller case only)")
     ap.add_argument("--matrices", default="",
                     help="comma list restricting the per-layer matrices (profiling only), e.g. q_proj")
+    ap.add_argument("--patterns", default="",
+                    help="comma list of N:M patterns of the 70B sweep (default 2:4,1:4,2:8,4:8)")
     a = ap.parse_args()
+    wl = {"7b": W7B, "layer": WLAYER, "70b": W70B}[a.config]
     if a.matrices:
         keep = set(a.matrices.split(","))
-        W7B.layer = [x for x in W7B.layer if x[0] in keep]
+        wl.layer = [x for x in wl.layer if x[0] in keep]
     if a.layers:
-        W7B.layers = a.layers
+        wl.layers = a.layers
+    if a.patterns:
+        PATTERNS_70B[:] = [tuple(int(v) for v in p.split(":")) for p in a.patterns.split(",")]
     return a
 
 
@@ -676,106 +681,134 @@ def run_ours(args):
 # sample split: calibration samples split across ranks, one exchange per tensor
 # ---------------------------------------------------------------------------
 def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
-    """Each rank holds samples [s0, s1) of every tensor.  Per tensor: the rank's
-    partial Fisher sum_t c_t g_t^2 over its samples (tb_fisher_weighted_sum),
-    an NCCL all-reduce of the N-float partials, and the fused pass over the
-    rank's group range from the summed Fisher (stateful entry, no samples).
-    Timed over one whole 7B pass; masks compared with the exact row-sharded
-    pass (the serial recurrence) on this rank's ranges."""
+    """Each rank holds samples [s0, s1) of every tensor of the headline pass.
+    Per tensor: the rank's partial Fisher sum_t c_t g_t^2 over its samples
+    (tb_fisher_weighted_sum, the EMA regrouped), then the exchange and the
+    fused pass over the rank's group range, in two variants:
+      nccl: an NCCL all-reduce of the N-float partials, then tb_score_mask_pack
+            from the summed Fisher (stateful entry, no samples);
+      peer: a one-element all-reduce as a stream-ordered barrier, then
+            tb_score_mask_pack_peer, which reads the ranks' partials of its
+            range from peer memory over NVLink inside the pass.
+    Each variant is timed over whole 7B passes; its masks are compared with the
+    exact (serial-recurrence) pass on this rank's ranges."""
     import tbdist as td
     dist, dev, m = ranks.dist, ranks.dev, wl.m
     s0, s1 = td.sample_shard(wl.S, ranks.world, ranks.rank)
     c = td.ema_weights(wl.S, 0.01, 0.99)[s0:s1].copy()
     nmax = max(T.n for ts in sets for T in ts)
-    F = torch.empty(nmax, dtype=torch.float32, device=dev)
     sptr = torch.cuda.current_stream().cuda_stream
     L = tb.lib()
-    items = []
-    for layer in range(wl.layers):
-        for j in range(len(wl.layer)):
-            T = sets[layer % len(sets)][j]
-            e0, e1 = td.group_shard(T.n, m, ranks.world, ranks.rank)
-            wo = torch.empty(max(1, e1 - e0), dtype=torch.float32, device=dev)
-            items.append((T, e0, e1, wo))
-    outs = {}
-    masks = {}
-    for si, ts in enumerate(sets):
-        for T in ts:
-            e0, e1 = td.group_shard(T.n, m, ranks.world, ranks.rank)
-            masks[id(T)] = torch.zeros(max(1, (e1 - e0) // m), dtype=torch.uint8, device=dev)
-            outs[id(T)] = torch.empty(max(1, e1 - e0), dtype=torch.float32, device=dev)
-    ties = torch.zeros(1, dtype=torch.int64, device=dev)
-    ev = {}
-
-    def one_pass(record=False, count=False):
-        for i, (T, e0, e1, _) in enumerate(items):
-            if record:
-                ev[i][0].record()
-            tb.check(L.tb_fisher_weighted_sum(F.data_ptr(), T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n,
-                                              T.n, c.ctypes.data, 0, sptr))
-            if record:
-                ev[i][1].record()
-            dist.all_reduce(F[:T.n])
-            if record:
-                ev[i][2].record()
-            if e1 > e0:
-                a = tb.prune_args(weights=T.w.data_ptr() + 2 * e0, w_dtype=tb.BF16, grads=None, g_dtype=tb.BF16,
-                                  S=0, N=e1 - e0, fisher_in=F.data_ptr() + 4 * e0, fisher_steps_in=wl.S,
-                                  alpha=0.01, beta=0.99, damping=0.01, mode=wl.mode, n=wl.n, m=m,
-                                  strategy=wl.strategy, redist=wl.redist, w_out=outs[id(T)].data_ptr(),
-                                  mask_out=masks[id(T)].data_ptr(), near_ties=ties.data_ptr() if count else None)
-                tb.check(L.tb_score_mask_pack(C.byref(a), sptr))
-            if record:
-                ev[i][3].record()
-
-    one_pass()  # warm-up
-    torch.cuda.synchronize()
-    ev = {i: [torch.cuda.Event(enable_timing=True) for _ in range(4)] for i in range(len(items))}
-    ph = [0.0, 0.0, 0.0]
-    ranks.barrier()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        one_pass(record=True)
-        torch.cuda.synchronize()
-        for i in range(len(items)):
-            for k in range(3):
-                ph[k] += ev[i][k].elapsed_time(ev[i][k + 1])
-    t1.record()
-    torch.cuda.synchronize()
-    ranks.barrier()
-    el = t0.elapsed_time(t1)
-    one_pass(count=True)
-    torch.cuda.synchronize()
-    # masks against the exact pass: this rank's ranges of the 14 distinct tensors
-    differ = 0
+    items = [sets[layer % len(sets)][j] for layer in range(wl.layers) for j in range(len(wl.layer))]
+    rng = {id(T): td.group_shard(T.n, m, ranks.world, ranks.rank) for ts in sets for T in ts}
+    outs, masks, exact = {}, {}, {}
     for ts in sets:
         for T in ts:
-            e0, e1 = td.group_shard(T.n, m, ranks.world, ranks.rank)
+            e0, e1 = rng[id(T)]
+            outs[id(T)] = torch.empty(max(16, e1 - e0), dtype=torch.float32, device=dev)
+            masks[id(T)] = torch.zeros(max(16, (e1 - e0) // m), dtype=torch.uint8, device=dev)
             if e1 > e0:
                 Me = torch.empty((e1 - e0) // m, dtype=torch.uint8, device=dev)
                 We = torch.empty(e1 - e0, dtype=torch.float32, device=dev)
                 tb.check(tb.score_mask_pack(args_for(tb, wl, T, e0, e1, wl.n, m, w_out=We.data_ptr(),
                                                      mask=Me.data_ptr()), sptr))
-                differ += int((Me != masks[id(T)][:(e1 - e0) // m]).sum().item())
-    tot = ranks.gather([el, ph[0], ph[1], ph[2], float(ties.item()), float(differ)])
-    elapsed = max(r[0] for r in tot)
-    bytes_reduced = sum(T.n for T, *_ in items) * 4
-    return {
-        "workload": "the headline 7B pass with each tensor's 64 samples split over the ranks",
-        "exchange": "NCCL all-reduce (sum, FP32) of each tensor's partial Fisher",
-        "value": round(wl.params * steps / (elapsed / 1e3) / 1e9, 3), "unit": "Gparams/s",
-        "ms_per_step": round(elapsed / steps, 3), "steps": steps,
-        "phase_ms_per_step_rank0": {"partial_fisher": round(tot[0][1] / steps, 3),
-                                    "all_reduce": round(tot[0][2] / steps, 3),
-                                    "score_mask_pack": round(tot[0][3] / steps, 3)},
-        "all_reduce_bytes_per_step": bytes_reduced,
-        "all_reduce_algbw_gbs_rank0": round(bytes_reduced / (tot[0][2] / steps / 1e3) / 1e9, 1),
-        "near_tie_groups": int(sum(r[4] for r in tot)),
-        "mask_bytes_differing_from_exact_pass": int(sum(r[5] for r in tot)),
-        "mask_bytes_compared": sum(T.n // m for ts in sets for T in ts),
-    }
+                exact[id(T)] = Me
+    F = torch.empty(nmax, dtype=torch.float32, device=dev)
+    bufs = td.PeerBuffers(dist, 4 * nmax, 2)
+    flag = torch.zeros(1, dtype=torch.float32, device=dev)
+    ties = torch.zeros(1, dtype=torch.int64, device=dev)
+    counter = [0]
+
+    def fused_args(T, e0, e1, count):
+        return tb.prune_args(weights=T.w.data_ptr() + 2 * e0, w_dtype=tb.BF16, grads=None, g_dtype=tb.BF16, S=0,
+                             N=e1 - e0, fisher_steps_in=wl.S, alpha=0.01, beta=0.99, damping=0.01, mode=wl.mode,
+                             n=wl.n, m=m, strategy=wl.strategy, redist=wl.redist, w_out=outs[id(T)].data_ptr(),
+                             mask_out=masks[id(T)].data_ptr(), near_ties=ties.data_ptr() if count else None)
+
+    def tensor_nccl(T, ev, count):
+        e0, e1 = rng[id(T)]
+        tb.check(L.tb_fisher_weighted_sum(F.data_ptr(), T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n,
+                                          T.n, c.ctypes.data, 0, sptr))
+        ev and ev[1].record()
+        dist.all_reduce(F[:T.n])
+        ev and ev[2].record()
+        if e1 > e0:
+            a = fused_args(T, e0, e1, count)
+            a.fisher_in = F.data_ptr() + 4 * e0
+            tb.check(L.tb_score_mask_pack(C.byref(a), sptr))
+
+    def tensor_peer(T, ev, count):
+        e0, e1 = rng[id(T)]
+        k = counter[0] & 1
+        counter[0] += 1
+        tb.check(L.tb_fisher_weighted_sum(bufs.local[k], T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n,
+                                          T.n, c.ctypes.data, 0, sptr))
+        ev and ev[1].record()
+        dist.all_reduce(flag)
+        ev and ev[2].record()
+        if e1 > e0:
+            parts = (C.c_void_p * ranks.world)(*[bufs.ptrs[k][r] + 4 * e0 for r in range(ranks.world)])
+            tb.check(L.tb_score_mask_pack_peer(C.byref(fused_args(T, e0, e1, count)),
+                                               C.cast(parts, C.POINTER(C.c_void_p)), ranks.world, sptr))
+
+    out = {"workload": "the headline 7B pass with each tensor's 64 samples split evenly over the ranks",
+           "samples_per_rank": s1 - s0}
+    for variant, fn in (("nccl", tensor_nccl), ("peer", tensor_peer)):
+        def one_pass(evs=None, count=False):
+            for i, T in enumerate(items):
+                ev = evs[i] if evs else None
+                ev and ev[0].record()
+                fn(T, ev, count)
+                ev and ev[3].record()
+
+        one_pass()  # warm-up
+        torch.cuda.synchronize()
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in items]
+        ph = [0.0, 0.0, 0.0]
+        ranks.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        el = 0.0
+        for _ in range(steps):
+            t0.record()
+            one_pass(evs)
+            t1.record()
+            torch.cuda.synchronize()
+            el += t0.elapsed_time(t1)
+            for ev in evs:
+                for k in range(3):
+                    ph[k] += ev[k].elapsed_time(ev[k + 1])
+        ranks.barrier()
+        ties.zero_()
+        one_pass(count=True)
+        torch.cuda.synchronize()
+        differ = 0
+        for key, Me in exact.items():
+            differ += int((Me != masks[key][:Me.numel()]).sum().item())
+        tot = ranks.gather([el, ph[0], ph[1], ph[2], float(ties.item()), float(differ)])
+        elapsed = max(r[0] for r in tot)
+        ex_bytes = sum(T.n for T in items) * 4
+        r = {"value": round(wl.params * steps / (elapsed / 1e3) / 1e9, 3), "unit": "Gparams/s",
+             "ms_per_step": round(elapsed / steps, 3), "steps": steps,
+             "phase_ms_per_step_rank0": {"partial_fisher": round(tot[0][1] / steps, 3),
+                                         "exchange": round(tot[0][2] / steps, 3),
+                                         "score_mask_pack": round(tot[0][3] / steps, 3)},
+             "near_tie_groups": int(sum(x[4] for x in tot)),
+             "mask_bytes_differing_from_exact_pass": int(sum(x[5] for x in tot)),
+             "mask_bytes_compared": sum(T.n // m for ts in sets for T in ts)}
+        if variant == "nccl":
+            r["exchange"] = "NCCL all-reduce (sum, FP32) of each tensor's N-float partial Fisher"
+            r["all_reduce_bytes_per_step"] = ex_bytes
+            r["all_reduce_algbw_gbs_rank0"] = round(ex_bytes / (tot[0][2] / steps / 1e3) / 1e9, 1)
+        else:
+            r["exchange"] = ("one-element NCCL all-reduce per tensor as a stream-ordered barrier; the pass reads the "
+                             "other ranks' partials of its range from peer memory (reduce-scatter fused into "
+                             "score/mask/pack)")
+            r["nvlink_read_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
+            r["fused_pass_gbs_rank0"] = round(ex_bytes / (tot[0][3] / steps / 1e3) / 1e9, 1)
+        out[variant] = r
+    bufs.close()
+    return out
 
 
 # ---------------------------------------------------------------------------

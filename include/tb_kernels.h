@@ -67,6 +67,20 @@ int         tb_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream
 int         tb_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
 int         tb_memset(void* dst, int value, size_t bytes, void* stream);
 int         tb_stream_sync(void* stream);
+/* Peer memory between the processes (or devices) of one node, for the
+ * sample-split pass below.  No reference counterpart: the reference prunes in
+ * one process and names multi-GPU collectives as future work
+ * (docs/CLOUD.md:155-169).  tb_ipc_handle exports a tb_malloc allocation as
+ * TB_IPC_HANDLE_BYTES opaque bytes; another process passes those bytes to
+ * tb_ipc_open and gets a device pointer to the same memory, readable by its
+ * kernels over NVLink, until tb_ipc_close.  Within one process,
+ * tb_enable_peer_access lets the current device read peer_device's memory
+ * (returns TB_OK when already enabled or when peer_device is the current one). */
+#define TB_IPC_HANDLE_BYTES 64
+int         tb_ipc_handle(const void* dev_ptr, void* handle_out);
+int         tb_ipc_open(const void* handle, void** dev_ptr_out);
+int         tb_ipc_close(void* dev_ptr);
+int         tb_enable_peer_access(int peer_device);
 /* Builds the per-device tie tables needed by TB_MASK_TOPN / TB_MASK_ITERATIVE
  * for this (n, m) on the current device.  Calls that need them build them on
  * first use; call this first if the stream will later be captured. */
@@ -265,6 +279,28 @@ typedef struct tb_prune_args {
 } tb_prune_args;
 
 int tb_score_mask_pack(const tb_prune_args* args, void* stream);
+
+/* Sample-split pass: the reduction of the ranks' partial Fisher sums fused
+ * into the score -> mask -> pack pass (a reduce-scatter over peer memory).
+ * When the S calibration gradients of a tensor are split across P ranks, each
+ * rank forms its partial F_r = sum over its samples of c_t g_t^2
+ * (tb_fisher_weighted_sum with the EMA weights, accumulate_fisher's
+ * recurrence of ehap.hpp:190-197 regrouped) for all elements; then every rank
+ * calls this on its own group range, reading the P partials of that range
+ * directly (its own and the peers', mapped with tb_ipc_open or peer access):
+ *   F[i] = ((partials[0][i] + partials[1][i]) + ...) + partials[P-1][i]
+ * (FP32 adds in index order, the same on every rank), then importance, mask,
+ * apply, redistribution and the .tb sections exactly as tb_score_mask_pack
+ * with that Fisher state.  args: as for tb_score_mask_pack with S == 0 and
+ * fisher_in == NULL; fisher_steps_in > 0 (the samples the partials cover).
+ * partials: host array of n_partials (1..8) device pointers, each already
+ * offset to this launch's first element.  The partials must be complete
+ * before the launch (e.g. a stream-ordered collective or event between the
+ * producers and this call) and must not be overwritten until every rank's
+ * call has finished.  Not bit-identical to the serial recurrence (different
+ * association); masks can differ only where scores nearly tie. */
+int tb_score_mask_pack_peer(const tb_prune_args* args, const float* const* partials, int n_partials,
+                            void* stream);
 
 /* Same pass with every pointer in args a HOST pointer (pinned memory is
  * fastest).  The library stages chunks through device buffers it allocates

@@ -239,7 +239,18 @@ __device__ __forceinline__ uint32_t select_group(float (&v)[M], int n, int strat
     if (permute) permute_by_magnitude<M>(v);
     if (strategy == TB_MASK_OPTIMAL) return select_optimal<M>(v, n);
     uint32_t byte = select_topn<M>(v, n, lut);
-    if (strategy == TB_MASK_ITERATIVE) byte = refine<M>(v, byte, rounds);
+    // A swap needs a pruned score greater than a kept one.  The top-N byte
+    // keeps every score with fewer than N strictly greater ones (ties at the
+    // boundary resolved by the table), so a pruned score above a kept one
+    // would have at least N + 1 scores above that kept one: impossible unless
+    // a comparison is undefined, i.e. the group holds a NaN.  Only such
+    // groups run the rounds, with the reference's comparisons.
+    if (strategy == TB_MASK_ITERATIVE) {
+        bool nan = false;
+#pragma unroll
+        for (int i = 0; i < M; ++i) nan |= (v[i] != v[i]);
+        if (nan) byte = refine<M>(v, byte, rounds);
+    }
     return byte;
 }
 

@@ -26,6 +26,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kEpt = 16;  // elements per thread in the vector kernel
+constexpr int kMaxParts = 8;  // partial Fisher sums of a sample-split pass (ranks of one node)
 
 struct FusedParams {
     const void* w;
@@ -47,6 +48,8 @@ struct FusedParams {
     int use_fin;     // F starts from fin
     int n, strategy, rounds, redist, permute;
     int wdt, gdt;    // dtypes (generic kernel)
+    int nparts;      // > 0: F starts as the sum of parts[0..nparts) (sample split)
+    const float* parts[kMaxParts];
 };
 
 // --- 16-element vector loads --------------------------------------------------
@@ -108,6 +111,20 @@ __device__ __forceinline__ void store16(float* base, size_t e0, const float (&x)
     for (int k = 0; k < 4; ++k) stg_stream(p + k, make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]));
 }
 
+// 16 FP32 values of one partial Fisher sum, which may live in a peer GPU's
+// memory: coherent streaming loads (ld.global.cs), not the read-only path.
+__device__ __forceinline__ void load16_part(const float* base, size_t e0, float (&x)[kEpt]) {
+    const float4* q = reinterpret_cast<const float4*>(base + e0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 v = __ldcs(q + k);
+        x[4 * k + 0] = v.x;
+        x[4 * k + 1] = v.y;
+        x[4 * k + 2] = v.z;
+        x[4 * k + 3] = v.w;
+    }
+}
+
 __device__ __forceinline__ void count_ties(unsigned long long* ties, int local) {
     const unsigned active = __activemask();
     const int total = __reduce_add_sync(active, local);
@@ -143,7 +160,11 @@ __device__ __forceinline__ uint64_t groups16(const FusedParams& p, const float (
 // sample recurrence issues its products as packed f32x2 (ema_next2, exact);
 // at the power-capped clock the pass is partly issue-bound, so fewer FP32
 // instructions per element show up as bandwidth.
-template <int WDT, int GDT, int M>
+//
+// PEER: the Fisher state starts as the sum of the p.nparts partial sums of a
+// sample-split pass (tb_score_mask_pack_peer); the headline instantiations
+// (PEER = false) compile without that branch.
+template <int WDT, int GDT, int M, bool PEER>
 __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParams p) {
     constexpr int GW = Vec16<GDT>::kWords;
     constexpr int U = (GW == 2) ? 4 : 2;  // samples in flight per thread
@@ -166,6 +187,14 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
 #pragma unroll
             for (int i = 0; i < kEpt; ++i) F[i] = ema_first(p.alpha, x[i]);
             s = 1;
+        } else if (PEER) {
+            load16_part(p.parts[0], e0, F);
+            for (int k = 1; k < p.nparts; ++k) {
+                float x[kEpt];
+                load16_part(p.parts[k], e0, x);
+#pragma unroll
+                for (int i = 0; i < kEpt; ++i) F[i] = __fadd_rn(F[i], x[i]);
+            }
         } else if (p.use_fin) {
             load16<TB_F32>(p.fin, e0, F);
         } else {
@@ -230,7 +259,10 @@ __global__ void __launch_bounds__(kThreads) fused_group_kernel(const FusedParams
             float f = 0.0f;
             size_t s = 0;
             if (p.first && p.S > 0) { f = ema_first(p.alpha, load_any(p.g, p.gdt, e)); s = 1; }
-            else if (p.use_fin) f = p.fin[e];
+            else if (p.nparts) {
+                f = __ldcs(p.parts[0] + e);
+                for (int q = 1; q < p.nparts; ++q) f = __fadd_rn(f, __ldcs(p.parts[q] + e));
+            } else if (p.use_fin) f = p.fin[e];
             for (; s < p.S; ++s) f = ema_next(f, p.beta, p.contrib, load_any(p.g, p.gdt, s * p.gstride + e));
             F[k] = f;
             w[k] = load_any(p.w, p.wdt, e);
@@ -258,11 +290,11 @@ unsigned grid_for(size_t items) {
     return static_cast<unsigned>(std::max<size_t>(1, std::min<size_t>(b, (size_t)1 << 30)));
 }
 
-template <int WDT, int GDT>
+template <int WDT, int GDT, bool PEER = false>
 void launch_vec_m(int m, unsigned grid, cudaStream_t st, const FusedParams& p) {
-    if (m == 2) fused_vec_kernel<WDT, GDT, 2><<<grid, kThreads, 0, st>>>(p);
-    else if (m == 4) fused_vec_kernel<WDT, GDT, 4><<<grid, kThreads, 0, st>>>(p);
-    else fused_vec_kernel<WDT, GDT, 8><<<grid, kThreads, 0, st>>>(p);
+    if (m == 2) fused_vec_kernel<WDT, GDT, 2, PEER><<<grid, kThreads, 0, st>>>(p);
+    else if (m == 4) fused_vec_kernel<WDT, GDT, 4, PEER><<<grid, kThreads, 0, st>>>(p);
+    else fused_vec_kernel<WDT, GDT, 8, PEER><<<grid, kThreads, 0, st>>>(p);
 }
 
 template <int WDT>
@@ -274,6 +306,12 @@ void launch_vec_g(int gdt, int m, unsigned grid, cudaStream_t st, const FusedPar
 
 void launch_vec(const FusedParams& p, int m, cudaStream_t st) {
     const unsigned grid = grid_for(p.N / kEpt);
+    if (p.nparts) {  // sample split: no gradient samples are read (S == 0)
+        if (p.wdt == TB_F32) launch_vec_m<TB_F32, TB_BF16, true>(m, grid, st, p);
+        else if (p.wdt == TB_BF16) launch_vec_m<TB_BF16, TB_BF16, true>(m, grid, st, p);
+        else launch_vec_m<TB_F16, TB_BF16, true>(m, grid, st, p);
+        return;
+    }
     if (p.wdt == TB_F32) launch_vec_g<TB_F32>(p.gdt, m, grid, st, p);
     else if (p.wdt == TB_BF16) launch_vec_g<TB_BF16>(p.gdt, m, grid, st, p);
     else launch_vec_g<TB_F16>(p.gdt, m, grid, st, p);
@@ -295,6 +333,12 @@ void launch_group(const FusedParams& p, int m, cudaStream_t st) {
 int dtype_bytes(int dt) { return dt == TB_F32 ? 4 : 2; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool parts_aligned16(const FusedParams& p) {
+    for (int k = 0; k < p.nparts; ++k)
+        if (!aligned16(p.parts[k])) return false;
+    return true;
+}
 
 // Validates args in the order the reference sequence would fail
 // (accumulate_fisher, compute_importance, generate_nm_mask) and fills the
@@ -363,7 +407,7 @@ int launch_fused(FusedParams p, int m, cudaStream_t st) {
                         (!p.use_fin || aligned16(p.fin)) && (!p.fout || aligned16(p.fout)) &&
                         (!p.sout || aligned16(p.sout)) &&
                         (reinterpret_cast<uintptr_t>(p.mout) % (kEpt / m) == 0) &&
-                        ((p.gstride * dtype_bytes(p.gdt)) % 16 == 0);
+                        ((p.gstride * dtype_bytes(p.gdt)) % 16 == 0) && parts_aligned16(p);
     const size_t nvec = vec_ok ? (p.N / kEpt) * kEpt : 0;
     if (nvec) {
         FusedParams q = p;
@@ -378,6 +422,7 @@ int launch_fused(FusedParams p, int m, cudaStream_t st) {
         t.w = static_cast<const char*>(p.w) + nvec * dtype_bytes(p.wdt);
         if (p.S) t.g = static_cast<const char*>(p.g) + nvec * dtype_bytes(p.gdt);
         if (p.fin) t.fin = p.fin + nvec;
+        for (int k = 0; k < p.nparts; ++k) t.parts[k] = p.parts[k] + nvec;
         t.wout = p.wout + nvec;
         t.mout = p.mout + nvec / m;
         if (p.fout) t.fout = p.fout + nvec;
@@ -476,6 +521,31 @@ int tb_score_mask_pack(const tb_prune_args* args, void* stream) {
     FusedParams p;
     int rc = prepare(args, p);
     if (rc) return rc;
+    return launch_fused(p, args->nm_m, static_cast<cudaStream_t>(stream));
+}
+
+int tb_score_mask_pack_peer(const tb_prune_args* args, const float* const* partials, int n_partials,
+                            void* stream) {
+    if (!args) return fail(TB_ERR_ARG, "null args");
+    if (n_partials < 1 || n_partials > kMaxParts)
+        return fail(TB_ERR_ARG, "tb_score_mask_pack_peer: %d partials (1..%d)", n_partials, kMaxParts);
+    if (!partials) return fail(TB_ERR_ARG, "tb_score_mask_pack_peer: null partials");
+    for (int k = 0; k < n_partials; ++k)
+        if (!partials[k]) return fail(TB_ERR_ARG, "tb_score_mask_pack_peer: partial %d is null", k);
+    if (args->S != 0 || args->fisher_in)
+        return fail(TB_ERR_ARG, "tb_score_mask_pack_peer: the partials are the Fisher state (S must be 0, "
+                                "fisher_in NULL)");
+    if (!args->use_fisher || args->fisher_steps_in == 0)
+        return fail(TB_ERR_ARG, "tb_score_mask_pack_peer: use_fisher with fisher_steps_in > 0 required");
+    tb_prune_args a = *args;
+    a.fisher_in = partials[0];  // passes the stateful-entry checks; replaced by the sum below
+    FusedParams p;
+    int rc = prepare(&a, p);
+    if (rc) return rc;
+    p.use_fin = 0;
+    p.fin = nullptr;
+    p.nparts = n_partials;
+    for (int k = 0; k < n_partials; ++k) p.parts[k] = partials[k];
     return launch_fused(p, args->nm_m, static_cast<cudaStream_t>(stream));
 }
 

@@ -2,6 +2,7 @@
 // (top-N tie tables, host-path staging buffers).
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
@@ -159,6 +160,52 @@ int tb_stream_sync(void* stream) {
     if (rc) return rc;
     cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaStreamSynchronize");
+}
+
+int tb_ipc_handle(const void* dev_ptr, void* handle_out) {
+    if (!dev_ptr || !handle_out) return fail(TB_ERR_ARG, "tb_ipc_handle: null pointer");
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    static_assert(sizeof(cudaIpcMemHandle_t) == TB_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    std::memcpy(handle_out, &h, sizeof(h));
+    return TB_OK;
+}
+
+int tb_ipc_open(const void* handle, void** dev_ptr_out) {
+    if (!handle || !dev_ptr_out) return fail(TB_ERR_ARG, "tb_ipc_open: null pointer");
+    *dev_ptr_out = nullptr;
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int tb_ipc_close(void* dev_ptr) {
+    if (!dev_ptr) return TB_OK;
+    cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int tb_enable_peer_access(int peer_device) {
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    int dev = 0, can = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceCanAccessPeer(&can, dev, peer_device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
+    if (peer_device == dev) return TB_OK;
+    if (!can) return fail(TB_ERR_UNSUPPORTED, "device %d cannot access device %d", dev, peer_device);
+    e = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+        return TB_OK;
+    }
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaDeviceEnablePeerAccess");
 }
 
 int tb_prepare_nm(int n, int m) {

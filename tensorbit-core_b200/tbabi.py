@@ -95,6 +95,10 @@ def lib() -> C.CDLL:
             "tb_memset": ([vp, i32, sz, vp], i32),
             "tb_stream_sync": ([vp], i32),
             "tb_prepare_nm": ([i32, i32], i32),
+            "tb_ipc_handle": ([vp, vp], i32),
+            "tb_ipc_open": ([vp, C.POINTER(vp)], i32),
+            "tb_ipc_close": ([vp], i32),
+            "tb_enable_peer_access": ([i32], i32),
             "tb_fisher_diagonal": ([vp, vp, sz, sz, vp], i32),
             "tb_fisher_accumulate": ([vp, vp, sz, f32, vp], i32),
             "tb_fisher_beta_decay": ([vp, f32, sz, vp], i32),
@@ -124,6 +128,7 @@ def lib() -> C.CDLL:
             "tb_obs_hessian_scaled": ([vp, i32, i32, f32, vp, vp], i32),
             "tb_obs_sparsegpt": ([vp, i32, i32, vp, f32, i32, i32, vp, vp, vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
+            "tb_score_mask_pack_peer": ([C.POINTER(PruneArgs), C.POINTER(vp), i32, vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),
             "tb_score_mask_pack_host_noalloc": ([C.POINTER(PruneArgs)], i32),
         }

@@ -8,14 +8,17 @@ docs prune shards in separate processes, docs/CLOUD.md:155-170):
   runs the fused pass on its range with no communication and writes its slice
   of the shared `.tb` file in place: weights at 4096 + 4*e0, mask bytes at
   masks_offset + e0/M.  Results are bit-identical to a single-GPU pass.
-* **sample splitting** (`prune_sample_split`): rank r holds a subset of the S
+* **sample splitting** (`prune_sample_split`, `prune_sample_split_peer`): rank r holds a subset of the S
   calibration gradients for all elements.  The EMA recurrence
   F_S = beta F_{S-1} + alpha (1-beta) g^2 (ehap.hpp:190-197) is regrouped as
   F = sum_t c_t g_t^2; each rank sums its own samples (tb_fisher_weighted_sum),
   one NCCL all-reduce adds the partials over NVLink, and every rank then scores,
-  masks and packs its group range from the summed Fisher.  F matches the serial
-  recurrence to FP32 rounding (the association differs), so masks can differ
-  only in near-tie groups, which the pass counts.
+  masks and packs its group range from the summed Fisher.  The peer variant
+  replaces the all-reduce by reads of the other ranks' partials inside the
+  pass itself (a reduce-scatter fused into score/mask/pack, half the NVLink
+  bytes of an all-reduce and no separate reduction kernel).  F matches the
+  serial recurrence to FP32 rounding (the association differs), so masks can
+  differ only in near-tie groups, which the pass counts.
 
 Column-block exact OBS of one layer (`obs_hessian_token_split`,
 `prune_obs_row_split`): the calibration tokens are split across ranks, each
@@ -199,6 +202,93 @@ def prune_sample_split(dist, torch, w_dev, w_dtype: int, g_local_dev, g_dtype: i
                           near_ties=ties.data_ptr(), **cfg)
         _check(tb.score_mask_pack(a, stream))
     return {"e0": e0, "e1": e1, "near_ties": ties, "fisher": F}
+
+
+class PeerBuffers:
+    """`count` device buffers of `nbytes` on every rank, each mapped into every
+    other rank's address space (tb_ipc_handle / tb_ipc_open over the process
+    group), for the sample-split pass that reads the ranks' partial Fisher sums
+    straight from peer memory.  ptrs[k][r] is rank r's buffer k as this rank's
+    kernels address it; local[k] is this rank's own."""
+
+    def __init__(self, dist, nbytes: int, count: int = 2):
+        self.dist = dist
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        L = tb.lib()
+        self.local = []
+        for _ in range(count):
+            p = C.c_void_p()
+            _check(L.tb_malloc(C.byref(p), nbytes))
+            self.local.append(p.value)
+        handles = []
+        for p in self.local:
+            h = C.create_string_buffer(64)
+            _check(L.tb_ipc_handle(p, h))
+            handles.append(h.raw)
+        every = [None] * self.world
+        dist.all_gather_object(every, handles)
+        self.opened = []
+        self.ptrs = []
+        for k in range(count):
+            row = []
+            for r in range(self.world):
+                if r == self.rank:
+                    row.append(self.local[k])
+                else:
+                    q = C.c_void_p()
+                    _check(L.tb_ipc_open(every[r][k], C.byref(q)))
+                    self.opened.append(q.value)
+                    row.append(q.value)
+            self.ptrs.append(row)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's; every rank must
+        have finished reading (a barrier comes first)."""
+        self.dist.barrier()
+        L = tb.lib()
+        for q in self.opened:
+            _check(L.tb_ipc_close(q))
+        self.dist.barrier()
+        for p in self.local:
+            _check(L.tb_free(p))
+        self.opened, self.local, self.ptrs = [], [], []
+
+
+def prune_sample_split_peer(dist, torch, bufs: PeerBuffers, k: int, w_dev, w_dtype: int, g_local_dev, g_dtype: int,
+                            S_total: int, s0: int, out_w, out_mask, *, n=2, m=4, alpha=0.01, beta=0.99,
+                            flag=None, fisher_out=None, near_ties=None, **cfg) -> dict:
+    """Sample-split pass of one tensor with the exchange fused into the pass:
+    this rank writes its partial Fisher (its samples [s0, s0 + S_local) of all
+    N elements) into its exchange buffer k, a one-element all-reduce orders
+    every rank's partial before any read (stream-ordered, no host wait), and
+    tb_score_mask_pack_peer sums the P partials of this rank's group range from
+    peer memory in rank order and prunes it.  Callers alternate k between
+    consecutive tensors: the next write into buffer k comes after the next
+    tensor's all-reduce, which every rank enters only after its read of buffer
+    k finished.  out_w / out_mask are full-size device tensors; this rank fills
+    [e0, e1)."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    N = w_dev.numel()
+    S_local = g_local_dev.shape[0] if g_local_dev is not None else 0
+    stream = torch.cuda.current_stream().cuda_stream
+    L = tb.lib()
+    c = ema_weights(S_total, alpha, beta)[s0:s0 + S_local].copy()
+    _check(L.tb_fisher_weighted_sum(bufs.local[k], g_local_dev.data_ptr() if S_local else None, g_dtype, S_local,
+                                    N, N, c.ctypes.data if S_local else None, 0, stream))
+    if flag is None:
+        flag = torch.zeros(1, dtype=torch.float32, device=w_dev.device)
+    dist.all_reduce(flag)
+    e0, e1 = group_shard(N, m, world, rank)
+    if e1 > e0:
+        parts = (C.c_void_p * world)(*[bufs.ptrs[k][r] + 4 * e0 for r in range(world)])
+        wsz = w_dev.element_size()
+        a = tb.prune_args(weights=w_dev.data_ptr() + e0 * wsz, w_dtype=w_dtype, grads=None, g_dtype=g_dtype, S=0,
+                          N=e1 - e0, fisher_steps_in=S_total, alpha=alpha, beta=beta, n=n, m=m,
+                          w_out=out_w.data_ptr() + 4 * e0, mask_out=out_mask.data_ptr() + e0 // m,
+                          fisher_out=(fisher_out.data_ptr() + 4 * e0) if fisher_out is not None else None,
+                          near_ties=near_ties.data_ptr() if near_ties is not None else None, **cfg)
+        _check(L.tb_score_mask_pack_peer(C.byref(a), C.cast(parts, C.POINTER(C.c_void_p)), world, stream))
+    return {"e0": e0, "e1": e1}
 
 
 # ---- column-block exact OBS --------------------------------------------------

@@ -1,7 +1,10 @@
-"""GPU, two or more devices: group sharding and NCCL sample splitting of one
+"""GPU, two or more devices: group sharding and sample splitting of one
 tensor's pass (tensorbit-core_b200/tbdist.py), checked against the single-GPU
-pass.  Group sharding must give the identical .tb file; sample splitting must
-give a Fisher within 1e-5 relative and masks equal outside near-tie groups."""
+pass.  Group sharding must give the identical .tb file; sample splitting, with
+the exchange as an NCCL all-reduce or fused into the pass over peer memory,
+must give a Fisher within 1e-5 relative and masks equal outside near-tie
+groups; the peer variant's Fisher must be exactly the rank-order sum of the
+ranks' partials."""
 import os
 import socket
 import sys
@@ -59,6 +62,23 @@ def _worker(rank, world, port_no, tmpdir):
     np.save(os.path.join(tmpdir, f"ss_m{rank}.npy"), out_m[e0 // 4:e1 // 4].cpu().numpy())
     np.save(os.path.join(tmpdir, f"ss_F{rank}.npy"), r["fisher"].cpu().numpy())
     np.save(os.path.join(tmpdir, f"ss_t{rank}.npy"), np.array([int(r["near_ties"].item()), e0, e1]))
+    # the same split with the exchange fused into the pass (peer reads of the partials)
+    bufs = td.PeerBuffers(dist, 4 * N, 2)
+    pw = torch.zeros(N, dtype=torch.float32, device="cuda")
+    pm = torch.zeros(N // 4, dtype=torch.uint8, device="cuda")
+    pF = torch.zeros(N, dtype=torch.float32, device="cuda")
+    for k in (0, 1, 0):  # reuse of buffer 0 after buffer 1 exercises the alternation
+        td.prune_sample_split_peer(dist, torch, bufs, k, wd, tb.BF16, gd, tb.BF16, S, s0, pw, pm,
+                                   strategy="optimal", redist="proportional", mode="obd", fisher_out=pF)
+    torch.cuda.synchronize()
+    part = torch.empty(N, dtype=torch.float32, device="cuda")
+    tb.check(tb.lib().tb_memcpy_d2d(part.data_ptr(), bufs.local[0], 4 * N, None))
+    torch.cuda.synchronize()
+    np.save(os.path.join(tmpdir, f"pp_part{rank}.npy"), part.cpu().numpy())
+    np.save(os.path.join(tmpdir, f"pp_w{rank}.npy"), pw[e0:e1].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"pp_m{rank}.npy"), pm[e0 // 4:e1 // 4].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"pp_F{rank}.npy"), pF[e0:e1].cpu().numpy())
+    bufs.close()
     dist.barrier(device_ids=[rank])
     dist.destroy_process_group()
 
@@ -93,6 +113,18 @@ def test_two_rank_group_shard_and_sample_split(cuda, tblib, port, tmp_path):
     assert not (differ & ~near).any(), "a mask differs outside the near-tie groups"
     same = np.repeat(~differ, 4)
     assert np.array_equal(wgot[same], wo[same])
+    # peer variant: F is exactly part_0 + part_1 (FP32, rank order) on each rank's range,
+    # within 1e-5 of the serial recurrence; masks equal the all-reduce variant's outside near ties
+    parts = [np.load(tmp_path / f"pp_part{r}.npy") for r in range(world)]
+    Fsum = (parts[0] + parts[1]).astype(np.float32)
+    Fp = np.concatenate([np.load(tmp_path / f"pp_F{r}.npy") for r in range(world)])
+    assert Fp.tobytes() == Fsum.tobytes()
+    np.testing.assert_allclose(Fp, Fo, rtol=1e-5, atol=0)
+    mp_ = np.concatenate([np.load(tmp_path / f"pp_m{r}.npy") for r in range(world)])
+    assert not ((mp_ != mo) & ~near).any(), "a peer-variant mask differs outside the near-tie groups"
+    wpp = np.concatenate([np.load(tmp_path / f"pp_w{r}.npy") for r in range(world)])
+    samep = np.repeat(mp_ == mo, 4)
+    assert np.array_equal(wpp[samep], wo[samep])
 
 
 def _obs_worker(rank, world, port_no, tmpdir):
