@@ -62,6 +62,10 @@ int         tb_device_count(int* count);
 int         tb_set_device(int device);
 int         tb_malloc(void** ptr, size_t bytes);  /* device memory for TensorDense (tensor.hpp:97-104) */
 int         tb_free(void* ptr);
+/* Page-locked host memory (usable from every device), for host buffers that
+ * feed tb_memcpy_h2d / tb_score_mask_pack_host at full PCIe speed. */
+int         tb_host_alloc(void** ptr, size_t bytes);
+int         tb_host_free(void* ptr);
 int         tb_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
 int         tb_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
 int         tb_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
@@ -279,6 +283,27 @@ typedef struct tb_prune_args {
 } tb_prune_args;
 
 int tb_score_mask_pack(const tb_prune_args* args, void* stream);
+
+/* tb-prune's per-tensor sequence (src/main.cpp:372-409) in three device
+ * passes: EHAPPruner::accumulate_fisher x S + compute_importance
+ * (ehap.hpp:148-285), the one-shot global select and apply (ehap.hpp:290-362,
+ * 425-439: keep = (size_t)(sparsity * (float)N), at least 1; every score >= the
+ * (N-keep)-th smallest kept, the rest zeroed), compute_importance again on the
+ * pruned weights, and CORINGPruner::prune + generate_nm_mask (coring.hpp:
+ * 90-313) with the .tb sections written - bit-identical to running those
+ * calls one after another (compensation none, Fisher normalisation off, as
+ * tb-prune configures them).  Pass 1 writes F (fisher_out, required when a
+ * Fisher state exists) and the scores (scores_out, required); the radix select
+ * ranks those scores; pass 2 recomputes each score, applies the threshold and
+ * runs CORING on the recomputed importance, writing w_out, mask_out and
+ * scores_out (now the importance CORING ranked).  *threshold_out (0 when
+ * everything is kept), *ehap_pruned_out (weights the threshold zeroed) and
+ * *coring_pruned_out (the analytic (N/M)*(M-N) of coring.hpp:192,222) are
+ * host values, any may be NULL; synchronises the stream.  Scratch: about
+ * 16 KB, stream-ordered.  Sparsity outside (0, 1) -> TB_ERR_CONFIG before any
+ * N:M check, as the reference's EHAP stage fails first. */
+int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* threshold_out,
+                         uint64_t* ehap_pruned_out, uint64_t* coring_pruned_out, void* stream);
 
 /* Sample-split pass: the reduction of the ranks' partial Fisher sums fused
  * into the score -> mask -> pack pass (a reduce-scatter over peer memory).

@@ -14,15 +14,19 @@
 
 #include <algorithm>
 #include <charconv>
+#include <condition_variable>
+#include <deque>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <filesystem>
 #include <fstream>
+#include <mutex>
 #include <random>
 #include <span>
 #include <string>
 #include <string_view>
+#include <thread>
 #include <vector>
 
 #include "tb_kernels.h"
@@ -51,6 +55,7 @@ struct Options {
     int vocab_size = 32000, max_seq_len = 2048;
     float norm_eps = 1e-5f, rope_theta = 10000.0f;
     bool use_mock = false, show_help = false, show_version = false;
+    int gpus = 1;  // devices pruning whole tensors side by side in real mode
 };
 
 void usage(const char* prog) {
@@ -67,6 +72,7 @@ void usage(const char* prog) {
                  "  --vocab-size N, --max-seq-len N   model.tbm config fields\n"
                  "  --damping VAL       EHAP Fisher damping                  [default: 0.01]\n"
                  "  --mock-size N       elements of the mock tensor          [default: 4096]\n"
+                 "  --gpus N            GPUs pruning tensors side by side    [default: 1, real mode]\n"
                  "  --help, -h / --version\n",
                  prog);
 }
@@ -158,6 +164,20 @@ TensorDense<float> device_copy(const float* host, std::size_t n) {
     return d;
 }
 
+/// dst = src * f element by element (FP32, round to nearest) on the device:
+/// a device copy followed by the legacy launcher that multiplies in place
+/// (launch_fisher_beta_decay, kernels.hpp:51-54); the product is the same
+/// single multiplication as the reference's host loops.
+bool scaled_copy(const TensorDense<float>& src, float f, TensorDense<float>& dst) {
+    if (src.empty()) return true;
+    if (tb_memcpy_d2d(dst.data(), src.data(), src.bytes(), nullptr) ||
+        tb_fisher_beta_decay(dst.data(), f, src.size(), nullptr)) {
+        TENSORBIT_LOG_ERROR("device scale failed: {}", tb_last_error());
+        return false;
+    }
+    return true;
+}
+
 struct Pruned {
     std::vector<float> weights;
     std::vector<uint8_t> masks;
@@ -167,18 +187,73 @@ struct Pruned {
 
 enum class Stage { kOk, kEhap, kCoring };
 
+/// The OneShot sequence of src/main.cpp:372-409 (accumulate_fisher with alpha
+/// 0.01, EHAP one-shot prune, compute_importance, CORING top-N prune with
+/// proportional redistribution, generate_nm_mask) as one library call: two
+/// fused passes around the global radix select, bit-identical to the calls
+/// made one by one.  EHAP's own failures (empty tensor, sparsity) are ruled
+/// out before, so a failed call is CORING's (N:M, numel % M) or the device's.
+Stage prune_one_shot_fused(const Options& o, const TensorDense<float>& w, const TensorDense<float>& g, Pruned& out) {
+    const std::size_t n = w.size();
+    const std::size_t groups = n / static_cast<std::size_t>(o.nm_m);
+    const bool fisher = o.method != "Magnitude";
+    if (n == 0 || !(o.sparsity_ratio > 0.0f && o.sparsity_ratio < 1.0f)) return Stage::kEhap;
+    TensorDense<float> wo(w.shape(), DeviceLocation::kDevice), F(w.shape(), DeviceLocation::kDevice),
+        s(w.shape(), DeviceLocation::kDevice);
+    TensorDense<uint8_t> mk(std::span<const std::size_t>(&groups, 1), DeviceLocation::kDevice);
+    tb_prune_args a{};
+    a.struct_size = sizeof(a);
+    a.weights = w.data();
+    a.w_dtype = TB_F32;
+    a.grads = fisher ? g.data() : nullptr;
+    a.g_dtype = TB_F32;
+    a.S = fisher ? 1 : 0;
+    a.N = n;
+    a.alpha = 0.01f;  // src/main.cpp:375
+    a.beta = ehap_config(o).ema_decay;
+    a.damping = o.damping;
+    a.importance_mode = TB_IMP_OBD;
+    a.use_fisher = fisher ? 1 : 0;
+    a.nm_n = o.nm_n;
+    a.nm_m = o.nm_m;
+    a.mask_strategy = TB_MASK_TOPN;
+    a.iterative_rounds = 3;
+    a.redist_mode = TB_REDIST_PROPORTIONAL;
+    a.w_out = wo.data();
+    a.mask_out = mk.data();
+    a.fisher_out = F.data();
+    a.scores_out = s.data();
+    uint64_t ehap_pruned = 0, coring_pruned = 0;
+    if (tb_prune_one_shot_nm(&a, o.sparsity_ratio, nullptr, &ehap_pruned, &coring_pruned, nullptr)) {
+        TENSORBIT_LOG_DEBUG("one-shot N:M pass: {}", tb_last_error());
+        return Stage::kCoring;
+    }
+    out.ehap_pruned = ehap_pruned;
+    out.coring_pruned = coring_pruned;
+    out.weights.resize(n);
+    out.masks.resize(groups);
+    if (tb_memcpy_d2h(out.weights.data(), wo.data(), wo.bytes(), nullptr) ||
+        tb_memcpy_d2h(out.masks.data(), mk.data(), groups, nullptr) || tb_stream_sync(nullptr)) {
+        TENSORBIT_LOG_ERROR("device to host copy failed: {}", tb_last_error());
+        return Stage::kCoring;
+    }
+    return Stage::kOk;
+}
+
 /// The per-tensor sequence of src/main.cpp:372-409 on device tensors.
 Stage prune_tensor(const Options& o, TensorDense<float>& w, const TensorDense<float>& g, Pruned& out) {
+    if (o.strategy != "Iterative" && o.strategy != "BlockOBS") return prune_one_shot_fused(o, w, g, out);
     const auto shape = w.shape();
     EHAPPruner<float> ehap(ehap_config(o));
     ehap.accumulate_fisher(g, 0.01f);
     if (o.strategy == "BlockOBS" && o.method != "Magnitude") {
         for (int k = 0; k < 4; ++k) {
-            // Snapshot k = g * (0.9 + 0.02 k), scaled on the host as the reference does.
-            auto hg = g.to_host();
+            // Snapshot k = g * (0.9 + 0.02 k): the reference scales a host copy,
+            // one float product per element; the same product on the device.
             const float f = 0.9f + 0.02f * static_cast<float>(k);
-            for (std::size_t i = 0; i < hg.size(); ++i) hg[i] *= f;
-            ehap.store_gradient(hg);
+            TensorDense<float> snap(shape, DeviceLocation::kDevice);
+            if (!scaled_copy(g, f, snap)) return Stage::kEhap;
+            ehap.store_gradient(snap);
         }
     }
     auto er = ehap.prune(w);
@@ -245,6 +320,174 @@ struct TbmEntry {
     int nm_n, nm_m;
 };
 
+/// One eligible tensor of a real-mode run as it moves through the pipeline.
+struct Job {
+    const loader::TensorMeta* meta = nullptr;
+    std::byte* raw = nullptr;  // pinned host copy of the tensor's bytes
+    std::size_t cap = 0;
+    bool read_ok = false;
+    bool done = false;
+    Stage stage = Stage::kOk;
+    bool skip_silently = false;  // a device copy failed after decoding (the reference's silent `continue`)
+    Pruned result;
+};
+
+/// Real mode as a pipeline over the tensors of one .safetensors file.  A reader
+/// thread copies the next tensors' bytes into page-locked buffers (at most
+/// `gpus + 1` ahead); one worker thread per GPU takes whole tensors, which are
+/// independent, and runs decode -> gradients -> EHAP -> CORING -> mask on its
+/// device; the calling thread logs and writes the .tb files in tensor order.
+/// Files, the model.tbm container and messages are those of the serial
+/// reference loop (src/main.cpp:437-636); only the overlap of disk, PCIe and
+/// GPU work differs.
+class Pipeline {
+public:
+    Pipeline(const Options& o, loader::SafeTensorsFile& sf, std::vector<Job>& jobs, int gpus)
+        : o_(o), sf_(sf), jobs_(jobs), gpus_(gpus) {}
+
+    void start() {
+        reader_ = std::thread([this] { read_all(); });
+        for (int d = 0; d < gpus_; ++d) workers_.emplace_back([this, d] { work(d); });
+    }
+
+    /// Blocks until job i is finished.  At most `gpus + 1` jobs are between
+    /// being read and being released by the caller, which bounds the pinned
+    /// buffers and the host copies of finished outputs.
+    Job& wait(std::size_t i) {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_done_.wait(lk, [&] { return jobs_[i].done; });
+        return jobs_[i];
+    }
+
+    void join() {
+        if (reader_.joinable()) reader_.join();
+        for (auto& t : workers_) t.join();
+        for (auto& b : pool_) tb_host_free(b.first);
+        pool_.clear();
+    }
+
+private:
+    void read_all() {
+        for (std::size_t i = 0; i < jobs_.size(); ++i) {
+            Job& j = jobs_[i];
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_room_.wait(lk, [&] { return in_flight_ < static_cast<std::size_t>(gpus_ + 1); });
+                ++in_flight_;
+                take_buffer(j);  // under the lock: the pool is shared with the workers
+            }
+            if (j.raw) j.read_ok = static_cast<bool>(sf_.read_tensor_data(*j.meta, std::span<std::byte>(j.raw, j.meta->length)));
+            else j.read_ok = j.meta->length == 0;
+            {
+                std::lock_guard<std::mutex> lk(mu_);
+                ready_.push_back(i);
+            }
+            cv_ready_.notify_one();
+        }
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            reader_done_ = true;
+        }
+        cv_ready_.notify_all();
+    }
+
+    // A pooled pinned buffer of at least the tensor's size, or a new one.
+    void take_buffer(Job& j) {
+        const std::size_t need = j.meta->length;
+        if (need == 0) return;
+        std::size_t best = pool_.size();
+        for (std::size_t k = 0; k < pool_.size(); ++k)
+            if (pool_[k].second >= need && (best == pool_.size() || pool_[k].second < pool_[best].second)) best = k;
+        if (best < pool_.size()) {
+            j.raw = pool_[best].first;
+            j.cap = pool_[best].second;
+            pool_.erase(pool_.begin() + static_cast<std::ptrdiff_t>(best));
+            return;
+        }
+        void* p = nullptr;
+        if (tb_host_alloc(&p, need) == TB_OK) {
+            j.raw = static_cast<std::byte*>(p);
+            j.cap = need;
+        }
+    }
+
+    void give_back(Job& j) {
+        std::lock_guard<std::mutex> lk(mu_);
+        if (j.raw) pool_.emplace_back(j.raw, j.cap);
+        j.raw = nullptr;
+    }
+
+public:
+    /// The caller is done with a finished job (written or skipped): its
+    /// outputs are dropped and the reader may read one tensor further ahead.
+    void release(Job& j) {
+        j.result = Pruned{};
+        std::lock_guard<std::mutex> lk(mu_);
+        --in_flight_;
+        cv_room_.notify_one();
+    }
+
+private:
+
+    void work(int dev) {
+        const bool device_ok = tb_set_device(dev) == TB_OK;
+        for (;;) {
+            std::size_t i;
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_ready_.wait(lk, [&] { return !ready_.empty() || reader_done_; });
+                if (ready_.empty()) return;
+                i = ready_.front();
+                ready_.pop_front();
+            }
+            Job& j = jobs_[i];
+            if (j.read_ok && device_ok) run(j);
+            else j.read_ok = false;
+            give_back(j);
+            {
+                std::lock_guard<std::mutex> lk(mu_);
+                j.done = true;
+            }
+            cv_done_.notify_all();
+        }
+    }
+
+    // Widen on the device (src/main.cpp:213-245), then gradients = 0.01 * w
+    // (src/main.cpp:253-259, the same float product on the device), then the
+    // pruner sequence.
+    void run(Job& j) {
+        const auto& meta = *j.meta;
+        const std::size_t n = meta.numel;
+        const int dt = meta.dtype == loader::STDtype::kF32 ? TB_F32 : meta.dtype == loader::STDtype::kBF16 ? TB_BF16 : TB_F16;
+        TensorDense<uint8_t> draw(std::span<const std::size_t>(&meta.length, 1), DeviceLocation::kDevice);
+        TensorDense<float> w(std::span<const std::size_t>(meta.shape.data(), meta.shape.size()), DeviceLocation::kDevice);
+        if (w.size() != n || (n && (tb_memcpy_h2d(draw.data(), j.raw, meta.length, nullptr) ||
+                                    tb_decode_to_f32(draw.data(), dt, w.data(), n, nullptr) || tb_stream_sync(nullptr)))) {
+            j.read_ok = false;
+            return;
+        }
+        TensorDense<float> g(w.shape(), DeviceLocation::kDevice);
+        if (n && (!scaled_copy(w, 0.01f, g) || tb_stream_sync(nullptr))) {
+            j.skip_silently = true;
+            return;
+        }
+        j.stage = w.empty() ? Stage::kEhap : prune_tensor(o_, w, g, j.result);
+    }
+
+    const Options& o_;
+    loader::SafeTensorsFile& sf_;
+    std::vector<Job>& jobs_;
+    int gpus_;
+    std::thread reader_;
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_room_, cv_ready_, cv_done_;
+    std::deque<std::size_t> ready_;
+    std::vector<std::pair<std::byte*, std::size_t>> pool_;
+    std::size_t in_flight_ = 0;
+    bool reader_done_ = false;
+};
+
 int run_model(const Options& o) {
     loader::SafeTensorsFile sf;
     if (auto r = sf.open(o.model_path); !r) {
@@ -260,32 +503,29 @@ int run_model(const Options& o) {
     std::vector<TbmEntry> entries;
     std::size_t count = 0, total = 0, total_pruned = 0;
     TENSORBIT_LOG_INFO("[Load] Processing {} tensor(s) from '{}'", metas.size(), o.model_path);
-    for (const auto& meta : metas) {
-        if (meta.dtype != loader::STDtype::kF32 && meta.dtype != loader::STDtype::kBF16 &&
-            meta.dtype != loader::STDtype::kF16)
-            continue;
-        std::vector<std::byte> raw(meta.length);
-        if (!sf.read_tensor_data(meta, raw)) { TENSORBIT_LOG_WARN("  SKIP {}: read error", meta.name); continue; }
-        // Widen on the device (src/main.cpp:213-245), then gradients = 0.01 * w (src/main.cpp:253-259).
-        const std::size_t n = meta.numel;
-        const int dt = meta.dtype == loader::STDtype::kF32 ? TB_F32 : meta.dtype == loader::STDtype::kBF16 ? TB_BF16 : TB_F16;
-        TensorDense<uint8_t> draw(std::span<const std::size_t>(&meta.length, 1), DeviceLocation::kDevice);
-        TensorDense<float> w(std::span<const std::size_t>(meta.shape.data(), meta.shape.size()), DeviceLocation::kDevice);
-        if (w.size() != n || (n && (tb_memcpy_h2d(draw.data(), raw.data(), meta.length, nullptr) ||
-                                    tb_decode_to_f32(draw.data(), dt, w.data(), n, nullptr) || tb_stream_sync(nullptr)))) {
-            TENSORBIT_LOG_WARN("  SKIP {}: read error", meta.name);
-            continue;
+    std::vector<Job> jobs;
+    for (const auto& meta : metas)
+        if (meta.dtype == loader::STDtype::kF32 || meta.dtype == loader::STDtype::kBF16 ||
+            meta.dtype == loader::STDtype::kF16) {
+            jobs.emplace_back();
+            jobs.back().meta = &meta;
         }
-        auto hw = w.to_host();
-        std::vector<float> hg(n);
-        for (std::size_t i = 0; i < n; ++i) hg[i] = hw[i] * 0.01f;
-        TensorDense<float> g(w.shape(), DeviceLocation::kDevice);
-        if (n && (tb_memcpy_h2d(g.data(), hg.data(), n * 4, nullptr) || tb_stream_sync(nullptr))) continue;
+    Pipeline pipe(o, sf, jobs, o.gpus);
+    pipe.start();
+    for (std::size_t i = 0; i < jobs.size(); ++i) {
+        Job& j = pipe.wait(i);
+        struct Release {
+            Pipeline& p;
+            Job& j;
+            ~Release() { p.release(j); }
+        } release{pipe, j};
+        const auto& meta = *j.meta;
+        if (!j.read_ok) { TENSORBIT_LOG_WARN("  SKIP {}: read error", meta.name); continue; }
+        if (j.skip_silently) continue;
         TENSORBIT_LOG_INFO("  [{}] {} — {} elements", count, meta.name, meta.numel);
-        Pruned p;
-        const Stage s = w.empty() ? Stage::kEhap : prune_tensor(o, w, g, p);
-        if (s == Stage::kEhap) { TENSORBIT_LOG_WARN("    SKIP (EHAP failed)"); continue; }
-        if (s == Stage::kCoring) { TENSORBIT_LOG_WARN("    SKIP (CORING failed)"); continue; }
+        const Pruned& p = j.result;
+        if (j.stage == Stage::kEhap) { TENSORBIT_LOG_WARN("    SKIP (EHAP failed)"); continue; }
+        if (j.stage == Stage::kCoring) { TENSORBIT_LOG_WARN("    SKIP (CORING failed)"); continue; }
         const auto fname = sanitise(meta.name) + ".tb";
         const auto path = out_dir / fname;
         TBWriter writer;
@@ -302,6 +542,7 @@ int run_model(const Options& o) {
         total += meta.numel;
         total_pruned += p.coring_pruned;
     }
+    pipe.join();
     sf.close();
     if (!entries.empty()) {
         const auto tbm_path = out_dir / "model.tbm";
@@ -375,6 +616,7 @@ int main(int argc, char** argv) {
         else if (a == "--max-seq-len") parse_number(next(), o.max_seq_len);
         else if (a == "--damping") parse_number(next(), o.damping);
         else if (a == "--mock-size") { parse_number(next(), o.mock_size); o.use_mock = true; }
+        else if (a == "--gpus") parse_number(next(), o.gpus);
         else if (a == "--help" || a == "-h") o.show_help = true;
         else if (a == "--version") o.show_version = true;
         else TENSORBIT_LOG_WARN("Unknown flag: '{}'", a);
@@ -386,6 +628,10 @@ int main(int argc, char** argv) {
     tb_device_count(&ndev);
     if (ndev == 0) {
         TENSORBIT_LOG_FATAL("no CUDA device: tb-prune runs every stage on the GPU");
+        return 1;
+    }
+    if (o.gpus < 1 || o.gpus > ndev) {
+        TENSORBIT_LOG_FATAL("--gpus {} outside 1..{} (visible devices)", o.gpus, ndev);
         return 1;
     }
     TENSORBIT_LOG_INFO("Tensorbit Core v0.2.0 — Pruning Pipeline (B200)");

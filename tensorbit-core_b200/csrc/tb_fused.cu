@@ -20,6 +20,7 @@
 
 #include "tb_device.cuh"
 #include "tb_runtime.h"
+#include "tb_threshold.h"
 
 namespace tb {
 namespace {
@@ -27,6 +28,13 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kEpt = 16;  // elements per thread in the vector kernel
 constexpr int kMaxParts = 8;  // partial Fisher sums of a sample-split pass (ranks of one node)
+
+// Variants of the pass (template argument of the vector kernel, p.variant in
+// the scalar one).
+constexpr int kVarPlain = 0;      // score -> mask -> pack
+constexpr int kVarPeer = 1;       // Fisher state = sum of peer partials (sample split)
+constexpr int kVarScores = 2;     // Fisher and importance only: writes fout / sout, no mask
+constexpr int kVarThreshold = 3;  // EHAP one-shot keep (s >= *thr) before CORING (tb-prune sequence)
 
 struct FusedParams {
     const void* w;
@@ -50,6 +58,9 @@ struct FusedParams {
     int wdt, gdt;    // dtypes (generic kernel)
     int nparts;      // > 0: F starts as the sum of parts[0..nparts) (sample split)
     const float* parts[kMaxParts];
+    int variant;     // kVar*
+    const float* thr;              // kVarThreshold: device address of the EHAP threshold
+    unsigned long long* thr_pruned;  // kVarThreshold: counter of weights the threshold zeroes
 };
 
 // --- 16-element vector loads --------------------------------------------------
@@ -125,10 +136,12 @@ __device__ __forceinline__ void load16_part(const float* base, size_t e0, float 
     }
 }
 
-__device__ __forceinline__ void count_ties(unsigned long long* ties, int local) {
+// Adds the active lanes' counts to a device counter with one atomic per warp.
+__device__ __forceinline__ void warp_add_count(unsigned long long* counter, int local) {
     const unsigned active = __activemask();
     const int total = __reduce_add_sync(active, local);
-    if (total && (threadIdx.x & 31) == (__ffs(active) - 1)) atomicAdd(ties, static_cast<unsigned long long>(total));
+    if (total && (threadIdx.x & 31) == (__ffs(active) - 1))
+        atomicAdd(counter, static_cast<unsigned long long>(total));
 }
 
 // Stage 2 on one thread's 16 scores: select, apply, redistribute; returns the
@@ -161,10 +174,13 @@ __device__ __forceinline__ uint64_t groups16(const FusedParams& p, const float (
 // at the power-capped clock the pass is partly issue-bound, so fewer FP32
 // instructions per element show up as bandwidth.
 //
-// PEER: the Fisher state starts as the sum of the p.nparts partial sums of a
-// sample-split pass (tb_score_mask_pack_peer); the headline instantiations
-// (PEER = false) compile without that branch.
-template <int WDT, int GDT, int M, bool PEER>
+// VAR selects a variant (kVar*); the plain instantiations compile without the
+// other variants' code.  kVarPeer: the Fisher state starts as the sum of the
+// p.nparts partial sums of a sample-split pass (tb_score_mask_pack_peer).
+// kVarScores: stage 1 and the importance only.  kVarThreshold: the EHAP
+// one-shot keep rule s >= threshold zeroes weights before the importance that
+// CORING ranks is recomputed (tb_prune_one_shot_nm).
+template <int WDT, int GDT, int M, int VAR>
 __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParams p) {
     constexpr int GW = Vec16<GDT>::kWords;
     constexpr int U = (GW == 2) ? 4 : 2;  // samples in flight per thread
@@ -172,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
     const size_t nchunks = p.N / kEpt;
     const size_t gstride_b = p.gstride * Dtype<GDT>::kBytes;
     int ties = 0;
+    int zeroed = 0;  // kVarThreshold
     for (size_t c = blockIdx.x * (size_t)kThreads + threadIdx.x; c < nchunks; c += (size_t)gridDim.x * kThreads) {
         const size_t e0 = c * kEpt;
         float F[kEpt];
@@ -187,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
 #pragma unroll
             for (int i = 0; i < kEpt; ++i) F[i] = ema_first(p.alpha, x[i]);
             s = 1;
-        } else if (PEER) {
+        } else if (VAR == kVarPeer) {
             load16_part(p.parts[0], e0, F);
             for (int k = 1; k < p.nparts; ++k) {
                 float x[kEpt];
@@ -229,6 +246,24 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
         float w[kEpt], sc[kEpt];
         load16<WDT>(p.w, e0, w);
         const bool have_f = p.have_f != 0;
+        if (VAR == kVarScores) {
+#pragma unroll
+            for (int i = 0; i < kEpt; ++i) sc[i] = importance(w[i], F[i], p.damp, p.mode, have_f);
+            if (p.fout && have_f) store16(p.fout, e0, F);
+            store16(p.sout, e0, sc);
+            continue;
+        }
+        if (VAR == kVarThreshold) {
+            // select_pruning_mask + apply_mask (ehap.hpp:313-362): keep where
+            // s >= threshold, others become +0 (NaN scores are not kept).
+            const float thr = *p.thr;
+#pragma unroll
+            for (int i = 0; i < kEpt; ++i) {
+                const bool keep = importance(w[i], F[i], p.damp, p.mode, have_f) >= thr;
+                w[i] = keep ? w[i] : 0.0f;
+                zeroed += keep ? 0 : 1;
+            }
+        }
 #pragma unroll
         for (int i = 0; i < kEpt; ++i) sc[i] = importance(w[i], F[i], p.damp, p.mode, have_f);
         // ---- stage 2: select, apply, redistribute, pack ----
@@ -241,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
         if (p.fout && have_f) store16(p.fout, e0, F);
         if (p.sout) store16(p.sout, e0, sc);
     }
-    if (p.ties) count_ties(p.ties, ties);
+    if (p.ties) warp_add_count(p.ties, ties);
+    if (VAR == kVarThreshold) warp_add_count(p.thr_pruned, zeroed);
 }
 
 // Generic kernel: one group of M elements per thread, scalar loads; covers any
@@ -250,6 +286,7 @@ template <int M>
 __global__ void __launch_bounds__(kThreads) fused_group_kernel(const FusedParams p) {
     const size_t G = p.N / M;
     int ties = 0;
+    int zeroed = 0;
     for (size_t g = blockIdx.x * (size_t)kThreads + threadIdx.x; g < G; g += (size_t)gridDim.x * kThreads) {
         const size_t e0 = g * M;
         float F[M], w[M], sc[M], v[M];
@@ -266,8 +303,21 @@ __global__ void __launch_bounds__(kThreads) fused_group_kernel(const FusedParams
             for (; s < p.S; ++s) f = ema_next(f, p.beta, p.contrib, load_any(p.g, p.gdt, s * p.gstride + e));
             F[k] = f;
             w[k] = load_any(p.w, p.wdt, e);
+            if (p.variant == kVarThreshold) {
+                const bool keep = importance(w[k], f, p.damp, p.mode, p.have_f != 0) >= *p.thr;
+                zeroed += keep ? 0 : 1;
+                w[k] = keep ? w[k] : 0.0f;
+            }
             sc[k] = importance(w[k], f, p.damp, p.mode, p.have_f != 0);
             v[k] = sc[k];
+        }
+        if (p.variant == kVarScores) {
+#pragma unroll
+            for (int k = 0; k < M; ++k) {
+                if (p.fout && p.have_f) p.fout[e0 + k] = F[k];
+                p.sout[e0 + k] = sc[k];
+            }
+            continue;
         }
         if (p.ties) ties += near_tie<M>(v, p.n) ? 1 : 0;
         const uint32_t byte = select_group<M>(v, p.n, p.strategy, p.rounds, p.permute != 0, p.lut);
@@ -282,7 +332,8 @@ __global__ void __launch_bounds__(kThreads) fused_group_kernel(const FusedParams
         }
         p.mout[g] = static_cast<uint8_t>(byte);
     }
-    if (p.ties) count_ties(p.ties, ties);
+    if (p.ties) warp_add_count(p.ties, ties);
+    if (p.variant == kVarThreshold) warp_add_count(p.thr_pruned, zeroed);
 }
 
 unsigned grid_for(size_t items) {
@@ -290,31 +341,42 @@ unsigned grid_for(size_t items) {
     return static_cast<unsigned>(std::max<size_t>(1, std::min<size_t>(b, (size_t)1 << 30)));
 }
 
-template <int WDT, int GDT, bool PEER = false>
+template <int WDT, int GDT, int VAR = kVarPlain>
 void launch_vec_m(int m, unsigned grid, cudaStream_t st, const FusedParams& p) {
-    if (m == 2) fused_vec_kernel<WDT, GDT, 2, PEER><<<grid, kThreads, 0, st>>>(p);
-    else if (m == 4) fused_vec_kernel<WDT, GDT, 4, PEER><<<grid, kThreads, 0, st>>>(p);
-    else fused_vec_kernel<WDT, GDT, 8, PEER><<<grid, kThreads, 0, st>>>(p);
+    if (m == 2) fused_vec_kernel<WDT, GDT, 2, VAR><<<grid, kThreads, 0, st>>>(p);
+    else if (m == 4) fused_vec_kernel<WDT, GDT, 4, VAR><<<grid, kThreads, 0, st>>>(p);
+    else fused_vec_kernel<WDT, GDT, 8, VAR><<<grid, kThreads, 0, st>>>(p);
 }
 
-template <int WDT>
+template <int WDT, int VAR>
 void launch_vec_g(int gdt, int m, unsigned grid, cudaStream_t st, const FusedParams& p) {
-    if (gdt == TB_F32) launch_vec_m<WDT, TB_F32>(m, grid, st, p);
-    else if (gdt == TB_BF16) launch_vec_m<WDT, TB_BF16>(m, grid, st, p);
-    else launch_vec_m<WDT, TB_F16>(m, grid, st, p);
+    if (gdt == TB_F32) launch_vec_m<WDT, TB_F32, VAR>(m, grid, st, p);
+    else if (gdt == TB_BF16) launch_vec_m<WDT, TB_BF16, VAR>(m, grid, st, p);
+    else launch_vec_m<WDT, TB_F16, VAR>(m, grid, st, p);
+}
+
+// Variants that read no gradient samples (S == 0) are instantiated for one
+// gradient type only.
+template <int VAR>
+void launch_vec_nosamples(int m, unsigned grid, cudaStream_t st, const FusedParams& p) {
+    if (p.wdt == TB_F32) launch_vec_m<TB_F32, TB_BF16, VAR>(m, grid, st, p);
+    else if (p.wdt == TB_BF16) launch_vec_m<TB_BF16, TB_BF16, VAR>(m, grid, st, p);
+    else launch_vec_m<TB_F16, TB_BF16, VAR>(m, grid, st, p);
 }
 
 void launch_vec(const FusedParams& p, int m, cudaStream_t st) {
     const unsigned grid = grid_for(p.N / kEpt);
-    if (p.nparts) {  // sample split: no gradient samples are read (S == 0)
-        if (p.wdt == TB_F32) launch_vec_m<TB_F32, TB_BF16, true>(m, grid, st, p);
-        else if (p.wdt == TB_BF16) launch_vec_m<TB_BF16, TB_BF16, true>(m, grid, st, p);
-        else launch_vec_m<TB_F16, TB_BF16, true>(m, grid, st, p);
+    if (p.variant == kVarPeer) return launch_vec_nosamples<kVarPeer>(m, grid, st, p);
+    if (p.variant == kVarThreshold) return launch_vec_nosamples<kVarThreshold>(m, grid, st, p);
+    if (p.variant == kVarScores) {
+        if (p.wdt == TB_F32) launch_vec_g<TB_F32, kVarScores>(p.gdt, m, grid, st, p);
+        else if (p.wdt == TB_BF16) launch_vec_g<TB_BF16, kVarScores>(p.gdt, m, grid, st, p);
+        else launch_vec_g<TB_F16, kVarScores>(p.gdt, m, grid, st, p);
         return;
     }
-    if (p.wdt == TB_F32) launch_vec_g<TB_F32>(p.gdt, m, grid, st, p);
-    else if (p.wdt == TB_BF16) launch_vec_g<TB_BF16>(p.gdt, m, grid, st, p);
-    else launch_vec_g<TB_F16>(p.gdt, m, grid, st, p);
+    if (p.wdt == TB_F32) launch_vec_g<TB_F32, kVarPlain>(p.gdt, m, grid, st, p);
+    else if (p.wdt == TB_BF16) launch_vec_g<TB_BF16, kVarPlain>(p.gdt, m, grid, st, p);
+    else launch_vec_g<TB_F16, kVarPlain>(p.gdt, m, grid, st, p);
 }
 
 void launch_group(const FusedParams& p, int m, cudaStream_t st) {
@@ -423,8 +485,8 @@ int launch_fused(FusedParams p, int m, cudaStream_t st) {
         if (p.S) t.g = static_cast<const char*>(p.g) + nvec * dtype_bytes(p.gdt);
         if (p.fin) t.fin = p.fin + nvec;
         for (int k = 0; k < p.nparts; ++k) t.parts[k] = p.parts[k] + nvec;
-        t.wout = p.wout + nvec;
-        t.mout = p.mout + nvec / m;
+        if (p.wout) t.wout = p.wout + nvec;
+        if (p.mout) t.mout = p.mout + nvec / m;
         if (p.fout) t.fout = p.fout + nvec;
         if (p.sout) t.sout = p.sout + nvec;
         launch_group(t, m, st);
@@ -545,8 +607,66 @@ int tb_score_mask_pack_peer(const tb_prune_args* args, const float* const* parti
     p.use_fin = 0;
     p.fin = nullptr;
     p.nparts = n_partials;
+    p.variant = kVarPeer;
     for (int k = 0; k < n_partials; ++k) p.parts[k] = partials[k];
     return launch_fused(p, args->nm_m, static_cast<cudaStream_t>(stream));
+}
+
+int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* threshold_out,
+                         uint64_t* ehap_pruned_out, uint64_t* coring_pruned_out, void* stream) {
+    if (!args) return fail(TB_ERR_ARG, "null args");
+    // EHAP's checks come first, as in the reference sequence (the global select
+    // runs before CORING sees the tensor).
+    size_t keep = 0;
+    int rc = threshold_args(args->N, sparsity, &keep);
+    if (rc) return rc;
+    FusedParams p;
+    if ((rc = prepare(args, p))) return rc;
+    if (!args->scores_out) return fail(TB_ERR_ARG, "tb_prune_one_shot_nm: scores_out is required");
+    if (p.have_f && !args->fisher_out)
+        return fail(TB_ERR_ARG, "tb_prune_one_shot_nm: fisher_out is required when a Fisher state exists");
+    const int m = args->nm_m;
+    const size_t N = args->N;
+    auto st = static_cast<cudaStream_t>(stream);
+    // Pass 1: Fisher EMA and the importance the global select ranks.
+    FusedParams a = p;
+    a.variant = kVarScores;
+    a.wout = nullptr;
+    a.mout = nullptr;
+    a.ties = nullptr;
+    a.fout = p.have_f ? args->fisher_out : nullptr;
+    a.sout = args->scores_out;
+    if ((rc = launch_fused(a, m, st))) return rc;
+    // The threshold's three digit passes over the scores (keep < N).
+    SelectState* sel = nullptr;
+    if (keep < N) {
+        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&sel), sizeof(SelectState), st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(select scratch)");
+        if ((rc = threshold_digits(args->scores_out, N, keep, sel, st))) {
+            cudaFreeAsync(sel, st);
+            return rc;
+        }
+    }
+    // Pass 2: threshold keep, recomputed importance, CORING, .tb sections.
+    FusedParams b = p;
+    b.S = 0;
+    b.g = nullptr;
+    b.first = 0;
+    b.use_fin = p.have_f;
+    b.fin = p.have_f ? args->fisher_out : nullptr;
+    b.fout = nullptr;
+    b.sout = args->scores_out;
+    if (sel) {
+        b.variant = kVarThreshold;
+        b.thr = &sel->threshold;
+        b.thr_pruned = &sel->pruned;
+    }
+    rc = launch_fused(b, m, st);
+    if (rc == TB_OK) rc = threshold_finish(N, keep, sel, threshold_out, ehap_pruned_out, st);
+    if (sel) cudaFreeAsync(sel, st);
+    if (rc == TB_OK && coring_pruned_out)
+        *coring_pruned_out = static_cast<uint64_t>(N / m) * static_cast<uint64_t>(m - args->nm_n);  // coring.hpp:192,222
+    return rc;
 }
 
 int tb_score_mask_pack_host(const tb_prune_args* a) {

@@ -121,6 +121,22 @@ int tb_malloc(void** ptr, size_t bytes) {
     return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaMalloc");
 }
 
+int tb_host_alloc(void** ptr, size_t bytes) {
+    if (!ptr) return fail(TB_ERR_ARG, "tb_host_alloc: null pointer");
+    *ptr = nullptr;
+    int rc = require_device(nullptr);
+    if (rc) return rc;
+    if (bytes == 0) return TB_OK;
+    cudaError_t e = cudaHostAlloc(ptr, bytes, cudaHostAllocPortable);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaHostAlloc");
+}
+
+int tb_host_free(void* ptr) {
+    if (!ptr) return TB_OK;
+    cudaError_t e = cudaFreeHost(ptr);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaFreeHost");
+}
+
 int tb_free(void* ptr) {
     if (!ptr) return TB_OK;
     cudaError_t e = cudaFree(ptr);

@@ -168,6 +168,16 @@ int threshold_launch(const float* scores, size_t N, size_t keep, uint8_t* mask_o
     return check_launch("threshold select");
 }
 
+int threshold_digits(const float* scores, size_t N, size_t keep, SelectState* st, cudaStream_t stream) {
+    init_state_kernel<<<1, 1024, 0, stream>>>(st, static_cast<unsigned long long>(N - keep));
+    const unsigned grid = grid_for(N);
+    for (int pass = 0; pass < 3; ++pass) {
+        radix_hist_kernel<<<grid, kThreads, 0, stream>>>(scores, N, st, pass);
+        radix_scan_kernel<<<1, 1024, 0, stream>>>(st, pass);
+    }
+    return check_launch("threshold digits");
+}
+
 int threshold_finish(size_t N, size_t keep, const SelectState* st, float* thr_out, uint64_t* pruned_out,
                      cudaStream_t stream) {
     float thr = 0.0f;

@@ -22,6 +22,10 @@ int threshold_args(size_t N, float sparsity, size_t* keep_out);
 // Enqueues the three digit passes and the mask pass on `stream`.
 int threshold_launch(const float* scores, size_t N, size_t keep, uint8_t* mask_out, SelectState* st,
                      cudaStream_t stream);
+// Enqueues only the three digit passes (keep < N): st->threshold holds the
+// threshold afterwards and st->pruned is zero, for a later pass that applies
+// the threshold itself and counts what it drops into st->pruned.
+int threshold_digits(const float* scores, size_t N, size_t keep, SelectState* st, cudaStream_t stream);
 // Reads threshold and pruned count back (synchronises `stream`).
 int threshold_finish(size_t N, size_t keep, const SelectState* st, float* thr_out, uint64_t* pruned_out,
                      cudaStream_t stream);

@@ -89,6 +89,8 @@ def lib() -> C.CDLL:
             "tb_set_device": ([i32], i32),
             "tb_malloc": ([C.POINTER(vp), sz], i32),
             "tb_free": ([vp], i32),
+            "tb_host_alloc": ([C.POINTER(vp), sz], i32),
+            "tb_host_free": ([vp], i32),
             "tb_memcpy_h2d": ([vp, vp, sz, vp], i32),
             "tb_memcpy_d2h": ([vp, vp, sz, vp], i32),
             "tb_memcpy_d2d": ([vp, vp, sz, vp], i32),
@@ -128,6 +130,8 @@ def lib() -> C.CDLL:
             "tb_obs_hessian_scaled": ([vp, i32, i32, f32, vp, vp], i32),
             "tb_obs_sparsegpt": ([vp, i32, i32, vp, f32, i32, i32, vp, vp, vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
+            "tb_prune_one_shot_nm": ([C.POINTER(PruneArgs), f32, C.POINTER(C.c_float), C.POINTER(C.c_uint64),
+                                      C.POINTER(C.c_uint64), vp], i32),
             "tb_score_mask_pack_peer": ([C.POINTER(PruneArgs), C.POINTER(vp), i32, vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),
             "tb_score_mask_pack_host_noalloc": ([C.POINTER(PruneArgs)], i32),
