@@ -111,7 +111,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--sweep-steps", type=int, default=2, help="timed steps per pattern of the 70B sweep")
     ap.add_argument("--split-steps", type=int, default=3, help="timed steps of each sample-split variant")
-    for k in ("e2e", "cpu", "obs", "block-obs", "ties", "layer", "sweep", "split", "digest", "verify"):
+    for k in ("e2e", "cpu", "obs", "block-obs", "ties", "layer", "sweep", "split", "digest", "verify", "tbprune"):
         ap.add_argument(f"--no-{k}", action="store_true")
     ap.add_argument("--obs-only", action="store_true", help="only the column-block exact OBS measurement")
     ap.add_argument("--block-obs-only", action="store_true", help="only the reference-semantics block OBS timing")
@@ -651,6 +651,10 @@ def run_ours(args):
     obs = None
     if not args.no_obs:
         obs = run_obs(torch, tb, ranks.dev, args.obs_steps, args.obs_shape, ranks.dist, bf16_peak)
+    tbp = None
+    if ranks.rank == 0 and ranks.world == 1 and not args.no_tbprune:
+        tbp = run_tb_prune_mode(torch, tb, ranks, args.steps, args.warmup)
+        torch.cuda.empty_cache()
     block_obs = None
     if ranks.rank == 0 and ranks.world == 1 and not args.no_block_obs:
         block_obs = run_block_obs(torch, tb, ranks, passes=args.block_obs_passes, cpu=not args.no_cpu)
@@ -671,7 +675,8 @@ def run_ours(args):
                                     "rule": "|s(N) - s(N+1)| <= 1e-6 max(|s(N)|, FLT_MIN) among a group's sorted "
                                             "scores; their masks are bit-exact too (the reference's selection and "
                                             "tie order are reproduced)"} if "groups" in res else None),
-                     "sample_split": split, "layer": layer, "sweep70b": sweep, "e2e": e2e, "obs": obs,
+                     "sample_split": split, "layer": layer, "sweep70b": sweep, "tb_prune_mode": tbp, "e2e": e2e,
+                     "obs": obs,
                      "block_obs": block_obs, "cpu_baseline": cpu})
         print(json.dumps(line), flush=True)
     ranks.close()
@@ -808,6 +813,84 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
             r["fused_pass_gbs_rank0"] = round(ex_bytes / (tot[0][3] / steps / 1e3) / 1e9, 1)
         out[variant] = r
     bufs.close()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# tb-prune mode: the CLI's own per-tensor sequence
+# ---------------------------------------------------------------------------
+def run_tb_prune_mode(torch, tb, ranks, steps, warmup):
+    """tb-prune's default per-tensor sequence (src/main.cpp:372-409: Fisher
+    from one gradient 0.01 w, EHAP one-shot global select at sparsity 0.5 and
+    apply, importance again, CORING top-N 2:4 with proportional
+    redistribution, mask regenerated) over one 7B-class decoder layer's seven
+    matrices, FP32 as the CLI widens them.  Fused: tb_prune_one_shot_nm, two
+    passes around three radix digit passes over the scores (16 + 12 + 12.25
+    B/param).  Staged: the same calls one by one through the stage entry
+    points, as the pruner objects issue them (about 83 B/param, with host
+    synchronisations for the select and the pruned counts)."""
+    import numpy as np
+    dev = ranks.dev
+    L = tb.lib()
+    sptr = torch.cuda.current_stream().cuda_stream
+    gen = torch.Generator(device=dev).manual_seed(31)
+    mats = []
+    for name, r, c in LAYER_7B:
+        n = r * c
+        w = torch.randn(n, device=dev, generator=gen).mul_(0.02)
+        g = w * 0.01
+        mats.append((n, w, g, torch.empty_like(w), torch.empty_like(w), torch.empty_like(w),
+                     torch.empty(n // 4, dtype=torch.uint8, device=dev), torch.empty(n, dtype=torch.uint8, device=dev)))
+    thr, ep, cp = C.c_float(), C.c_uint64(), C.c_uint64()
+
+    def fused():
+        for n, w, g, wo, F, sc, mk, _ in mats:
+            a = tb.prune_args(weights=w.data_ptr(), w_dtype=tb.F32, grads=g.data_ptr(), g_dtype=tb.F32, S=1, N=n,
+                              mode="obd", strategy="topn", redist="proportional", w_out=wo.data_ptr(),
+                              mask_out=mk.data_ptr(), fisher_out=F.data_ptr(), scores_out=sc.data_ptr())
+            tb.check(L.tb_prune_one_shot_nm(C.byref(a), 0.5, C.byref(thr), C.byref(ep), C.byref(cp), sptr))
+
+    def staged():
+        for n, w, g, wo, F, sc, mk, m1 in mats:
+            tb.check(L.tb_memcpy_d2d(wo.data_ptr(), w.data_ptr(), 4 * n, sptr))
+            tb.check(L.tb_fisher_ema_step(F.data_ptr(), g.data_ptr(), tb.F32, n, 0.01, 0.99, 1, sptr))
+            tb.check(L.tb_importance(wo.data_ptr(), tb.F32, F.data_ptr(), sc.data_ptr(), n, 0.01, 0, sptr))
+            tb.check(L.tb_threshold_select(sc.data_ptr(), n, 0.5, m1.data_ptr(), C.byref(thr), C.byref(ep), sptr))
+            tb.check(L.tb_ehap_apply_mask(wo.data_ptr(), m1.data_ptr(), n, C.byref(cp), sptr))
+            tb.check(L.tb_importance(wo.data_ptr(), tb.F32, F.data_ptr(), sc.data_ptr(), n, 0.01, 0, sptr))
+            tb.check(L.tb_nm_mask(sc.data_ptr(), mk.data_ptr(), n, 2, 4, 0, 3, 0, sptr))
+            tb.check(L.tb_apply_mask(wo.data_ptr(), mk.data_ptr(), n, 4, sptr))
+            tb.check(L.tb_redistribute(wo.data_ptr(), mk.data_ptr(), sc.data_ptr(), n, 4, 1, sptr))
+            tb.check(L.tb_nm_mask(sc.data_ptr(), mk.data_ptr(), n, 2, 4, 0, 3, 0, sptr))
+
+    out = {"workload": "tb-prune OneShot per-tensor sequence on one 7B-class decoder layer (7 FP32 matrices, "
+                       "218,103,808 params), Fisher from one gradient 0.01 w, sparsity 0.5, top-N 2:4, proportional",
+           "params_per_step": sum(x[0] for x in mats)}
+    outs = {}
+    for name, fn in (("fused", fused), ("staged", staged)):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        outs[name] = (ms, [(x[3].clone(), x[6].clone()) for x in mats])
+        out[name] = {"ms_per_step": round(ms, 3),
+                     "value": round(out["params_per_step"] / (ms / 1e3) / 1e9, 3), "unit": "Gparams/s"}
+    bpp = 16 + 12 + 12.25
+    hbm, _, kind = peaks()
+    ach = out["params_per_step"] * bpp / (outs["fused"][0] / 1e3) / 1e9
+    out["fused"]["roofline"] = {"bound": "hbm", "algorithmic_bytes_per_param": bpp, "achieved": round(ach, 1),
+                                "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4), "peak_kind": kind,
+                                "note": "the time includes the select's host read-back of the threshold and count"}
+    same = all(torch.equal(a[0].view(torch.int32), b[0].view(torch.int32)) and torch.equal(a[1], b[1])
+               for a, b in zip(outs["fused"][1], outs["staged"][1]))
+    out["fused_equals_staged_bitwise"] = bool(same)
+    out["speedup_fused_vs_staged"] = round(outs["staged"][0] / outs["fused"][0], 2)
     return out
 
 

@@ -70,3 +70,45 @@ def layer_loss(W0, W1, X):
     D = (np.asarray(W0, np.float64) - np.asarray(W1, np.float64)) @ X.T
     B = np.asarray(W0, np.float64) @ X.T
     return float((D ** 2).sum() / (B ** 2).sum())
+
+
+def sparsegpt_rows_torch(torch, W, U, n_keep=2, m=4, block=128):
+    """The same float64 sweep for a few rows with torch tensors (any device):
+    W [r, d] float64 rows of the layer, U [d, d] float64 upper Cholesky factor
+    of the damped H^-1.  Rows are independent given U, so checking a subset of
+    a large layer's rows needs only U.  Returns (pruned rows, mask bytes
+    [r, d/m], per-group saliency gap)."""
+    W = W.clone()
+    r, d = W.shape
+    dev = W.device
+    mask = torch.zeros(r, d // m, dtype=torch.uint8, device=dev)
+    gap = torch.zeros(r, d // m, dtype=torch.float64, device=dev)
+    bitw = 1 << torch.arange(m, device=dev)
+    prune_cnt = m - n_keep
+    for i1 in range(0, d, block):
+        i2 = min(i1 + block, d)
+        W1 = W[:, i1:i2].clone()
+        Q1 = torch.zeros_like(W1)
+        E1 = torch.zeros_like(W1)
+        U1 = U[i1:i2, i1:i2]
+        du = torch.diagonal(U1)
+        keep = None
+        for i in range(i2 - i1):
+            if i % m == 0:
+                sal = W1[:, i:i + m] ** 2 / du[i:i + m] ** 2
+                order = torch.argsort(sal, dim=1, stable=True)
+                keep = torch.ones(r, m, dtype=torch.bool, device=dev)
+                keep.scatter_(1, order[:, :prune_cnt], False)
+                g = (i1 + i) // m
+                mask[:, g] = (keep.long() * bitw).sum(1).to(torch.uint8)
+                s = torch.sort(sal, dim=1).values
+                gap[:, g] = (s[:, prune_cnt] - s[:, prune_cnt - 1]) / torch.clamp(s[:, prune_cnt], min=1e-300)
+            w = W1[:, i]
+            q = torch.where(keep[:, i % m], w, torch.zeros_like(w))
+            Q1[:, i] = q
+            err = (w - q) / U1[i, i]
+            W1[:, i:] -= torch.outer(err, U1[i, i:])
+            E1[:, i] = err
+        W[:, i1:i2] = Q1
+        W[:, i2:] -= E1 @ U[i1:i2, i2:]
+    return W, mask, gap

@@ -85,3 +85,60 @@ def test_sparsegpt_full_layer_is_reproducible(cuda, tblib):
         assert bool((pop == 2).all())
         digests.add(hashlib.sha256(W.cpu().numpy().tobytes() + mask.cpu().numpy().tobytes()).hexdigest())
     assert len(digests) == 1
+
+
+def test_sparsegpt_full_layer_against_float64(cuda, tblib):
+    """The benchmark layer itself (4096 x 14336 down_proj, 2048 tokens, 1 %
+    heavy columns x20: H is 7x rank-deficient before damping) against float64
+    on the device: H from the same BF16 activations, U = chol_upper((H +
+    lambda I)^-1) by float64 Cholesky, then the float64 sweep of 256 rows (two
+    128-row units at either end of W; rows are independent given U).  Same
+    bars as the small cases: U within 2e-4, >= 99.9 % of the rows' masks
+    equal with the first difference of a row a float64 near tie, and the
+    rows' reconstruction loss within 1 %."""
+    torch = cuda
+    r, d, n = 4096, 14336, 2048
+    g = torch.Generator(device="cuda").manual_seed(4)
+    X = torch.randn(n, d, device="cuda", generator=g)
+    hot = torch.randperm(d, device="cuda", generator=g)[: d // 100]
+    X[:, hot] *= 20
+    xt = X.t().contiguous().to(torch.bfloat16)
+    del X
+    W0 = (torch.randn(r, d, device="cuda", generator=g) * 0.02).to(torch.bfloat16).float()
+    H = torch.zeros(d, d, device="cuda")
+    tblib.check(tblib.lib().tb_obs_hessian(xt.data_ptr(), d, n, H.data_ptr(), None))
+    W = W0.clone()
+    mask = torch.empty(r * d // 4, dtype=torch.uint8, device="cuda")
+    ut = torch.empty(d, d, device="cuda")
+    tblib.check(tblib.lib().tb_obs_sparsegpt(W.data_ptr(), r, d, H.data_ptr(), 0.01, 2, 4, mask.data_ptr(),
+                                             ut.data_ptr(), None))
+    torch.cuda.synchronize()
+    del H
+    # float64 restatement on the device
+    x64 = xt.double()  # [d, n], the BF16 activations the kernels saw
+    H64 = (x64 @ x64.t()) / n
+    del x64
+    H64.diagonal().add_(0.01 * H64.diagonal().mean())
+    Hinv = torch.cholesky_inverse(torch.linalg.cholesky(H64))
+    del H64
+    U = torch.linalg.cholesky(Hinv).t().contiguous()
+    del Hinv
+    err = (ut.double() - U.t()).abs().max().item()
+    assert err <= 2e-4 * U.abs().max().item(), err
+    del ut
+    rows = torch.cat([torch.arange(0, 128), torch.arange(r - 128, r)]).cuda()
+    Wr, mr, gap = ref.sparsegpt_rows_torch(torch, W0[rows].double(), U, 2, 4, 128)
+    mg = mask.view(r, d // 4)[rows]
+    differ = mg != mr
+    assert differ.double().mean().item() <= 1e-3
+    bad = differ.any(1)
+    if bool(bad.any()):
+        first = torch.argmax(differ.int(), dim=1)
+        idx = torch.nonzero(bad).flatten()
+        assert bool((gap[idx, first[idx]] < 1e-2).all())
+    # reconstruction loss of those rows
+    xs = xt.double()  # [d, n]
+    B = W0[rows].double() @ xs
+    lg = (((W0[rows].double() - W[rows].double()) @ xs) ** 2).sum() / (B ** 2).sum()
+    lr = (((W0[rows].double() - Wr) @ xs) ** 2).sum() / (B ** 2).sum()
+    assert abs(lg.item() - lr.item()) <= 0.01 * lr.item(), (lg.item(), lr.item())

@@ -218,3 +218,18 @@ def test_port_vs_reference_block_obs(port, ref, N, block, K, S, use_fisher, sp):
     a = port.block_obs(w, g, hist, block=block, sparsity=sp, use_fisher=use_fisher, hist_size=max(K, 1))
     b = ref.block_obs(w, g, hist, block=block, sparsity=sp, use_fisher=use_fisher, hist_size=max(K, 1))
     assert a[0] == b[0] == 0 and a[2] == b[2] and same(a[1], b[1])
+
+
+def test_sparsegpt_torch_rows_equal_the_numpy_restatement():
+    """The float64 sweep written with torch (used on the device for the full
+    4096 x 14336 layer) equals the numpy restatement on a small layer."""
+    import torch
+    import sparsegpt_ref as sref
+    X = inputs.activations(192, 256, 5)
+    W = inputs.normal(48 * 256, 0.02, 6).reshape(48, 256)
+    Wn, mn, U, gn = sref.sparsegpt(W, X, 0.01, 2, 4, 128)
+    Wt, mt, gt = sref.sparsegpt_rows_torch(torch, torch.from_numpy(W.astype(np.float64)),
+                                           torch.from_numpy(U), 2, 4, 128)
+    assert np.array_equal(mt.numpy(), mn)
+    np.testing.assert_allclose(Wt.numpy(), Wn, rtol=0, atol=1e-12)
+    np.testing.assert_allclose(gt.numpy(), gn, rtol=1e-9, atol=1e-12)
