@@ -694,7 +694,11 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
             from the summed Fisher (stateful entry, no samples);
       peer: a one-element all-reduce as a stream-ordered barrier, then
             tb_score_mask_pack_peer, which reads the ranks' partials of its
-            range from peer memory over NVLink inside the pass.
+            range from peer memory over NVLink inside the pass;
+      push: tb_fisher_partial_scatter computes the partial through the
+            bulk-copy ring and stores each owner's range into the owner's
+            memory (NVLink writes), then the barrier, then
+            tb_score_mask_pack_peer over the P local slots.
     Each variant is timed over whole 7B passes; its masks are compared with the
     exact (serial-recurrence) pass on this rank's ranges."""
     import tbdist as td
@@ -719,7 +723,8 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
                                                      mask=Me.data_ptr()), sptr))
                 exact[id(T)] = Me
     F = torch.empty(nmax, dtype=torch.float32, device=dev)
-    bufs = td.PeerBuffers(dist, 4 * nmax, 2)
+    W = ranks.world
+    bufs = td.PeerBuffers(dist, 4 * max(nmax, W * td.push_slot(nmax, m, W)), 2)
     flag = torch.zeros(1, dtype=torch.float32, device=dev)
     ties = torch.zeros(1, dtype=torch.int64, device=dev)
     counter = [0]
@@ -756,9 +761,36 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
             tb.check(L.tb_score_mask_pack_peer(C.byref(fused_args(T, e0, e1, count)),
                                                C.cast(parts, C.POINTER(C.c_void_p)), ranks.world, sptr))
 
+    # push variant: per distinct tensor, the owners' ranges and, per exchange
+    # buffer, where this rank's partial of each range goes / where its slots are
+    scatter = {}
+    for ts in sets:
+        for T in ts:
+            slot = td.push_slot(T.n, m, W)
+            ranges = [td.group_shard(T.n, m, W, r) for r in range(W)]
+            starts = (C.c_uint64 * (W + 1))(*([a for a, _ in ranges] + [T.n]))
+            dests = [(C.c_void_p * W)(*[bufs.ptrs[k][r] + 4 * ranks.rank * slot for r in range(W)]) for k in (0, 1)]
+            parts = [(C.c_void_p * W)(*[bufs.local[k] + 4 * q * slot for q in range(W)]) for k in (0, 1)]
+            scatter[id(T)] = (starts, dests, parts)
+
+    def tensor_push(T, ev, count):
+        e0, e1 = rng[id(T)]
+        k = counter[0] & 1
+        counter[0] += 1
+        starts, dests, parts = scatter[id(T)]
+        tb.check(L.tb_fisher_partial_scatter(T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n, T.n,
+                                             c.ctypes.data, W, starts, C.cast(dests[k], C.POINTER(C.c_void_p)),
+                                             sptr))
+        ev and ev[1].record()
+        dist.all_reduce(flag)
+        ev and ev[2].record()
+        if e1 > e0:
+            tb.check(L.tb_score_mask_pack_peer(C.byref(fused_args(T, e0, e1, count)),
+                                               C.cast(parts[k], C.POINTER(C.c_void_p)), W, sptr))
+
     out = {"workload": "the headline 7B pass with each tensor's 64 samples split evenly over the ranks",
            "samples_per_rank": s1 - s0}
-    for variant, fn in (("nccl", tensor_nccl), ("peer", tensor_peer)):
+    for variant, fn in (("nccl", tensor_nccl), ("peer", tensor_peer), ("push", tensor_push)):
         def one_pass(evs=None, count=False):
             for i, T in enumerate(items):
                 ev = evs[i] if evs else None
@@ -805,12 +837,19 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
             r["exchange"] = "NCCL all-reduce (sum, FP32) of each tensor's N-float partial Fisher"
             r["all_reduce_bytes_per_step"] = ex_bytes
             r["all_reduce_algbw_gbs_rank0"] = round(ex_bytes / (tot[0][2] / steps / 1e3) / 1e9, 1)
-        else:
+        elif variant == "peer":
             r["exchange"] = ("one-element NCCL all-reduce per tensor as a stream-ordered barrier; the pass reads the "
                              "other ranks' partials of its range from peer memory (reduce-scatter fused into "
                              "score/mask/pack)")
             r["nvlink_read_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
             r["fused_pass_gbs_rank0"] = round(ex_bytes / (tot[0][3] / steps / 1e3) / 1e9, 1)
+        else:
+            r["exchange"] = ("the partial-Fisher kernel (bulk-copy ring over the rank's samples) stores each owner's "
+                             "range into that owner's memory (NVLink writes inside the pass); a one-element NCCL "
+                             "all-reduce per tensor orders it; the pass sums the P slots of its range locally")
+            r["nvlink_write_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
+            part_bytes = sum(T.n for T in items) * 2 * (s1 - s0) + ex_bytes
+            r["partial_kernel_gbs_rank0"] = round(part_bytes / (tot[0][1] / steps / 1e3) / 1e9, 1)
         out[variant] = r
     bufs.close()
     return out

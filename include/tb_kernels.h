@@ -283,6 +283,13 @@ typedef struct tb_prune_args {
 } tb_prune_args;
 
 int tb_score_mask_pack(const tb_prune_args* args, void* stream);
+/* Synchronises the stream and returns TB_ERR_TIMEOUT if, since the previous
+ * call on this device, a bounded wait inside a fused pass expired (its
+ * outputs are then incomplete); TB_OK otherwise.  Passes with 16-bit
+ * gradients stream the gradient rows through shared memory with bulk copies
+ * (set TB_FUSED_RING=0 in the environment to use the register-staged kernel
+ * for every pass); their waits are bounded at 2 s. */
+int tb_score_mask_pack_status(void* stream);
 
 /* tb-prune's per-tensor sequence (src/main.cpp:372-409) in three device
  * passes: EHAPPruner::accumulate_fisher x S + compute_importance
@@ -304,6 +311,25 @@ int tb_score_mask_pack(const tb_prune_args* args, void* stream);
  * N:M check, as the reference's EHAP stage fails first. */
 int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* threshold_out,
                          uint64_t* ehap_pruned_out, uint64_t* coring_pruned_out, void* stream);
+
+/* Sample split, producer side: this rank's partial Fisher
+ *   F_part[i] = sum over its S samples of weights[s] * g_s[i]^2
+ * (from +0, samples in order: the arithmetic of tb_fisher_weighted_sum, bit
+ * for bit) for all N elements, each element stored to the rank that owns it:
+ * ranks r = 0..n_ranks-1 own [starts[r], starts[r+1]) (host array of
+ * n_ranks + 1 offsets from 0 to N, inner ones multiples of 8) and element
+ * starts[r] lands at dest[r][0] (host array of device pointers: a peer's
+ * buffer mapped with tb_ipc_open, or this device's own).  The stores to other
+ * GPUs travel over NVLink inside the pass, so the exchange of an all-reduce
+ * becomes writes of (P-1)/P of the partial, and each owner then reads the P
+ * partials of its range from its own memory (tb_score_mask_pack_peer with
+ * local pointers).  No counterpart in the reference (one process, no
+ * collectives; docs/CLOUD.md:155-169).  S <= 128 per call (TB_ERR_CAPACITY);
+ * 16-bit gradients with 16-byte aligned rows stream through shared memory by
+ * bulk copies (bounded waits, see tb_score_mask_pack_status). */
+int tb_fisher_partial_scatter(const void* gradients, int g_dtype, size_t S, size_t g_stride, size_t N,
+                              const float* weights, int n_ranks, const uint64_t* starts, float* const* dest,
+                              void* stream);
 
 /* Sample-split pass: the reduction of the ranks' partial Fisher sums fused
  * into the score -> mask -> pack pass (a reduce-scatter over peer memory).

@@ -13,10 +13,13 @@ docs prune shards in separate processes, docs/CLOUD.md:155-170):
   F_S = beta F_{S-1} + alpha (1-beta) g^2 (ehap.hpp:190-197) is regrouped as
   F = sum_t c_t g_t^2; each rank sums its own samples (tb_fisher_weighted_sum),
   one NCCL all-reduce adds the partials over NVLink, and every rank then scores,
-  masks and packs its group range from the summed Fisher.  The peer variant
-  replaces the all-reduce by reads of the other ranks' partials inside the
-  pass itself (a reduce-scatter fused into score/mask/pack, half the NVLink
-  bytes of an all-reduce and no separate reduction kernel).  F matches the
+  masks and packs its group range from the summed Fisher.  The peer variants
+  replace the all-reduce by a reduce-scatter over peer memory, half the NVLink
+  bytes of an all-reduce and no reduction kernel: `prune_sample_split_peer`
+  reads the other ranks' partials of its range inside the pass;
+  `prune_sample_split_push` (the fast one) has each rank's partial kernel
+  store every owner's range straight into that owner's memory, so the pass
+  reads all partials locally.  F matches the
   serial recurrence to FP32 rounding (the association differs), so masks can
   differ only in near-tie groups, which the pass counts.
 
@@ -281,6 +284,54 @@ def prune_sample_split_peer(dist, torch, bufs: PeerBuffers, k: int, w_dev, w_dty
     e0, e1 = group_shard(N, m, world, rank)
     if e1 > e0:
         parts = (C.c_void_p * world)(*[bufs.ptrs[k][r] + 4 * e0 for r in range(world)])
+        wsz = w_dev.element_size()
+        a = tb.prune_args(weights=w_dev.data_ptr() + e0 * wsz, w_dtype=w_dtype, grads=None, g_dtype=g_dtype, S=0,
+                          N=e1 - e0, fisher_steps_in=S_total, alpha=alpha, beta=beta, n=n, m=m,
+                          w_out=out_w.data_ptr() + 4 * e0, mask_out=out_mask.data_ptr() + e0 // m,
+                          fisher_out=(fisher_out.data_ptr() + 4 * e0) if fisher_out is not None else None,
+                          near_ties=near_ties.data_ptr() if near_ties is not None else None, **cfg)
+        _check(L.tb_score_mask_pack_peer(C.byref(a), C.cast(parts, C.POINTER(C.c_void_p)), world, stream))
+    return {"e0": e0, "e1": e1}
+
+
+def push_slot(N: int, m: int, world: int) -> int:
+    """Floats per writer slot in an owner's exchange buffer: the largest group
+    range rounded up to 16 elements (every slot stays 64-byte aligned)."""
+    longest = max(e1 - e0 for e0, e1 in (group_shard(N, m, world, r) for r in range(world)))
+    return (longest + 15) // 16 * 16
+
+
+def prune_sample_split_push(dist, torch, bufs: PeerBuffers, k: int, w_dev, w_dtype: int, g_local_dev, g_dtype: int,
+                            S_total: int, s0: int, out_w, out_mask, *, n=2, m=4, alpha=0.01, beta=0.99,
+                            flag=None, fisher_out=None, near_ties=None, **cfg) -> dict:
+    """Sample-split pass of one tensor with the exchange done as writes: this
+    rank's partial Fisher over its samples is computed once for all N
+    elements and each owner's range is stored straight into that owner's
+    exchange buffer k, in this rank's slot (tb_fisher_partial_scatter; remote
+    stores over NVLink); after a one-element all-reduce (stream-ordered
+    barrier) every rank sums the P slots of its own range from local memory
+    inside the fused pass (tb_score_mask_pack_peer).  Buffers alternate per
+    tensor as in prune_sample_split_peer; each holds P slots of push_slot()
+    floats."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    N = w_dev.numel()
+    S_local = g_local_dev.shape[0] if g_local_dev is not None else 0
+    stream = torch.cuda.current_stream().cuda_stream
+    L = tb.lib()
+    slot = push_slot(N, m, world)
+    ranges = [group_shard(N, m, world, r) for r in range(world)]
+    starts = (C.c_uint64 * (world + 1))(*([e0 for e0, _ in ranges] + [N]))
+    dest = (C.c_void_p * world)(*[bufs.ptrs[k][r] + 4 * rank * slot for r in range(world)])
+    c = ema_weights(S_total, alpha, beta)[s0:s0 + S_local].copy()
+    _check(L.tb_fisher_partial_scatter(g_local_dev.data_ptr() if S_local else None, g_dtype, S_local, N, N,
+                                       c.ctypes.data if S_local else None, world, starts,
+                                       C.cast(dest, C.POINTER(C.c_void_p)), stream))
+    if flag is None:
+        flag = torch.zeros(1, dtype=torch.float32, device=w_dev.device)
+    dist.all_reduce(flag)
+    e0, e1 = ranges[rank]
+    if e1 > e0:
+        parts = (C.c_void_p * world)(*[bufs.local[k] + 4 * q * slot for q in range(world)])
         wsz = w_dev.element_size()
         a = tb.prune_args(weights=w_dev.data_ptr() + e0 * wsz, w_dtype=w_dtype, grads=None, g_dtype=g_dtype, S=0,
                           N=e1 - e0, fisher_steps_in=S_total, alpha=alpha, beta=beta, n=n, m=m,

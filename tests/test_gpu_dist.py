@@ -79,6 +79,20 @@ def _worker(rank, world, port_no, tmpdir):
     np.save(os.path.join(tmpdir, f"pp_m{rank}.npy"), pm[e0 // 4:e1 // 4].cpu().numpy())
     np.save(os.path.join(tmpdir, f"pp_F{rank}.npy"), pF[e0:e1].cpu().numpy())
     bufs.close()
+    # and with the exchange as NVLink writes from the partial kernel (push)
+    bufs = td.PeerBuffers(dist, 4 * world * td.push_slot(N, 4, world), 2)
+    qw = torch.zeros(N, dtype=torch.float32, device="cuda")
+    qm = torch.zeros(N // 4, dtype=torch.uint8, device="cuda")
+    qF = torch.zeros(N, dtype=torch.float32, device="cuda")
+    for k in (0, 1, 0):
+        td.prune_sample_split_push(dist, torch, bufs, k, wd, tb.BF16, gd, tb.BF16, S, s0, qw, qm,
+                                   strategy="optimal", redist="proportional", mode="obd", fisher_out=qF)
+    tb.check(tb.lib().tb_score_mask_pack_status(None))
+    torch.cuda.synchronize()
+    np.save(os.path.join(tmpdir, f"pu_w{rank}.npy"), qw[e0:e1].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"pu_m{rank}.npy"), qm[e0 // 4:e1 // 4].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"pu_F{rank}.npy"), qF[e0:e1].cpu().numpy())
+    bufs.close()
     dist.barrier(device_ids=[rank])
     dist.destroy_process_group()
 
@@ -125,6 +139,10 @@ def test_two_rank_group_shard_and_sample_split(cuda, tblib, port, tmp_path):
     wpp = np.concatenate([np.load(tmp_path / f"pp_w{r}.npy") for r in range(world)])
     samep = np.repeat(mp_ == mo, 4)
     assert np.array_equal(wpp[samep], wo[samep])
+    # push variant: the same partials (same arithmetic), so the same bits as the peer-read variant
+    for key, ref_ in (("F", Fp), ("m", mp_), ("w", wpp)):
+        got = np.concatenate([np.load(tmp_path / f"pu_{key}{r}.npy") for r in range(world)])
+        assert got.tobytes() == ref_.tobytes(), f"push variant {key} differs from the peer-read variant"
 
 
 def _obs_worker(rank, world, port_no, tmpdir):

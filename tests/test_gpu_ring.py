@@ -1,0 +1,142 @@
+"""GPU: the fused pass with 16-bit gradients, which streams each 4096-element
+slab's gradient rows through a ring of shared-memory stages (bulk copies),
+against the oracle bit for bit - whole slabs plus a ragged tail handled by the
+register-staged kernels, every N:M pattern, both 16-bit gradient types, a
+prior Fisher state, optional outputs and the near-tie counter - and against
+the register-staged kernel alone (TB_FUSED_RING=0, in a fresh process)."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import inputs
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def case(N, S, seed, gdt):
+    w = inputs.normal(N, 0.02, seed)
+    g32 = inputs.normal((S, N), 1e-3, seed + 1)
+    if gdt == "bf16":
+        bits = inputs.to_bf16_bits(g32)
+        return w, bits.view(np.int16), inputs.bf16_bits_to_f32(bits), 2
+    h = g32.astype(np.float16)
+    from oracle import Oracle
+    return w, h.view(np.int16), Oracle("port").decode_half(h.view(np.uint16), False).reshape(S, N), 1
+
+
+def run(torch, tb, w, gbits, gcode, n, m, strategy, *, fin=None, steps_in=0, outs=True):
+    N = w.size
+    S = gbits.shape[0]
+    wd = torch.from_numpy(w).cuda()
+    gd = torch.from_numpy(np.ascontiguousarray(gbits)).cuda()
+    wo = torch.full((N,), float("nan"), device="cuda")
+    mk = torch.full((N // m,), 0x5A, dtype=torch.uint8, device="cuda")
+    F = torch.full((N,), float("nan"), device="cuda")
+    s = torch.full((N,), float("nan"), device="cuda")
+    ties = torch.zeros(1, dtype=torch.int64, device="cuda")
+    fd = torch.from_numpy(fin).cuda() if fin is not None else None
+    a = tb.prune_args(weights=wd.data_ptr(), w_dtype=tb.F32, grads=gd.data_ptr(), g_dtype=gcode, S=S, N=N,
+                      fisher_in=fd.data_ptr() if fd is not None else None, fisher_steps_in=steps_in, n=n, m=m,
+                      strategy=strategy, mode="obd", redist="proportional", w_out=wo.data_ptr(),
+                      mask_out=mk.data_ptr(), fisher_out=F.data_ptr() if outs else None,
+                      scores_out=s.data_ptr() if outs else None, near_ties=ties.data_ptr())
+    tb.check(tb.score_mask_pack(a, None))
+    tb.check(tb.lib().tb_score_mask_pack_status(None))
+    return wo.cpu().numpy(), mk.cpu().numpy(), F.cpu().numpy(), s.cpu().numpy(), int(ties.item())
+
+
+@pytest.mark.parametrize("gdt", ["bf16", "f16"])
+@pytest.mark.parametrize("n,m,strategy", [(2, 4, "optimal"), (2, 4, "topn"), (1, 4, "iterative"),
+                                          (2, 8, "iterative"), (4, 8, "topn"), (1, 2, "optimal")])
+def test_ring_matches_oracle(cuda, tblib, port, gdt, n, m, strategy):
+    N = 5 * 4096 + 96  # five slabs through the ring, a tail through the other kernels
+    w, gbits, g32, gcode = case(N, 19, 80 + m, gdt)
+    wo, mk, F, s, ties = run(cuda, tblib, w, gbits, gcode, n, m, strategy)
+    rc, wp, mp, Fp, sp, _, _ = port.pipeline(w, g32, n=n, m=m, strategy=strategy, redist="proportional")
+    assert rc == 0
+    assert wo.tobytes() == wp.tobytes() and mk.tobytes() == mp.tobytes()
+    assert F.tobytes() == Fp.tobytes() and s.tobytes() == sp.tobytes()
+    assert ties == port.near_ties(sp, n, m)
+
+
+def test_ring_continues_a_prior_fisher_state(cuda, tblib, port):
+    N, S = 8 * 4096, 6
+    w, gbits, g32, gcode = case(N, S, 91, "bf16")
+    rc, F0 = port.fisher(inputs.normal((3, N), 1e-3, 92))
+    wo, mk, F, s, _ = run(cuda, tblib, w, gbits, gcode, 2, 4, "optimal", fin=F0, steps_in=3)
+    # the oracle continues the recurrence from F0 with the same samples
+    Fr = F0.copy()
+    beta, contrib = np.float32(0.99), np.float32(np.float32(0.01) * (np.float32(1) - np.float32(0.99)))
+    for k in range(S):
+        Fr = (beta * Fr + (contrib * g32[k]) * g32[k]).astype(np.float32)
+    assert F.tobytes() == Fr.tobytes()
+
+
+def test_ring_without_optional_outputs_and_many_slabs(cuda, tblib, port):
+    # more slabs than resident CTAs, so each CTA's producer runs several slabs ahead
+    N, S = 700 * 4096, 3
+    w, gbits, g32, gcode = case(N, S, 93, "bf16")
+    wo, mk, _, _, _ = run(cuda, tblib, w, gbits, gcode, 2, 4, "optimal", outs=False)
+    rc, wp, mp, *_ = port.pipeline(w, g32, strategy="optimal", redist="proportional")
+    assert wo.tobytes() == wp.tobytes() and mk.tobytes() == mp.tobytes()
+
+
+def test_ring_equals_register_staged_kernel(cuda, tblib, tmp_path):
+    N, S = 40 * 4096 + 32, 33
+    w, gbits, _, gcode = case(N, S, 95, "bf16")
+    np.save(tmp_path / "w.npy", w)
+    np.save(tmp_path / "g.npy", gbits)
+    code = (
+        "import sys, numpy as np, torch\n"
+        f"sys.path[:0] = [{os.path.join(os.path.dirname(HERE), 'tensorbit-core_b200')!r}, {HERE!r}]\n"
+        "import tbabi as tb, test_gpu_ring as t\n"
+        f"w = np.load({str(tmp_path / 'w.npy')!r}); g = np.load({str(tmp_path / 'g.npy')!r})\n"
+        "wo, mk, F, s, ties = t.run(torch, tb, w, g, 2, 2, 4, 'iterative')\n"
+        f"np.save({str(tmp_path / 'out.npy')!r}, np.concatenate([wo.view(np.uint8), mk, F.view(np.uint8), "
+        "s.view(np.uint8)]))\n"
+    )
+    env = dict(os.environ, TB_FUSED_RING="0")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    ref = np.load(tmp_path / "out.npy")
+    wo, mk, F, s, _ = run(cuda, tblib, w, gbits, gcode, 2, 4, "iterative")
+    got = np.concatenate([wo.view(np.uint8), mk, F.view(np.uint8), s.view(np.uint8)])
+    assert got.tobytes() == ref.tobytes()
+
+
+@pytest.mark.parametrize("gdt", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("P", [1, 2, 3, 8])
+def test_partial_scatter_equals_weighted_sum(cuda, tblib, gdt, P):
+    """tb_fisher_partial_scatter with P owners emulated by buffers on this one
+    device: every owner's slot holds exactly tb_fisher_weighted_sum's values
+    for its range (whole slabs through the ring, the tail and FP32 gradients
+    through the scalar kernel)."""
+    import ctypes as C
+    import tbdist as td
+    torch = cuda
+    N, S = 9 * 4096 + 48, 17
+    if gdt == "f32":
+        gd = torch.from_numpy(inputs.normal((S, N), 1e-3, 97)).cuda()
+        code = tblib.F32
+    else:
+        _, gbits, _, code = case(N, S, 97, gdt)
+        gd = torch.from_numpy(np.ascontiguousarray(gbits)).cuda()
+    c = td.ema_weights(S, 0.01, 0.99)
+    ref = torch.empty(N, device="cuda")
+    tblib.check(tblib.lib().tb_fisher_weighted_sum(ref.data_ptr(), gd.data_ptr(), code, S, N, N, c.ctypes.data, 0,
+                                                   None))
+    ranges = [td.group_shard(N, 4, P, r) for r in range(P)]
+    slot = td.push_slot(N, 4, P)
+    owners = [torch.full((slot,), float("nan"), device="cuda") for _ in range(P)]
+    starts = (C.c_uint64 * (P + 1))(*([a for a, _ in ranges] + [N]))
+    dest = (C.c_void_p * P)(*[o.data_ptr() for o in owners])
+    tblib.check(tblib.lib().tb_fisher_partial_scatter(gd.data_ptr(), code, S, N, N, c.ctypes.data, P, starts,
+                                                      C.cast(dest, C.POINTER(C.c_void_p)), None))
+    tblib.check(tblib.lib().tb_score_mask_pack_status(None))
+    for (e0, e1), o in zip(ranges, owners):
+        assert torch.equal(o[:e1 - e0].view(torch.int32), ref[e0:e1].view(torch.int32))
