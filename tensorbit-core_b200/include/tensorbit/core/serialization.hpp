@@ -112,40 +112,44 @@ public:
         file_.open(std::string(path), std::ios::binary);
         if (!file_.is_open()) return unexpected(TBError::kFileOpen);
         TBHeader hdr{};
-        file_.read(reinterpret_cast<char*>(&hdr), sizeof(hdr));
-        if (!file_.good() || file_.gcount() != static_cast<std::streamsize>(sizeof(hdr)))
-            return unexpected(TBError::kTruncated);
+        if (auto r = read_section(0, sizeof(hdr), &hdr, TBError::kTruncated); !r) return unexpected(r.error());
         if (hdr.magic != kTBMagic) return unexpected(TBError::kBadMagic);
         if (hdr.version != kTBVersion) return unexpected(TBError::kVersionMismatch);
         header_ = hdr;
         return hdr;
     }
 
+    /// The weight section (num_weights values at weights_offset).
     template <FloatingPoint F>
     auto read_weights(std::span<F> out) -> Result<void, TBError> {
         if (!file_.is_open()) return unexpected(TBError::kFileOpen);
         if (out.size() < header_.num_weights) return unexpected(TBError::kTruncated);
-        file_.seekg(static_cast<std::streamoff>(header_.weights_offset));
-        if (!file_.good()) return unexpected(TBError::kSeekFailed);
-        file_.read(reinterpret_cast<char*>(out.data()), static_cast<std::streamsize>(header_.num_weights * sizeof(F)));
-        if (!file_.good()) return unexpected(TBError::kFileRead);
-        return {};
+        return read_section(header_.weights_offset, header_.num_weights * sizeof(F), out.data(), TBError::kFileRead);
     }
 
+    /// The mask section (num_mask_bytes at masks_offset).
     auto read_masks(std::span<uint8_t> out) -> Result<void, TBError> {
         if (!file_.is_open()) return unexpected(TBError::kFileOpen);
         if (out.size() < header_.num_mask_bytes) return unexpected(TBError::kTruncated);
-        file_.seekg(static_cast<std::streamoff>(header_.masks_offset));
-        if (!file_.good()) return unexpected(TBError::kSeekFailed);
-        file_.read(reinterpret_cast<char*>(out.data()), static_cast<std::streamsize>(header_.num_mask_bytes));
-        if (!file_.good()) return unexpected(TBError::kFileRead);
-        return {};
+        return read_section(header_.masks_offset, header_.num_mask_bytes, out.data(), TBError::kFileRead);
     }
 
     void close() { file_.close(); }
     [[nodiscard]] const TBHeader& header() const noexcept { return header_; }
 
 private:
+    /// `bytes` from file offset `offset` into dst.  The codes are the
+    /// reader's interface: a seek that fails is kSeekFailed, a read that fails
+    /// or comes up short is `on_short` (kTruncated for the header, kFileRead
+    /// for a section).
+    auto read_section(std::uint64_t offset, std::size_t bytes, void* dst, TBError on_short) -> Result<void, TBError> {
+        file_.seekg(static_cast<std::streamoff>(offset));
+        if (!file_.good()) return unexpected(TBError::kSeekFailed);
+        file_.read(static_cast<char*>(dst), static_cast<std::streamsize>(bytes));
+        if (!file_.good() || file_.gcount() != static_cast<std::streamsize>(bytes)) return unexpected(on_short);
+        return {};
+    }
+
     std::ifstream file_;
     TBHeader header_{};
 };

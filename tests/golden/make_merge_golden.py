@@ -1,6 +1,6 @@
 """Regenerates tests/golden/merge.json from the REFERENCE's own merge script.
 
-    python tests/golden/make_merge_golden.py
+    python tests/golden/make_merge_golden.py [REFERENCE_ROOT]   (or TB_REFERENCE_DIR=...)
 
 Builds the shard directories of tests/inputs.merge_tree() in a fresh temporary
 tree for each run of tests/inputs.MERGE_RUNS, runs the reference's
@@ -22,7 +22,10 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 import inputs  # noqa: E402
 
-SCRIPT = "/root/reference/scripts/merge_tbm.py"
+# The reference checkout: TB_REFERENCE_DIR, else the first argument, else the
+# default mount point of this build's container.
+REF_ROOT = os.environ.get("TB_REFERENCE_DIR") or (sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+SCRIPT = os.path.join(REF_ROOT, "scripts", "merge_tbm.py")
 
 
 def output_arg(args):
