@@ -695,10 +695,9 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
       peer: a one-element all-reduce as a stream-ordered barrier, then
             tb_score_mask_pack_peer, which reads the ranks' partials of its
             range from peer memory over NVLink inside the pass;
-      push: tb_fisher_partial_scatter computes the partial through the
-            bulk-copy ring and stores each owner's range into the owner's
-            memory (NVLink writes), then the barrier, then
-            tb_score_mask_pack_peer over the P local slots.
+      push: tb_fisher_partial_scatter computes the partial and stores each
+            owner's range into the owner's memory (NVLink writes), then the
+            barrier, then tb_score_mask_pack_peer over the P local slots.
     Each variant is timed over whole 7B passes; its masks are compared with the
     exact (serial-recurrence) pass on this rank's ranges."""
     import tbdist as td
@@ -844,7 +843,7 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
             r["nvlink_read_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
             r["fused_pass_gbs_rank0"] = round(ex_bytes / (tot[0][3] / steps / 1e3) / 1e9, 1)
         else:
-            r["exchange"] = ("the partial-Fisher kernel (bulk-copy ring over the rank's samples) stores each owner's "
+            r["exchange"] = ("the partial-Fisher kernel (over the rank's samples) stores each owner's "
                              "range into that owner's memory (NVLink writes inside the pass); a one-element NCCL "
                              "all-reduce per tensor orders it; the pass sums the P slots of its range locally")
             r["nvlink_write_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world

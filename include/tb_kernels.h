@@ -283,13 +283,6 @@ typedef struct tb_prune_args {
 } tb_prune_args;
 
 int tb_score_mask_pack(const tb_prune_args* args, void* stream);
-/* Synchronises the stream and returns TB_ERR_TIMEOUT if, since the previous
- * call on this device, a bounded wait inside a fused pass expired (its
- * outputs are then incomplete); TB_OK otherwise.  Passes with 16-bit
- * gradients stream the gradient rows through shared memory with bulk copies
- * (set TB_FUSED_RING=0 in the environment to use the register-staged kernel
- * for every pass); their waits are bounded at 2 s. */
-int tb_score_mask_pack_status(void* stream);
 
 /* tb-prune's per-tensor sequence (src/main.cpp:372-409) in three device
  * passes: EHAPPruner::accumulate_fisher x S + compute_importance
@@ -324,9 +317,7 @@ int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* thres
  * becomes writes of (P-1)/P of the partial, and each owner then reads the P
  * partials of its range from its own memory (tb_score_mask_pack_peer with
  * local pointers).  No counterpart in the reference (one process, no
- * collectives; docs/CLOUD.md:155-169).  S <= 128 per call (TB_ERR_CAPACITY);
- * 16-bit gradients with 16-byte aligned rows stream through shared memory by
- * bulk copies (bounded waits, see tb_score_mask_pack_status). */
+ * collectives; docs/CLOUD.md:155-169).  S <= 128 per call (TB_ERR_CAPACITY). */
 int tb_fisher_partial_scatter(const void* gradients, int g_dtype, size_t S, size_t g_stride, size_t N,
                               const float* weights, int n_ranks, const uint64_t* starts, float* const* dest,
                               void* stream);

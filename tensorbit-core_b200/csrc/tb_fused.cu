@@ -15,7 +15,6 @@
 // HBM-bound (about 2S+6 bytes per parameter against ~3 FP ops per
 // parameter-sample).
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -106,22 +105,6 @@ template <> struct Vec16<TB_F16> {
         }
     }
 };
-
-// 8 elements of a 16-bit type from one 16-byte word, as Vec16 decodes them.
-template <int DT>
-__device__ __forceinline__ void decode8(const uint4 b, float (&x)[8]) {
-    const uint32_t u[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        if (DT == TB_BF16) {
-            x[2 * j + 0] = __uint_as_float(u[j] << 16);
-            x[2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
-        } else {
-            x[2 * j + 0] = f16ref_to_f32(u[j] & 0xFFFFu);
-            x[2 * j + 1] = f16ref_to_f32(u[j] >> 16);
-        }
-    }
-}
 
 template <int DT>
 __device__ __forceinline__ void load16(const void* base, size_t e0, float (&x)[kEpt]) {
@@ -297,227 +280,6 @@ __global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParam
     if (VAR == kVarThreshold) warp_add_count(p.thr_pruned, zeroed);
 }
 
-// ---- bulk-copy ring: gradient rows staged through shared memory ------------
-// The register-staged kernel above keeps U samples of loads in flight per
-// thread, so its memory parallelism is bounded by registers and occupancy;
-// with few samples per element (32 for the 70B sweep) the selection phase,
-// during which a thread has no load in flight, leaves HBM idle.  Here one
-// producer thread per CTA streams the gradient rows of each 4096-element slab
-// into a ring of shared-memory stages with cp.async.bulk (8 KB per row and
-// stage, completion on an mbarrier), so the copies of the next slab are in
-// flight while the consumers select and store the current one.  Consumers
-// (8 warps) read their elements from the stage, release it through an
-// "empty" mbarrier and keep the Fisher recurrence in registers.  Every wait is
-// bounded (2 s); on expiry the CTA records an error, stops issuing copies,
-// waits (bounded) for the copies it issued and leaves.
-constexpr int kRingConsumers = 256;           // 8 warps x 32 lanes x 16 elements
-constexpr int kSlab = kRingConsumers * kEpt;  // 4096 elements per slab
-constexpr int kRingMaxStages = 16;
-constexpr uint64_t kRingWaitNs = 2000000000ull;
-
-__device__ int g_ring_error;  // 1 = a ring wait expired (read and cleared by tb_score_mask_pack_status)
-
-__device__ __forceinline__ uint32_t smem_u32(const void* q) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(q));
-}
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void ring_bar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void ring_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void ring_arrive_expect(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-// Bounded wait for phase `parity` of the barrier; false on expiry or when
-// another thread of the CTA has given up (*abort set).
-__device__ __forceinline__ bool ring_wait(uint32_t bar, uint32_t parity, const volatile int* abort) {
-    const uint64_t t0 = global_ns();
-    for (uint32_t k = 0;; ++k) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.b32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if ((k & 63) == 63 && ((abort && *abort) || global_ns() - t0 > kRingWaitNs)) return false;
-    }
-}
-// One contiguous global -> shared copy completing on `bar` (no multicast).
-__device__ __forceinline__ void ring_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
-// 8 consecutive elements of dtype DT widened to FP32 (16 B for 16-bit types,
-// 32 B for FP32), non-L1-allocating.
-template <int DT>
-__device__ __forceinline__ void load8(const void* base, size_t e0, float (&x)[8]) {
-    const uint4* q = reinterpret_cast<const uint4*>(static_cast<const char*>(base) + e0 * Dtype<DT>::kBytes);
-    if (DT == TB_F32) {
-        const uint4 a = ldg_stream(q), b = ldg_stream(q + 1);
-        const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = __uint_as_float(u[i]);
-    } else {
-        decode8<DT>(ldg_stream(q), x);
-    }
-}
-
-// The producer of a ring (one thread): for each of this CTA's slabs, the S
-// gradient rows of `row_bytes` each, into stages it % nst; stage reuse waits
-// for the consumers' release.  It stays until every issued stage has been
-// released, or, if a wait expired anywhere in the CTA, until the copies it
-// issued have landed; then it records the error.
-__device__ __forceinline__ void ring_produce(const void* g0, size_t S, size_t gstride_b, uint32_t row_bytes,
-                                             size_t nslabs, int nst, unsigned char* ring, uint64_t* full,
-                                             uint64_t* empty, volatile int* abort) {
-    uint32_t it = 0;
-    bool ok = true;
-    for (size_t sl = blockIdx.x; ok && sl < nslabs; sl += gridDim.x) {
-        const char* g = static_cast<const char*>(g0) + sl * static_cast<size_t>(row_bytes);
-        for (size_t s = 0; s < S; ++s, ++it) {
-            const uint32_t st = it % nst, use = it / nst;
-            if (use > 0 && !ring_wait(smem_u32(&empty[st]), (use - 1) & 1u, abort)) {
-                ok = false;
-                break;
-            }
-            ring_arrive_expect(smem_u32(&full[st]), row_bytes);
-            ring_copy(smem_u32(ring + st * row_bytes), g + s * gstride_b, row_bytes, smem_u32(&full[st]));
-        }
-    }
-    if (!ok) *abort = 1;  // consumers stop waiting for stages that will not come
-    const uint32_t first = it > static_cast<uint32_t>(nst) ? it - nst : 0;
-    for (uint32_t j = first; j < it; ++j) {
-        if (ok && ring_wait(smem_u32(&empty[j % nst]), (j / nst) & 1u, abort)) continue;
-        ok = false;
-        ring_wait(smem_u32(&full[j % nst]), (j / nst) & 1u, nullptr);
-    }
-    if (!ok) {
-        *abort = 1;
-        atomicExch(&g_ring_error, 1);
-    }
-}
-
-// Barrier setup shared by the ring kernels (thread 0, then a CTA barrier).
-__device__ __forceinline__ void ring_setup(int nst, uint64_t* full, uint64_t* empty, int* abort_flag) {
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < nst; ++i) {
-            ring_bar_init(smem_u32(&full[i]), 1);
-            ring_bar_init(smem_u32(&empty[i]), kRingConsumers / 32);
-        }
-        *abort_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-}
-
-template <int N>
-__device__ __forceinline__ float (&part8(float (&x)[N], int k))[8] {
-    return *reinterpret_cast<float(*)[8]>(&x[8 * k]);
-}
-
-// Plain pass over nslabs whole slabs with 16-bit gradients through the ring.
-// Thread (warp w, lane l) owns two 8-element pieces of each slab, at slab
-// offsets 512 w + 256 k + 8 l (k = 0, 1): each warp reads a stage in two
-// conflict-free 512-byte sweeps, and every N:M group (M <= 8) lies inside a
-// piece.  Requirements (checked on the host): 16-byte aligned W, W', G,
-// Fisher buffers and g_stride * 2; mask alignment for the piece's bytes.
-template <int WDT, int GDT, int M>
-__global__ void __launch_bounds__(kRingConsumers + 32, 2) fused_ring_kernel(const FusedParams p, size_t nslabs,
-                                                                            int nst) {
-    extern __shared__ __align__(128) unsigned char ring[];
-    __shared__ __align__(8) uint64_t full[kRingMaxStages];
-    __shared__ __align__(8) uint64_t empty[kRingMaxStages];
-    __shared__ int abort_flag;
-    constexpr uint32_t kRow = kSlab * Dtype<GDT>::kBytes;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    ring_setup(nst, full, empty, &abort_flag);
-    volatile int* abort = &abort_flag;
-    if (warp == kRingConsumers / 32) {
-        if (lane == 0) ring_produce(p.g, p.S, p.gstride * Dtype<GDT>::kBytes, kRow, nslabs, nst, ring, full, empty,
-                                    abort);
-        return;
-    }
-    // ---- consumers ----
-    const uint64_t beta2 = pack2(p.beta, p.beta), c2 = pack2(p.contrib, p.contrib);
-    int ties = 0;
-    uint32_t it = 0;
-    for (size_t sl = blockIdx.x; sl < nslabs; sl += gridDim.x) {
-        const size_t e0 = sl * kSlab + warp * 512 + lane * 8;  // piece k at e0 + 256 k
-        float w[kEpt], F[kEpt];
-        load8<WDT>(p.w, e0, part8(w, 0));
-        load8<WDT>(p.w, e0 + 256, part8(w, 1));
-        if (p.use_fin) {
-            load8<TB_F32>(p.fin, e0, part8(F, 0));
-            load8<TB_F32>(p.fin, e0 + 256, part8(F, 1));
-        } else {
-#pragma unroll
-            for (int i = 0; i < kEpt; ++i) F[i] = 0.0f;
-        }
-        for (size_t s = 0; s < p.S; ++s, ++it) {
-            const uint32_t st = it % nst;
-            if (!ring_wait(smem_u32(&full[st]), (it / nst) & 1u, abort)) {
-                *abort = 1;
-                atomicExch(&g_ring_error, 1);
-                return;
-            }
-            const unsigned char* row = ring + st * kRow + (warp * 512 + lane * 8) * Dtype<GDT>::kBytes;
-            const uint4 a = *reinterpret_cast<const uint4*>(row);
-            const uint4 b = *reinterpret_cast<const uint4*>(row + 256 * Dtype<GDT>::kBytes);
-            __syncwarp();
-            if (lane == 0) ring_arrive(smem_u32(&empty[st]));
-            float x[kEpt];
-            decode8<GDT>(a, part8(x, 0));
-            decode8<GDT>(b, part8(x, 1));
-            if (s == 0 && p.first) {
-#pragma unroll
-                for (int i = 0; i < kEpt; ++i) F[i] = ema_first(p.alpha, x[i]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < kEpt; i += 2) ema_next2(F[i], F[i + 1], beta2, c2, x[i], x[i + 1]);
-            }
-        }
-        float sc[kEpt];
-        const bool have_f = p.have_f != 0;
-#pragma unroll
-        for (int i = 0; i < kEpt; ++i) sc[i] = importance(w[i], F[i], p.damp, p.mode, have_f);
-        const uint64_t packed = groups16<M>(p, sc, w, ties);
-        constexpr int kPieceBytes = 8 / M;  // mask bytes of one 8-element piece
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const size_t e = e0 + 256 * k;
-            float4* wo = reinterpret_cast<float4*>(p.wout + e);
-            stg_stream(wo, make_float4(w[8 * k], w[8 * k + 1], w[8 * k + 2], w[8 * k + 3]));
-            stg_stream(wo + 1, make_float4(w[8 * k + 4], w[8 * k + 5], w[8 * k + 6], w[8 * k + 7]));
-            const uint64_t bits = packed >> (8 * kPieceBytes * k);
-            if (kPieceBytes == 4) *reinterpret_cast<uint32_t*>(p.mout + e / M) = static_cast<uint32_t>(bits);
-            else if (kPieceBytes == 2) *reinterpret_cast<uint16_t*>(p.mout + e / M) = static_cast<uint16_t>(bits);
-            else p.mout[e / M] = static_cast<uint8_t>(bits);
-            if (p.fout && have_f) {
-                float4* fo = reinterpret_cast<float4*>(p.fout + e);
-                stg_stream(fo, make_float4(F[8 * k], F[8 * k + 1], F[8 * k + 2], F[8 * k + 3]));
-                stg_stream(fo + 1, make_float4(F[8 * k + 4], F[8 * k + 5], F[8 * k + 6], F[8 * k + 7]));
-            }
-            if (p.sout) {
-                float4* so = reinterpret_cast<float4*>(p.sout + e);
-                stg_stream(so, make_float4(sc[8 * k], sc[8 * k + 1], sc[8 * k + 2], sc[8 * k + 3]));
-                stg_stream(so + 1, make_float4(sc[8 * k + 4], sc[8 * k + 5], sc[8 * k + 6], sc[8 * k + 7]));
-            }
-        }
-    }
-    if (p.ties) warp_add_count(p.ties, ties);
-}
-
 // ---- sample split: partial Fisher sums pushed to the ranks that own them ------
 constexpr int kMaxScatterRanks = 8;
 constexpr int kMaxPartialSamples = 128;
@@ -551,66 +313,65 @@ __device__ __forceinline__ void wsum_next2(float& a0, float& a1, uint64_t c2, fl
     a1 = __fadd_rn(a1, t1);
 }
 
-// Whole slabs: the rank's samples of each 4096-element slab through the ring,
-// sum_t c_t g_t^2 per element in registers (from +0, samples in order, the
-// arithmetic of tb_fisher_weighted_sum), each 8-element piece stored to its
-// owner (a peer's memory over NVLink, or this GPU's own).  Starts are
-// multiples of 8, so no piece straddles two owners.
+// 16 consecutive elements per thread, U samples' loads in flight as in the
+// fused vector kernel: sum_t c_t g_t^2 per element in registers (from +0,
+// samples in order: the arithmetic of tb_fisher_weighted_sum, bit for bit),
+// each 8-element half stored to its owner (a peer's memory over NVLink, or
+// this GPU's own).  Range starts are multiples of 8, so no half straddles two
+// owners.  Requires 16-byte aligned gradients, rows and destinations.
 template <int GDT>
-__global__ void __launch_bounds__(kRingConsumers + 32, 2) partial_ring_kernel(const PartialSpec q, size_t nslabs,
-                                                                              int nst) {
-    extern __shared__ __align__(128) unsigned char ring[];
-    __shared__ __align__(8) uint64_t full[kRingMaxStages];
-    __shared__ __align__(8) uint64_t empty[kRingMaxStages];
-    __shared__ int abort_flag;
-    constexpr uint32_t kRow = kSlab * Dtype<GDT>::kBytes;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    ring_setup(nst, full, empty, &abort_flag);
-    volatile int* abort = &abort_flag;
-    if (warp == kRingConsumers / 32) {
-        if (lane == 0) ring_produce(q.g, q.S, q.gstride * Dtype<GDT>::kBytes, kRow, nslabs, nst, ring, full, empty,
-                                    abort);
-        return;
-    }
-    uint32_t it = 0;
-    for (size_t sl = blockIdx.x; sl < nslabs; sl += gridDim.x) {
-        const size_t e0 = sl * kSlab + warp * 512 + lane * 8;
+__global__ void __launch_bounds__(kThreads, 3) partial_vec_kernel(const PartialSpec q) {
+    constexpr int GW = Vec16<GDT>::kWords;
+    constexpr int U = (GW == 2) ? 4 : 2;
+    const size_t nchunks = q.N / kEpt;
+    const size_t gstride_b = q.gstride * Dtype<GDT>::kBytes;
+    for (size_t c = blockIdx.x * (size_t)kThreads + threadIdx.x; c < nchunks; c += (size_t)gridDim.x * kThreads) {
+        const size_t e0 = c * kEpt;
         float acc[kEpt];
 #pragma unroll
         for (int i = 0; i < kEpt; ++i) acc[i] = 0.0f;
-        for (size_t s = 0; s < q.S; ++s, ++it) {
-            const uint32_t st = it % nst;
-            if (!ring_wait(smem_u32(&full[st]), (it / nst) & 1u, abort)) {
-                *abort = 1;
-                atomicExch(&g_ring_error, 1);
-                return;
+        const char* gb = static_cast<const char*>(q.g) + e0 * Dtype<GDT>::kBytes;
+        size_t s = 0;
+        for (; s + U <= q.S; s += U) {
+            uint4 b[U][GW];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int k = 0; k < GW; ++k)
+                    b[u][k] = ldg_stream(reinterpret_cast<const uint4*>(gb + (s + u) * gstride_b) + k);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float x[kEpt];
+                Vec16<GDT>::decode(b[u], x);
+                const uint64_t c2 = pack2(q.c[s + u], q.c[s + u]);
+#pragma unroll
+                for (int i = 0; i < kEpt; i += 2) wsum_next2(acc[i], acc[i + 1], c2, x[i], x[i + 1]);
             }
-            const unsigned char* row = ring + st * kRow + (warp * 512 + lane * 8) * Dtype<GDT>::kBytes;
-            const uint4 a = *reinterpret_cast<const uint4*>(row);
-            const uint4 b = *reinterpret_cast<const uint4*>(row + 256 * Dtype<GDT>::kBytes);
-            __syncwarp();
-            if (lane == 0) ring_arrive(smem_u32(&empty[st]));
+        }
+        for (; s < q.S; ++s) {
+            uint4 b[GW];
+#pragma unroll
+            for (int k = 0; k < GW; ++k) b[k] = ldg_stream(reinterpret_cast<const uint4*>(gb + s * gstride_b) + k);
             float x[kEpt];
-            decode8<GDT>(a, part8(x, 0));
-            decode8<GDT>(b, part8(x, 1));
+            Vec16<GDT>::decode(b, x);
             const uint64_t c2 = pack2(q.c[s], q.c[s]);
 #pragma unroll
             for (int i = 0; i < kEpt; i += 2) wsum_next2(acc[i], acc[i + 1], c2, x[i], x[i + 1]);
         }
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const size_t e = e0 + 256 * k;
+        for (int h = 0; h < 2; ++h) {
+            const size_t e = e0 + 8 * h;
             const int r = owner_of(q, e);
             float4* d = reinterpret_cast<float4*>(q.dest[r] + (e - q.start[r]));
-            __stcs(d, make_float4(acc[8 * k], acc[8 * k + 1], acc[8 * k + 2], acc[8 * k + 3]));
-            __stcs(d + 1, make_float4(acc[8 * k + 4], acc[8 * k + 5], acc[8 * k + 6], acc[8 * k + 7]));
+            __stcs(d, make_float4(acc[8 * h], acc[8 * h + 1], acc[8 * h + 2], acc[8 * h + 3]));
+            __stcs(d + 1, make_float4(acc[8 * h + 4], acc[8 * h + 5], acc[8 * h + 6], acc[8 * h + 7]));
         }
     }
     __threadfence_system();  // the pushed partials are visible to their owners once the kernel ends
 }
 
-// Elements [e_begin, N) one per thread: any dtype and alignment, and the
-// ring's ragged tail.
+// Elements [e_begin, N) one per thread: any alignment, and the vector
+// kernel's ragged tail.
 __global__ void __launch_bounds__(kThreads) partial_scalar_kernel(const PartialSpec q, int gdt, size_t e_begin) {
     for (size_t i = e_begin + blockIdx.x * (size_t)kThreads + threadIdx.x; i < q.N; i += (size_t)gridDim.x * kThreads) {
         float acc = 0.0f;
@@ -736,49 +497,6 @@ void launch_group(const FusedParams& p, int m, cudaStream_t st) {
     }
 }
 
-// ---- ring launch ---------------------------------------------------------------
-constexpr int kRingStages = 12;  // 12 x 8 KB = 96 KB per CTA, two CTAs per SM
-
-// The bulk-copy ring runs the plain pass unless TB_FUSED_RING=0 is set in the
-// environment (read once), which selects the register-staged kernel instead.
-bool ring_enabled() {
-    static const bool on = [] {
-        const char* v = std::getenv("TB_FUSED_RING");
-        return !(v && v[0] == '0');
-    }();
-    return on;
-}
-
-int sm_count() {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    return sms;
-}
-
-template <int WDT, int GDT, int M>
-void launch_ring_t(const FusedParams& p, size_t nslabs, cudaStream_t st) {
-    const int smem = kRingStages * kSlab * Dtype<GDT>::kBytes;
-    cudaFuncSetAttribute(fused_ring_kernel<WDT, GDT, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    const size_t grid = std::min<size_t>(nslabs, static_cast<size_t>(2 * sm_count()));
-    fused_ring_kernel<WDT, GDT, M><<<static_cast<unsigned>(grid), kRingConsumers + 32, smem, st>>>(p, nslabs,
-                                                                                                   kRingStages);
-}
-
-template <int WDT, int GDT>
-void launch_ring_m(const FusedParams& p, int m, size_t nslabs, cudaStream_t st) {
-    if (m == 2) launch_ring_t<WDT, GDT, 2>(p, nslabs, st);
-    else if (m == 4) launch_ring_t<WDT, GDT, 4>(p, nslabs, st);
-    else launch_ring_t<WDT, GDT, 8>(p, nslabs, st);
-}
-
-template <int GDT>
-void launch_ring_g(const FusedParams& p, int m, size_t nslabs, cudaStream_t st) {
-    if (p.wdt == TB_F32) launch_ring_m<TB_F32, GDT>(p, m, nslabs, st);
-    else if (p.wdt == TB_BF16) launch_ring_m<TB_BF16, GDT>(p, m, nslabs, st);
-    else launch_ring_m<TB_F16, GDT>(p, m, nslabs, st);
-}
-
 int dtype_bytes(int dt) { return dt == TB_F32 ? 4 : 2; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -857,27 +575,6 @@ int launch_fused(FusedParams p, int m, cudaStream_t st) {
                         (!p.sout || aligned16(p.sout)) &&
                         (reinterpret_cast<uintptr_t>(p.mout) % (kEpt / m) == 0) &&
                         ((p.gstride * dtype_bytes(p.gdt)) % 16 == 0) && parts_aligned16(p);
-    // Whole 4096-element slabs of a plain pass with 16-bit gradients go through
-    // the bulk-copy ring; the rest through the register-staged kernels below.
-    const bool ring_ok = ring_enabled() && vec_ok && p.variant == kVarPlain && p.S > 0 && p.gdt != TB_F32 &&
-                         aligned16(p.g) && (m != 2 || reinterpret_cast<uintptr_t>(p.mout) % 4 == 0) &&
-                         (m != 4 || reinterpret_cast<uintptr_t>(p.mout) % 2 == 0);
-    const size_t nslabs = ring_ok ? p.N / kSlab : 0;
-    if (nslabs) {
-        if (p.gdt == TB_BF16) launch_ring_g<TB_BF16>(p, m, nslabs, st);
-        else launch_ring_g<TB_F16>(p, m, nslabs, st);
-        if ((rc = check_launch("fused_ring_kernel"))) return rc;
-        const size_t done = nslabs * kSlab;
-        if (done == p.N) return TB_OK;
-        p.N -= done;
-        p.w = static_cast<const char*>(p.w) + done * dtype_bytes(p.wdt);
-        p.g = static_cast<const char*>(p.g) + done * dtype_bytes(p.gdt);
-        if (p.fin) p.fin += done;
-        p.wout += done;
-        p.mout += done / m;
-        if (p.fout) p.fout += done;
-        if (p.sout) p.sout += done;
-    }
     const size_t nvec = vec_ok ? (p.N / kEpt) * kEpt : 0;
     if (nvec) {
         FusedParams q = p;
@@ -1025,43 +722,21 @@ int tb_fisher_partial_scatter(const void* gradients, int g_dtype, size_t S, size
     int rc = require_device(nullptr);
     if (rc) return rc;
     auto st = static_cast<cudaStream_t>(stream);
-    const bool ring = ring_enabled() && S > 0 && g_dtype != TB_F32 && aligned && aligned16(gradients) &&
-                      (stride * 2) % 16 == 0;
-    const size_t nslabs = ring ? N / kSlab : 0;
-    if (nslabs) {
-        const int smem = kRingStages * kSlab * 2;
-        const size_t grid = std::min<size_t>(nslabs, static_cast<size_t>(2 * sm_count()));
-        if (g_dtype == TB_BF16) {
-            cudaFuncSetAttribute(partial_ring_kernel<TB_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            partial_ring_kernel<TB_BF16><<<static_cast<unsigned>(grid), kRingConsumers + 32, smem, st>>>(q, nslabs,
-                                                                                                       kRingStages);
-        } else {
-            cudaFuncSetAttribute(partial_ring_kernel<TB_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            partial_ring_kernel<TB_F16><<<static_cast<unsigned>(grid), kRingConsumers + 32, smem, st>>>(q, nslabs,
-                                                                                                      kRingStages);
-        }
-        if ((rc = check_launch("partial_ring_kernel"))) return rc;
+    const bool vec = S > 0 && aligned && aligned16(gradients) && (stride * dtype_bytes(g_dtype)) % 16 == 0;
+    const size_t nvec = vec ? N / kEpt * kEpt : 0;
+    if (nvec) {
+        const unsigned grid = grid_for(nvec / kEpt);
+        if (g_dtype == TB_BF16) partial_vec_kernel<TB_BF16><<<grid, kThreads, 0, st>>>(q);
+        else if (g_dtype == TB_F16) partial_vec_kernel<TB_F16><<<grid, kThreads, 0, st>>>(q);
+        else partial_vec_kernel<TB_F32><<<grid, kThreads, 0, st>>>(q);
+        if ((rc = check_launch("partial_vec_kernel"))) return rc;
     }
-    const size_t done = nslabs * kSlab;
+    const size_t done = nvec;
     if (done < N) {
         partial_scalar_kernel<<<grid_for(N - done), kThreads, 0, st>>>(q, g_dtype, done);
         if ((rc = check_launch("partial_scalar_kernel"))) return rc;
     }
     return TB_OK;
-}
-
-int tb_score_mask_pack_status(void* stream) {
-    int rc = require_device(nullptr);
-    if (rc) return rc;
-    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return cuda_fail(e, "tb_score_mask_pack_status");
-    int err = 0;
-    const int zero = 0;
-    e = cudaMemcpyFromSymbol(&err, g_ring_error, sizeof(int));
-    if (e == cudaSuccess && err) e = cudaMemcpyToSymbol(g_ring_error, &zero, sizeof(int));
-    if (e != cudaSuccess) return cuda_fail(e, "tb_score_mask_pack_status");
-    return err ? fail(TB_ERR_TIMEOUT, "a staging wait of the fused pass expired; its outputs are incomplete")
-               : TB_OK;
 }
 
 int tb_score_mask_pack(const tb_prune_args* args, void* stream) {

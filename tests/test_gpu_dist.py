@@ -87,7 +87,6 @@ def _worker(rank, world, port_no, tmpdir):
     for k in (0, 1, 0):
         td.prune_sample_split_push(dist, torch, bufs, k, wd, tb.BF16, gd, tb.BF16, S, s0, qw, qm,
                                    strategy="optimal", redist="proportional", mode="obd", fisher_out=qF)
-    tb.check(tb.lib().tb_score_mask_pack_status(None))
     torch.cuda.synchronize()
     np.save(os.path.join(tmpdir, f"pu_w{rank}.npy"), qw[e0:e1].cpu().numpy())
     np.save(os.path.join(tmpdir, f"pu_m{rank}.npy"), qm[e0 // 4:e1 // 4].cpu().numpy())
