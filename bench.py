@@ -1180,6 +1180,8 @@ def run_block_obs(torch, tb, ranks, passes=10, n=4096 * 4096, cpu=True):
                                  "max": round(max(kern), 2)},
            "importance_device_ms_median": round(statistics.median(p[0] for p in phases), 3),
            "host_targets_ms_median": round(statistics.median(p[1] for p in phases), 3),
+           "call_host_ms": [round(p[3], 2) for p in phases],
+           "note": "nvidia-smi samples the clocks every 200 ms during the passes, as a driver's sampler would",
            "clocks": clk, "blocks": n // block,
            "blocks_per_s": round(n / block / (t / 1e3)), "gparams_per_s": round(n / (t / 1e3) / 1e9, 4),
            "pruned": pruned.value}

@@ -148,7 +148,8 @@ int tb_redistribute(float* weights, const uint8_t* mask, const float* importance
  * every score >= it is kept.  Writes 1 byte per element to mask_out (may be
  * NULL), the threshold and the number of pruned elements to host memory, and
  * synchronises the stream.  keep >= N keeps everything (threshold 0, pruned 0).
- * Scratch: about 16 KB of device memory, allocated stream-ordered per call. */
+ * Scratch: about 16 KB of device memory, stream-ordered from a pool the
+ * library keeps per device (its memory is retained between calls). */
 int tb_threshold_select(const float* scores, size_t N, float sparsity, uint8_t* mask_out,
                         float* threshold_out, uint64_t* pruned_out, void* stream);
 /* EHAPPruner::apply_mask (ehap.hpp:334-362): zero weights[i] where mask[i] == 0
@@ -173,7 +174,9 @@ int tb_compensate(float* weights, const uint8_t* mask, const float* importance, 
  * updates and rank-1 deflation.  Weights are updated in place; the number
  * pruned goes to *pruned_out (host) and the call synchronises the stream.
  * Scratch (the per-block importances, targets and launch order, ~12 bytes per
- * block) is stream-ordered (cudaMallocAsync) and freed before returning.
+ * block) is stream-ordered from the library's per-device pool (memory
+ * retained between calls, so later calls allocate nothing from the driver);
+ * the launch setup per (block, snapshots) is queried once per device.
  * block <= 224 (one thread per row; a block's downdate columns, up to
  * block - 1 of them, live in shared memory). */
 int tb_block_obs(float* weights, const float* fisher, const float* const* hist, int K, size_t N,
@@ -300,7 +303,7 @@ int tb_score_mask_pack(const tb_prune_args* args, void* stream);
  * everything is kept), *ehap_pruned_out (weights the threshold zeroed) and
  * *coring_pruned_out (the analytic (N/M)*(M-N) of coring.hpp:192,222) are
  * host values, any may be NULL; synchronises the stream.  Scratch: about
- * 16 KB, stream-ordered.  Sparsity outside (0, 1) -> TB_ERR_CONFIG before any
+ * 16 KB, stream-ordered from the library's per-device pool.  Sparsity outside (0, 1) -> TB_ERR_CONFIG before any
  * N:M check, as the reference's EHAP stage fails first. */
 int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* threshold_out,
                          uint64_t* ehap_pruned_out, uint64_t* coring_pruned_out, void* stream);

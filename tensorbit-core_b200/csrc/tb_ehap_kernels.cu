@@ -95,9 +95,12 @@ int tb_ehap_apply_mask(float* weights, const uint8_t* mask, size_t N, uint64_t* 
     auto st = static_cast<cudaStream_t>(stream);
     unsigned long long* cnt = nullptr;
     if (pruned_out) {
-        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&cnt), sizeof(*cnt), st);
-        if (e == cudaSuccess) e = cudaMemsetAsync(cnt, 0, sizeof(*cnt), st);
-        if (e != cudaSuccess) return cuda_fail(e, "tb_ehap_apply_mask counter");
+        if ((rc = scratch_alloc(reinterpret_cast<void**>(&cnt), sizeof(*cnt), st))) return rc;
+        cudaError_t e = cudaMemsetAsync(cnt, 0, sizeof(*cnt), st);
+        if (e != cudaSuccess) {
+            scratch_free(cnt, st);
+            return cuda_fail(e, "tb_ehap_apply_mask counter");
+        }
     }
     ehap_apply_kernel<<<grid_for(N), kThreads, 0, st>>>(weights, mask, N, cnt);
     rc = check_launch("ehap_apply_kernel");
@@ -105,7 +108,7 @@ int tb_ehap_apply_mask(float* weights, const uint8_t* mask, size_t N, uint64_t* 
         unsigned long long h = 0;
         cudaError_t e = cudaMemcpyAsync(&h, cnt, sizeof(h), cudaMemcpyDeviceToHost, st);
         if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-        cudaFreeAsync(cnt, st);
+        scratch_free(cnt, st);
         if (!rc && e != cudaSuccess) rc = cuda_fail(e, "tb_ehap_apply_mask readback");
         *pruned_out = h;
     }
@@ -119,12 +122,11 @@ int tb_fisher_normalize(float* fisher, size_t N, void* stream) {
     if (rc) return rc;
     auto st = static_cast<cudaStream_t>(stream);
     float* norm = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&norm), sizeof(float), st);
-    if (e != cudaSuccess) return cuda_fail(e, "tb_fisher_normalize scratch");
+    if ((rc = scratch_alloc(reinterpret_cast<void**>(&norm), sizeof(float), st))) return rc;
     fisher_norm_sum_kernel<<<1, 32, 0, st>>>(fisher, N, norm);
     fisher_scale_kernel<<<grid_for(N), kThreads, 0, st>>>(fisher, N, norm);
     rc = check_launch("fisher normalisation");
-    cudaFreeAsync(norm, st);
+    scratch_free(norm, st);
     return rc;
 }
 

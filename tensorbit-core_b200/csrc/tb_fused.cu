@@ -800,10 +800,9 @@ int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* thres
     // The threshold's three digit passes over the scores (keep < N).
     SelectState* sel = nullptr;
     if (keep < N) {
-        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&sel), sizeof(SelectState), st);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(select scratch)");
+        if ((rc = scratch_alloc(reinterpret_cast<void**>(&sel), sizeof(SelectState), st))) return rc;
         if ((rc = threshold_digits(args->scores_out, N, keep, sel, st))) {
-            cudaFreeAsync(sel, st);
+            scratch_free(sel, st);
             return rc;
         }
     }
@@ -823,7 +822,7 @@ int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* thres
     }
     rc = launch_fused(b, m, st);
     if (rc == TB_OK) rc = threshold_finish(N, keep, sel, threshold_out, ehap_pruned_out, st);
-    if (sel) cudaFreeAsync(sel, st);
+    scratch_free(sel, st);
     if (rc == TB_OK && coring_pruned_out)
         *coring_pruned_out = static_cast<uint64_t>(N / m) * static_cast<uint64_t>(m - args->nm_n);  // coring.hpp:192,222
     return rc;

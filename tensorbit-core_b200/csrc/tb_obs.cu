@@ -24,6 +24,9 @@
 #include <cfloat>
 #include <chrono>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <vector>
 
 #include "tb_device.cuh"
@@ -277,6 +280,42 @@ struct PhaseEvents {
 }  // namespace
 }  // namespace tb
 
+namespace tb {
+namespace {
+// Launch setup of block_obs_kernel per (device, block, snapshots): the
+// shared-memory limit raised once to the largest target a block can have
+// (B - 1), and the CTAs per SM for every target 1..B-1, queried once - so a
+// call makes no attribute or occupancy queries after the first.
+struct OccKey {
+    int dev, B, K;
+    bool operator<(const OccKey& o) const { return std::tie(dev, B, K) < std::tie(o.dev, o.B, o.K); }
+};
+std::mutex g_occ_mu;
+std::map<OccKey, std::vector<int>> g_occ;
+
+int obs_occupancy(int B, int K, unsigned threads, const std::vector<int>** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    auto it = g_occ.find({dev, B, K});
+    if (it == g_occ.end()) {
+        const size_t tcap = B > 1 ? static_cast<size_t>(B - 1) : 0;
+        e = cudaFuncSetAttribute(block_obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(obs_smem_bytes(B, K, tcap)));
+        std::vector<int> occ(static_cast<size_t>(B) + 1, 0);
+        for (size_t t = 1; t <= tcap && e == cudaSuccess; ++t)
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[t], block_obs_kernel, static_cast<int>(threads),
+                                                              obs_smem_bytes(B, K, t));
+        if (e != cudaSuccess) return cuda_fail(e, "tb_block_obs setup");
+        it = g_occ.emplace(OccKey{dev, B, K}, std::move(occ)).first;
+    }
+    *out = &it->second;
+    return TB_OK;
+}
+}  // namespace
+}  // namespace tb
+
 extern "C" int tb_block_obs_phase_times(float* ms_out, int n) {
     if (!ms_out || n < 1) return fail(TB_ERR_ARG, "tb_block_obs_phase_times: null or empty output");
     for (int i = 0; i < n && i < 4; ++i) ms_out[i] = g_obs_phase_ms[i];
@@ -311,16 +350,16 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
     float* d_imp = nullptr;
     uint32_t* d_tgt = nullptr;
     unsigned long long* d_cnt = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d_imp), nb * sizeof(float), st);
-    // targets by block, then the launch order of the blocks
-    if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&d_tgt), 2 * nb * sizeof(uint32_t), st);
-    if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&d_cnt), sizeof(unsigned long long), st);
-    if (e != cudaSuccess) return cuda_fail(e, "tb_block_obs scratch");
-    auto release = [&] {
-        cudaFreeAsync(d_imp, st);
-        cudaFreeAsync(d_tgt, st);
-        cudaFreeAsync(d_cnt, st);
-    };
+    // one scratch block: importances [nb] f32, targets then launch order
+    // [2 nb] u32, the pruned counter (8-byte aligned)
+    const size_t o_tgt = nb * sizeof(float), o_cnt = (o_tgt + 2 * nb * sizeof(uint32_t) + 7) / 8 * 8;
+    char* scratch = nullptr;
+    if ((rc = scratch_alloc(reinterpret_cast<void**>(&scratch), o_cnt + sizeof(unsigned long long), st))) return rc;
+    d_imp = reinterpret_cast<float*>(scratch);
+    d_tgt = reinterpret_cast<uint32_t*>(scratch + o_tgt);
+    d_cnt = reinterpret_cast<unsigned long long*>(scratch + o_cnt);
+    cudaError_t e = cudaSuccess;
+    auto release = [&] { scratch_free(scratch, st); };
     block_importance_kernel<<<static_cast<unsigned>(std::min<size_t>((nb + 255) / 256, 148 * 16)), 256, 0, st>>>(
         weights, fisher, damping, N, static_cast<int>(B), nb, d_imp);
     std::vector<float> imp(nb);
@@ -378,15 +417,11 @@ extern "C" int tb_block_obs(float* weights, const float* fisher, const float* co
     uint32_t tmax = 0;
     for (uint32_t x : tgt) tmax = std::max(tmax, x);
     const unsigned threads = static_cast<unsigned>((B + 31) / 32 * 32);
-    e = cudaFuncSetAttribute(block_obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(obs_smem_bytes(B, K ? K : 1, tmax)));
     // CTAs per SM for each target: the downdate columns in shared memory grow
     // with it, so blocks that prune fewer weights fit more CTAs on an SM
-    std::vector<int> occ(tmax + 1, 0);
-    for (uint32_t t = 1; t <= tmax && e == cudaSuccess; ++t)
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[t], block_obs_kernel, static_cast<int>(threads),
-                                                          obs_smem_bytes(B, K ? K : 1, t));
-    if (e != cudaSuccess) { release(); return cuda_fail(e, "tb_block_obs setup"); }
+    const std::vector<int>* occp = nullptr;
+    if ((rc = obs_occupancy(static_cast<int>(B), K ? K : 1, threads, &occp))) { release(); return rc; }
+    const std::vector<int>& occ = *occp;
     // Within each slice of at most 2^30 blocks (block ids stay 32-bit), the
     // blocks run in descending order of target (counting sort, block id order
     // within a target; target-0 blocks are left out), one launch per run of

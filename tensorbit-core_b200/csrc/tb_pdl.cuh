@@ -12,8 +12,22 @@
 // only when it exits.  With the trigger issued right after pdl_wait() in every
 // kernel (successors resident early), the exact-OBS chain of a 14336-wide
 // layer gave results that differed from run to run on B200, some with a failed
-// Cholesky pivot, although every ordering of the schedule checks out; without
-// the early trigger it is bit-reproducible and barely slower.
+// Cholesky pivot, although every event and stream ordering of the schedule
+// checks out.  The edge the trigger breaks is a cache contract, not an
+// ordering: base_chol_inv_kernel reads the Schur-updated block A, and
+// inblock_kernel the error-updated columns Wr and the factor V, through
+// const __restrict__ pointers, which lets the compiler serve those loads from
+// the non-coherent read-only path, whose contract is that the data does not
+// change during the reading kernel's lifetime.  Each of those buffers is
+// written by the launch just before the reader in its stream (a GEMM epilogue
+// or the previous base kernel).  With an early trigger the reader's lifetime
+// begins while those writes are still being made, so the contract no longer
+// holds; without it a kernel starts only after its predecessor has exited and
+// every read-only load sees the finished data.  The schedule is therefore
+// race-free exactly as launched here: stream order for a kernel's own
+// predecessor, events for the other streams, and no kernel resident before
+// the kernel whose output it reads has ended.  (The early trigger was also
+// not faster: 26.3 against 25.7 ms per pass.)
 #pragma once
 
 #include <cuda_runtime.h>

@@ -27,6 +27,42 @@ std::mutex g_mu;
 std::map<TableKey, uint8_t*> g_tables;
 }  // namespace
 
+namespace {
+std::mutex g_pool_mu;
+std::map<int, cudaMemPool_t> g_pools;
+}  // namespace
+
+int scratch_alloc(void** ptr, size_t bytes, cudaStream_t stream) {
+    int dev = 0;
+    int rc = require_device(&dev);
+    if (rc) return rc;
+    cudaMemPool_t pool = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_pool_mu);
+        auto it = g_pools.find(dev);
+        if (it == g_pools.end()) {
+            cudaMemPoolProps props{};
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = dev;
+            cudaError_t e = cudaMemPoolCreate(&pool, &props);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemPoolCreate(scratch)");
+            uint64_t keep = UINT64_MAX;
+            e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemPoolSetAttribute(scratch)");
+            g_pools[dev] = pool;
+        } else {
+            pool = it->second;
+        }
+    }
+    cudaError_t e = cudaMallocFromPoolAsync(ptr, bytes, pool, stream);
+    return e == cudaSuccess ? TB_OK : cuda_fail(e, "cudaMallocFromPoolAsync(scratch)");
+}
+
+void scratch_free(void* ptr, cudaStream_t stream) {
+    if (ptr) cudaFreeAsync(ptr, stream);
+}
+
 int fail(int code, const char* fmt, ...) {
     char buf[512];
     va_list ap;

@@ -22,5 +22,13 @@ int topn_table(int n, int m, const uint8_t** out);
 // True when the current device already holds the top-n-of-m tie table
 // (no build, no allocation).
 bool topn_table_ready(int n, int m);
+// Stream-ordered scratch for a call's small working buffers, from a memory
+// pool the library keeps per device with its memory retained between calls
+// (release threshold: never), so that after the first calls no allocation
+// reaches the driver's memory manager - where it could wait behind other
+// clients of the driver, such as a clock sampler - and calls on different
+// streams still get separate buffers.
+int scratch_alloc(void** ptr, size_t bytes, cudaStream_t stream);
+void scratch_free(void* ptr, cudaStream_t stream);
 
 }  // namespace tb

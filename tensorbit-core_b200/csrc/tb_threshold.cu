@@ -212,12 +212,11 @@ int tb_threshold_select(const float* scores, size_t N, float sparsity, uint8_t* 
     auto st = static_cast<cudaStream_t>(stream);
     SelectState* scratch = nullptr;
     if (keep < N) {
-        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), sizeof(SelectState), st);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(select scratch)");
+        if ((rc = scratch_alloc(reinterpret_cast<void**>(&scratch), sizeof(SelectState), st))) return rc;
     }
     rc = threshold_launch(scores, N, keep, mask_out, scratch, st);
     if (rc == TB_OK) rc = threshold_finish(N, keep, scratch, threshold_out, pruned_out, st);
-    if (scratch) cudaFreeAsync(scratch, st);
+    scratch_free(scratch, st);
     return rc;
 }
 
