@@ -165,3 +165,24 @@ MERGE_RUNS = {
     "dot_input": (["--input", ".", "--output", "../dot/model.tbm"], "shard1"),
     "empty": (["--input", "empty", "--output", "e.tbm"], "."),
 }
+
+
+def layered_model(path, layers=3, seed=300):
+    """A multi-tensor checkpoint for the pipelined real mode: per layer an F32
+    q_proj (256 x 256), a BF16 up_proj (512 x 256), an F16 down_proj
+    (256 x 512) and a norm vector (258 elements, not a multiple of M: tb-prune
+    skips it at CORING), then an I64 tensor (skipped as non-float) and an F32
+    lm_head - about 0.9 M weights per layer in the reference's dtypes."""
+    tensors = []
+    for k in range(layers):
+        s = seed + 10 * k
+        tensors.append((f"model.layers.{k}.self_attn.q_proj.weight", "F32", (256, 256),
+                        normal(256 * 256, 0.02, s).tobytes()))
+        tensors.append((f"model.layers.{k}.mlp.up_proj.weight", "BF16", (512, 256),
+                        to_bf16_bits(normal(512 * 256, 0.02, s + 1)).tobytes()))
+        tensors.append((f"model.layers.{k}.mlp.down_proj.weight", "F16", (256, 512),
+                        normal(256 * 512, 0.02, s + 2).astype(np.float16).view(np.uint16).tobytes()))
+        tensors.append((f"model.layers.{k}.input_layernorm.weight", "F32", (258,), normal(258, 1.0, s + 3).tobytes()))
+    tensors.append(("position_ids", "I64", (16,), np.arange(16, dtype=np.int64).tobytes()))
+    tensors.append(("lm_head.weight", "F32", (64, 256), normal(64 * 256, 0.02, seed + 99).tobytes()))
+    write_safetensors(path, tensors)
