@@ -282,27 +282,33 @@ struct PhaseEvents {
 
 namespace tb {
 namespace {
-// Launch setup of block_obs_kernel per (device, block, snapshots): the
-// shared-memory limit raised once to the largest target a block can have
-// (B - 1), and the CTAs per SM for every target 1..B-1, queried once - so a
-// call makes no attribute or occupancy queries after the first.
+// Launch setup of block_obs_kernel: the kernel's shared-memory limit (one
+// value per device, shared by every call) raised once to the largest any call
+// can need, and per (device, block, snapshots) the CTAs per SM for every
+// target 1..B-1, queried once - so a call makes no attribute or occupancy
+// queries after the first of its shape.
 struct OccKey {
     int dev, B, K;
     bool operator<(const OccKey& o) const { return std::tie(dev, B, K) < std::tie(o.dev, o.B, o.K); }
 };
 std::mutex g_occ_mu;
 std::map<OccKey, std::vector<int>> g_occ;
+std::vector<int> g_obs_smem_set;  // devices whose limit is raised
 
 int obs_occupancy(int B, int K, unsigned threads, const std::vector<int>** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     std::lock_guard<std::mutex> lk(g_occ_mu);
+    if (std::find(g_obs_smem_set.begin(), g_obs_smem_set.end(), dev) == g_obs_smem_set.end()) {
+        e = cudaFuncSetAttribute(block_obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(obs_smem_bytes(kMaxBlock, kMaxK, kMaxBlock - 1)));
+        if (e != cudaSuccess) return cuda_fail(e, "tb_block_obs setup");
+        g_obs_smem_set.push_back(dev);
+    }
     auto it = g_occ.find({dev, B, K});
     if (it == g_occ.end()) {
         const size_t tcap = B > 1 ? static_cast<size_t>(B - 1) : 0;
-        e = cudaFuncSetAttribute(block_obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(obs_smem_bytes(B, K, tcap)));
         std::vector<int> occ(static_cast<size_t>(B) + 1, 0);
         for (size_t t = 1; t <= tcap && e == cudaSuccess; ++t)
             e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[t], block_obs_kernel, static_cast<int>(threads),
