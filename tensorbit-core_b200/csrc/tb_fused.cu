@@ -367,7 +367,11 @@ __global__ void __launch_bounds__(kThreads, 3) partial_vec_kernel(const PartialS
             __stcs(d + 1, make_float4(acc[8 * h + 4], acc[8 * h + 5], acc[8 * h + 6], acc[8 * h + 7]));
         }
     }
-    __threadfence_system();  // the pushed partials are visible to their owners once the kernel ends
+    // The pushed partials are visible to their owners once the kernel ends: the
+    // CTA's stores are collected by the barrier and one system-scope fence
+    // (cumulative) per CTA, not one per thread waiting on its remote stores.
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
 }
 
 // Elements [e_begin, N) one per thread: any alignment, and the vector
@@ -382,7 +386,8 @@ __global__ void __launch_bounds__(kThreads) partial_scalar_kernel(const PartialS
         const int r = owner_of(q, i);
         q.dest[r][i - q.start[r]] = acc;
     }
-    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
 }
 
 // Generic kernel: one group of M elements per thread, scalar loads; covers any
