@@ -114,6 +114,10 @@ def parse():
     for k in ("e2e", "cpu", "obs", "block-obs", "ties", "layer", "sweep", "split", "digest", "verify", "tbprune"):
         ap.add_argument(f"--no-{k}", action="store_true")
     ap.add_argument("--obs-only", action="store_true", help="only the column-block exact OBS measurement")
+    ap.add_argument("--tb-prune-real", type=int, metavar="LAYERS", default=0,
+                    help="only: tb-prune real mode over a BF16 checkpoint of LAYERS 7B-class layers, against the "
+                         "reference CLI")
+    ap.add_argument("--workdir", default="/tmp/tb_prune_real", help="scratch directory for --tb-prune-real")
     ap.add_argument("--block-obs-only", action="store_true", help="only the reference-semantics block OBS timing")
     ap.add_argument("--block-obs-size", type=int, default=4096 * 4096,
                     help="weights of the block OBS tensor (default one 4096 x 4096 q_proj)")
@@ -581,6 +585,19 @@ def run_ours(args):
                   flush=True)
         ranks.close()
         return
+    if args.tb_prune_real:
+        if ranks.rank == 0:
+            import shutil
+            shutil.rmtree(args.workdir, ignore_errors=True)
+            os.makedirs(args.workdir)
+            try:
+                print(json.dumps({"tb_prune_real": run_tb_prune_real(torch, args.tb_prune_real,
+                                                                     torch.cuda.device_count(), args.workdir)}),
+                      flush=True)
+            finally:
+                shutil.rmtree(args.workdir, ignore_errors=True)
+        ranks.close()
+        return
     if args.obs_only:
         obs = run_obs(torch, tb, ranks.dev, args.obs_steps, args.obs_shape, ranks.dist, bf16_peak)
         if ranks.rank == 0:
@@ -930,6 +947,58 @@ def run_tb_prune_mode(torch, tb, ranks, steps, warmup):
     out["fused_equals_staged_bitwise"] = bool(same)
     out["speedup_fused_vs_staged"] = round(outs["staged"][0] / outs["fused"][0], 2)
     return out
+
+
+# ---------------------------------------------------------------------------
+# tb-prune real mode over a multi-GB checkpoint (the CLI drop-in)
+# ---------------------------------------------------------------------------
+def run_tb_prune_real(torch, layers, gpus, workdir, compare=True):
+    """Writes a BF16 safetensors checkpoint of `layers` 7B-class decoder layers
+    (random-init weights) to `workdir`, runs tb-prune real mode on it
+    (`--gpus`), and times the whole CLI run (host clock: read, H2D, decode,
+    gradients 0.01 w, EHAP + CORING, D2H, .tb writes, model.tbm).  The input
+    file was just written, so it is read from the page cache, not the disk.
+    With `compare`, the reference CLI (compiled under oracle/_ref) runs on the
+    same file and every output file must be byte-identical."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import inputs
+    model = os.path.join(workdir, "model.safetensors")
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    tensors = []
+    for k in range(layers):
+        for name, r, c in LAYER_7B:
+            w = (torch.randn(r * c, device="cuda", generator=gen, dtype=torch.bfloat16) * 0.02).view(torch.int16)
+            tensors.append((f"model.layers.{k}.{name}.weight", "BF16", (r, c), w.cpu().numpy().tobytes()))
+    inputs.write_safetensors(model, tensors)
+    del tensors
+    size = os.path.getsize(model)
+    params = layers * sum(r * c for _, r, c in LAYER_7B)
+    exe = os.path.join(ROOT, "tensorbit-core_b200", "bin", "tb-prune")
+    out = os.path.join(workdir, "ours")
+    t0 = time.perf_counter()
+    r = subprocess.run([exe, "--model", model, "--output", out, "--gpus", str(gpus)], capture_output=True, text=True)
+    el = time.perf_counter() - t0
+    assert r.returncode == 0, r.stderr[-2000:]
+    res = {"workload": f"tb-prune real mode, {layers} 7B-class decoder layers in BF16 ({params:,} params, "
+                       f"{size / 1e9:.2f} GB file, page-cache resident), OneShot EHAP + CORING 2:4, {gpus} GPU(s)",
+           "seconds": round(el, 2), "gparams_per_s": round(params / el / 1e9, 3),
+           "input_gb_per_s": round(size / el / 1e9, 2),
+           "output_gb": round(sum(os.path.getsize(os.path.join(out, f)) for f in os.listdir(out)) / 1e9, 2)}
+    ref = os.path.join(ROOT, "oracle", "_ref", "tb-prune")
+    if compare and os.path.exists(ref):
+        rout = os.path.join(workdir, "ref")
+        t0 = time.perf_counter()
+        rr = subprocess.run([ref, "--model", model, "--output", rout], capture_output=True, text=True)
+        rel = time.perf_counter() - t0
+        assert rr.returncode == 0, rr.stderr[-2000:]
+        names = sorted(os.listdir(rout))
+        same = names == sorted(os.listdir(out)) and all(
+            open(os.path.join(out, f), "rb").read() == open(os.path.join(rout, f), "rb").read() for f in names)
+        res["reference_cli"] = {"seconds": round(rel, 2), "gparams_per_s": round(params / rel / 1e9, 4),
+                                "kind": "reference", "cores": 1, "files": len(names),
+                                "all_files_byte_identical": bool(same)}
+    return res
 
 
 # ---------------------------------------------------------------------------
