@@ -980,11 +980,23 @@ def run_tb_prune_real(torch, layers, gpus, workdir, compare=True):
     r = subprocess.run([exe, "--model", model, "--output", out, "--gpus", str(gpus)], capture_output=True, text=True)
     el = time.perf_counter() - t0
     assert r.returncode == 0, r.stderr[-2000:]
+    # the same box's buffered sequential write rate over as many bytes as the run writes
+    out_bytes = sum(os.path.getsize(os.path.join(out, f)) for f in os.listdir(out))
+    probe = os.path.join(workdir, "write_probe.bin")
+    chunk = np.zeros(64 << 20, np.uint8)
+    t0 = time.perf_counter()
+    with open(probe, "wb") as f:
+        for _ in range(max(1, out_bytes // chunk.size)):
+            f.write(chunk)
+    wr = (max(1, out_bytes // chunk.size) * chunk.size) / (time.perf_counter() - t0) / 1e9
+    os.remove(probe)
     res = {"workload": f"tb-prune real mode, {layers} 7B-class decoder layers in BF16 ({params:,} params, "
                        f"{size / 1e9:.2f} GB file, page-cache resident), OneShot EHAP + CORING 2:4, {gpus} GPU(s)",
            "seconds": round(el, 2), "gparams_per_s": round(params / el / 1e9, 3),
            "input_gb_per_s": round(size / el / 1e9, 2),
-           "output_gb": round(sum(os.path.getsize(os.path.join(out, f)) for f in os.listdir(out)) / 1e9, 2)}
+           "output_gb": round(out_bytes / 1e9, 2), "output_gb_per_s": round(out_bytes / el / 1e9, 3),
+           "buffered_write_probe_gb_per_s": round(wr, 3),
+           "bound": "the .tb and model.tbm writes (output_gb_per_s against the same box's buffered write rate)"}
     ref = os.path.join(ROOT, "oracle", "_ref", "tb-prune")
     if compare and os.path.exists(ref):
         rout = os.path.join(workdir, "ref")
