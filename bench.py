@@ -880,7 +880,7 @@ def run_tb_prune_mode(torch, tb, ranks, steps, warmup):
     apply, importance again, CORING top-N 2:4 with proportional
     redistribution, mask regenerated) over one 7B-class decoder layer's seven
     matrices, FP32 as the CLI widens them.  Fused: tb_prune_one_shot_nm, two
-    passes around three radix digit passes over the scores (16 + 12 + 12.25
+    passes around three radix digit passes over the scores (16 + 12 + 16.25
     B/param).  Staged: the same calls one by one through the stage entry
     points, as the pruner objects issue them (about 83 B/param, with host
     synchronisations for the select and the pruned counts)."""
@@ -936,7 +936,7 @@ def run_tb_prune_mode(torch, tb, ranks, steps, warmup):
         outs[name] = (ms, [(x[3].clone(), x[6].clone()) for x in mats])
         out[name] = {"ms_per_step": round(ms, 3),
                      "value": round(out["params_per_step"] / (ms / 1e3) / 1e9, 3), "unit": "Gparams/s"}
-    bpp = 16 + 12 + 12.25
+    bpp = 16 + 12 + 16.25  # pass 1: w, g in, F, s out; digits: 3 x s; pass 2: w, F in, W', mask, s out
     hbm, _, kind = peaks()
     ach = out["params_per_step"] * bpp / (outs["fused"][0] / 1e3) / 1e9
     out["fused"]["roofline"] = {"bound": "hbm", "algorithmic_bytes_per_param": bpp, "achieved": round(ach, 1),

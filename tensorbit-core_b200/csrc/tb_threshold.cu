@@ -47,9 +47,17 @@ __global__ void __launch_bounds__(kThreads) radix_hist_kernel(const float* __res
     const size_t n4 = N / 4;
     const float4* s4 = reinterpret_cast<const float4*>(s);
     const size_t stride = (size_t)gridDim.x * kThreads;
+    // Scores cluster in a few top-digit bins, so lanes of a warp often hit the
+    // same bin: the lanes that share a bin add their count with one atomic.
     auto add = [&](float f) {
         const uint32_t k = order_key(f);
-        if (hi >= 32 || (k >> hi) == prefix) atomicAdd(&sh[(k >> shift) & dmask], 1u);
+        const bool in = hi >= 32 || (k >> hi) == prefix;
+        const unsigned active = __activemask();
+        const unsigned voters = __ballot_sync(active, in);
+        if (!in) return;
+        const uint32_t bin = (k >> shift) & dmask;
+        const unsigned peers = __match_any_sync(voters, bin);
+        if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&sh[bin], static_cast<unsigned>(__popc(peers)));
     };
     if ((reinterpret_cast<uintptr_t>(s) & 15u) == 0) {
         for (size_t i = blockIdx.x * (size_t)kThreads + threadIdx.x; i < n4; i += stride) {
