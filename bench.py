@@ -351,7 +351,7 @@ def time_plan(torch, tb, ranks, plan, steps, warmup, clocks=None):
     return {"per_rank": per, "clocks": clk, "steps": steps}
 
 
-def summarize(wl, timing, world, hbm, replicas=False):
+def summarize(wl, timing, hbm):
     per = timing["per_rank"]
     steps = timing["steps"]
     elapsed = max(r[0] for r in per)
@@ -539,7 +539,7 @@ def run_workload(torch, tb, ranks, wl, steps, warmup, args, hbm, sets=None, patt
             tb.check(tb.lib().tb_prepare_nm(n, m))
         plan = shard_plan(tb, w, sets, ranks, replicas=args.replicas)
         timing = time_plan(torch, tb, ranks, plan, steps, warmup, clocks)
-        res = summarize(w, timing, ranks.world, hbm, args.replicas)
+        res = summarize(w, timing, hbm)
         res["clocks"] = timing["clocks"]
         if not args.no_ties:
             res["near_tie_groups"] = count_near_ties(torch, tb, ranks, plan)
@@ -644,7 +644,7 @@ def run_ours(args):
     # ---- sample-split Fisher with the exchange (N > 1) ----------------------
     split = None
     if ranks.world > 1 and not args.no_split and not args.replicas:
-        split = run_sample_split(torch, tb, ranks, W7B, sets, args.split_steps, hbm)
+        split = run_sample_split(torch, tb, ranks, W7B, sets, args.split_steps)
     del sets, plan, out
     torch.cuda.empty_cache()
 
@@ -702,7 +702,7 @@ def run_ours(args):
 # ---------------------------------------------------------------------------
 # sample split: calibration samples split across ranks, one exchange per tensor
 # ---------------------------------------------------------------------------
-def run_sample_split(torch, tb, ranks, wl, sets, steps, hbm):
+def run_sample_split(torch, tb, ranks, wl, sets, steps):
     """Each rank holds samples [s0, s1) of every tensor of the headline pass.
     Per tensor: the rank's partial Fisher sum_t c_t g_t^2 over its samples
     (tb_fisher_weighted_sum, the EMA regrouped), then the exchange and the
