@@ -47,17 +47,12 @@ __global__ void __launch_bounds__(kThreads) radix_hist_kernel(const float* __res
     const size_t n4 = N / 4;
     const float4* s4 = reinterpret_cast<const float4*>(s);
     const size_t stride = (size_t)gridDim.x * kThreads;
-    // Scores cluster in a few top-digit bins, so lanes of a warp often hit the
-    // same bin: the lanes that share a bin add their count with one atomic.
+    // One shared-memory atomic per element.  (Aggregating the lanes of a warp
+    // that share a bin with __match_any_sync measured slower on B200: 3.67
+    // against 2.63 ms for tb-prune's sequence over a 7B-class layer.)
     auto add = [&](float f) {
         const uint32_t k = order_key(f);
-        const bool in = hi >= 32 || (k >> hi) == prefix;
-        const unsigned active = __activemask();
-        const unsigned voters = __ballot_sync(active, in);
-        if (!in) return;
-        const uint32_t bin = (k >> shift) & dmask;
-        const unsigned peers = __match_any_sync(voters, bin);
-        if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&sh[bin], static_cast<unsigned>(__popc(peers)));
+        if (hi >= 32 || (k >> hi) == prefix) atomicAdd(&sh[(k >> shift) & dmask], 1u);
     };
     if ((reinterpret_cast<uintptr_t>(s) & 15u) == 0) {
         for (size_t i = blockIdx.x * (size_t)kThreads + threadIdx.x; i < n4; i += stride) {
