@@ -186,7 +186,7 @@ class Ranks:
 
 
 class Clocks:
-    """nvidia-smi samples (200 ms) of this rank's GPU while a timed region runs."""
+    """nvidia-smi samples (100 ms) of this rank's GPU while a timed region runs."""
     FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -201,7 +201,7 @@ class Clocks:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -235,7 +235,8 @@ class Clocks:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "power_w_max": max(power),
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "samples": len(sm), "reasons": sorted(reasons),
+                "window": "nvidia-smi every 100 ms over the warm-up (at least 1 s) and the timed steps"}
 
 
 def peaks():
@@ -326,15 +327,21 @@ def time_plan(torch, tb, ranks, plan, steps, warmup, clocks=None):
             if events is not None:
                 events[i][1].record(stream)
 
-    for _ in range(warmup):
+    # The clock sampler starts before the warm-up, which runs at least a
+    # second (extra untimed steps if needed), so that it has samples under this
+    # load even when the timed steps take only a fraction of a second.
+    if clocks:
+        clocks.start()
+    t_load = time.perf_counter()
+    done = 0
+    while done < warmup or (clocks and time.perf_counter() - t_load < 1.0):
         step()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        done += 1
     events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in plan]
               for _ in range(steps)]
     ranks.barrier()
     torch.cuda.synchronize()
-    if clocks:
-        clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for k in range(steps):
@@ -714,7 +721,9 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
             range from peer memory over NVLink inside the pass;
       push: tb_fisher_partial_scatter computes the partial and stores each
             owner's range into the owner's memory (NVLink writes), then the
-            barrier, then tb_score_mask_pack_peer over the P local slots.
+            barrier, then tb_score_mask_pack_peer over the P local slots;
+      copy: the partial written locally, each owner's range copied to it by
+            the copy engines, then the barrier and the same local sum.
     Each variant is timed over whole 7B passes; its masks are compared with the
     exact (serial-recurrence) pass on this rank's ranges."""
     import tbdist as td
@@ -804,9 +813,34 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
             tb.check(L.tb_score_mask_pack_peer(C.byref(fused_args(T, e0, e1, count)),
                                                C.cast(parts[k], C.POINTER(C.c_void_p)), W, sptr))
 
+    scratch = torch.empty(nmax, dtype=torch.float32, device=dev)
+
+    def tensor_copy(T, ev, count):
+        e0, e1 = rng[id(T)]
+        k = counter[0] & 1
+        counter[0] += 1
+        starts, _, _ = scatter[id(T)]
+        base = scratch.data_ptr()
+        local = (C.c_void_p * W)(*[base + 4 * starts[r] for r in range(W)])
+        tb.check(L.tb_fisher_partial_scatter(T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n, T.n,
+                                             c.ctypes.data, W, starts, C.cast(local, C.POINTER(C.c_void_p)), sptr))
+        slot = td.push_slot(T.n, m, W)
+        for r in range(W):
+            if r != ranks.rank and starts[r + 1] > starts[r]:
+                tb.check(L.tb_memcpy_d2d(bufs.ptrs[k][r] + 4 * ranks.rank * slot, base + 4 * starts[r],
+                                         4 * (starts[r + 1] - starts[r]), sptr))
+        ev and ev[1].record()
+        dist.all_reduce(flag)
+        ev and ev[2].record()
+        if e1 > e0:
+            parts = (C.c_void_p * W)(*[(base + 4 * e0) if q == ranks.rank else (bufs.local[k] + 4 * q * slot)
+                                       for q in range(W)])
+            tb.check(L.tb_score_mask_pack_peer(C.byref(fused_args(T, e0, e1, count)),
+                                               C.cast(parts, C.POINTER(C.c_void_p)), W, sptr))
+
     out = {"workload": "the headline 7B pass with each tensor's 64 samples split evenly over the ranks",
            "samples_per_rank": s1 - s0}
-    for variant, fn in (("nccl", tensor_nccl), ("peer", tensor_peer), ("push", tensor_push)):
+    for variant, fn in (("nccl", tensor_nccl), ("peer", tensor_peer), ("push", tensor_push), ("copy", tensor_copy)):
         def one_pass(evs=None, count=False):
             for i, T in enumerate(items):
                 ev = evs[i] if evs else None
@@ -859,6 +893,12 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
                              "score/mask/pack)")
             r["nvlink_read_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
             r["fused_pass_gbs_rank0"] = round(ex_bytes / (tot[0][3] / steps / 1e3) / 1e9, 1)
+        elif variant == "copy":
+            r["exchange"] = ("the partial-Fisher kernel writes the rank's partial locally; each other owner's range "
+                             "goes to its memory by one device-to-device copy (copy engines over NVLink, in the "
+                             "'partial_fisher' phase); a one-element NCCL all-reduce per tensor orders it; the pass "
+                             "sums the P slots of its range locally")
+            r["nvlink_write_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
         else:
             r["exchange"] = ("the partial-Fisher kernel (over the rank's samples) stores each owner's "
                              "range into that owner's memory (NVLink writes inside the pass); a one-element NCCL "

@@ -17,9 +17,11 @@ docs prune shards in separate processes, docs/CLOUD.md:155-170):
   replace the all-reduce by a reduce-scatter over peer memory, half the NVLink
   bytes of an all-reduce and no reduction kernel: `prune_sample_split_peer`
   reads the other ranks' partials of its range inside the pass;
-  `prune_sample_split_push` (the fast one) has each rank's partial kernel
-  store every owner's range straight into that owner's memory, so the pass
-  reads all partials locally.  F matches the
+  `prune_sample_split_push` has each rank's partial kernel store every
+  owner's range straight into that owner's memory, and
+  `prune_sample_split_copy` moves the owners' ranges of a locally written
+  partial with device-to-device copies (the copy engines), so the pass reads
+  all partials locally.  F matches the
   serial recurrence to FP32 rounding (the association differs), so masks can
   differ only in near-tie groups, which the pass counts.
 
@@ -332,6 +334,54 @@ def prune_sample_split_push(dist, torch, bufs: PeerBuffers, k: int, w_dev, w_dty
     e0, e1 = ranges[rank]
     if e1 > e0:
         parts = (C.c_void_p * world)(*[bufs.local[k] + 4 * q * slot for q in range(world)])
+        wsz = w_dev.element_size()
+        a = tb.prune_args(weights=w_dev.data_ptr() + e0 * wsz, w_dtype=w_dtype, grads=None, g_dtype=g_dtype, S=0,
+                          N=e1 - e0, fisher_steps_in=S_total, alpha=alpha, beta=beta, n=n, m=m,
+                          w_out=out_w.data_ptr() + 4 * e0, mask_out=out_mask.data_ptr() + e0 // m,
+                          fisher_out=(fisher_out.data_ptr() + 4 * e0) if fisher_out is not None else None,
+                          near_ties=near_ties.data_ptr() if near_ties is not None else None, **cfg)
+        _check(L.tb_score_mask_pack_peer(C.byref(a), C.cast(parts, C.POINTER(C.c_void_p)), world, stream))
+    return {"e0": e0, "e1": e1}
+
+
+def prune_sample_split_copy(dist, torch, bufs: PeerBuffers, k: int, scratch, w_dev, w_dtype: int, g_local_dev,
+                            g_dtype: int, S_total: int, s0: int, out_w, out_mask, *, n=2, m=4, alpha=0.01,
+                            beta=0.99, flag=None, fisher_out=None, near_ties=None, **cfg) -> dict:
+    """Sample-split pass of one tensor with the exchange on the copy engines:
+    this rank's partial Fisher over its samples is written to its own
+    `scratch` (a device tensor of at least N floats; tb_fisher_partial_scatter
+    with every range local), each other owner's range then goes to that
+    owner's exchange buffer k by one device-to-device copy over NVLink (DMA,
+    no SM time), a one-element all-reduce orders the ranks, and the owner's
+    fused pass sums its own partial and the P - 1 received slots from local
+    memory (tb_score_mask_pack_peer).  Same bits as the other sample-split
+    passes (same partials, summed in rank order).  Buffers alternate per
+    tensor; `scratch` is rewritten by the next tensor only after this rank's
+    copies and its own pass, which precede it on the stream."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    N = w_dev.numel()
+    S_local = g_local_dev.shape[0] if g_local_dev is not None else 0
+    stream = torch.cuda.current_stream().cuda_stream
+    L = tb.lib()
+    slot = push_slot(N, m, world)
+    ranges = [group_shard(N, m, world, r) for r in range(world)]
+    starts = (C.c_uint64 * (world + 1))(*([e0 for e0, _ in ranges] + [N]))
+    base = scratch.data_ptr()
+    local = (C.c_void_p * world)(*[base + 4 * e0 for e0, _ in ranges])
+    c = ema_weights(S_total, alpha, beta)[s0:s0 + S_local].copy()
+    _check(L.tb_fisher_partial_scatter(g_local_dev.data_ptr() if S_local else None, g_dtype, S_local, N, N,
+                                       c.ctypes.data if S_local else None, world, starts,
+                                       C.cast(local, C.POINTER(C.c_void_p)), stream))
+    for r, (e0, e1) in enumerate(ranges):
+        if r != rank and e1 > e0:
+            _check(L.tb_memcpy_d2d(bufs.ptrs[k][r] + 4 * rank * slot, base + 4 * e0, 4 * (e1 - e0), stream))
+    if flag is None:
+        flag = torch.zeros(1, dtype=torch.float32, device=w_dev.device)
+    dist.all_reduce(flag)
+    e0, e1 = ranges[rank]
+    if e1 > e0:
+        parts = (C.c_void_p * world)(*[(base + 4 * e0) if q == rank else (bufs.local[k] + 4 * q * slot)
+                                       for q in range(world)])
         wsz = w_dev.element_size()
         a = tb.prune_args(weights=w_dev.data_ptr() + e0 * wsz, w_dtype=w_dtype, grads=None, g_dtype=g_dtype, S=0,
                           N=e1 - e0, fisher_steps_in=S_total, alpha=alpha, beta=beta, n=n, m=m,

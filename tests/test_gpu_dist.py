@@ -91,6 +91,16 @@ def _worker(rank, world, port_no, tmpdir):
     np.save(os.path.join(tmpdir, f"pu_w{rank}.npy"), qw[e0:e1].cpu().numpy())
     np.save(os.path.join(tmpdir, f"pu_m{rank}.npy"), qm[e0 // 4:e1 // 4].cpu().numpy())
     np.save(os.path.join(tmpdir, f"pu_F{rank}.npy"), qF[e0:e1].cpu().numpy())
+    # and with the owners' ranges moved by the copy engines
+    scratch = torch.empty(N, dtype=torch.float32, device="cuda")
+    cw, cm, cF = torch.zeros_like(qw), torch.zeros_like(qm), torch.zeros_like(qF)
+    for k in (0, 1, 0):
+        td.prune_sample_split_copy(dist, torch, bufs, k, scratch, wd, tb.BF16, gd, tb.BF16, S, s0, cw, cm,
+                                   strategy="optimal", redist="proportional", mode="obd", fisher_out=cF)
+    torch.cuda.synchronize()
+    np.save(os.path.join(tmpdir, f"cp_w{rank}.npy"), cw[e0:e1].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"cp_m{rank}.npy"), cm[e0 // 4:e1 // 4].cpu().numpy())
+    np.save(os.path.join(tmpdir, f"cp_F{rank}.npy"), cF[e0:e1].cpu().numpy())
     bufs.close()
     dist.barrier(device_ids=[rank])
     dist.destroy_process_group()
@@ -139,9 +149,10 @@ def test_two_rank_group_shard_and_sample_split(cuda, tblib, port, tmp_path):
     samep = np.repeat(mp_ == mo, 4)
     assert np.array_equal(wpp[samep], wo[samep])
     # push variant: the same partials (same arithmetic), so the same bits as the peer-read variant
-    for key, ref_ in (("F", Fp), ("m", mp_), ("w", wpp)):
-        got = np.concatenate([np.load(tmp_path / f"pu_{key}{r}.npy") for r in range(world)])
-        assert got.tobytes() == ref_.tobytes(), f"push variant {key} differs from the peer-read variant"
+    for variant in ("pu", "cp"):  # push (SM stores) and copy (copy engines)
+        for key, ref_ in (("F", Fp), ("m", mp_), ("w", wpp)):
+            got = np.concatenate([np.load(tmp_path / f"{variant}_{key}{r}.npy") for r in range(world)])
+            assert got.tobytes() == ref_.tobytes(), f"{variant} variant {key} differs from the peer-read variant"
 
 
 def _obs_worker(rank, world, port_no, tmpdir):
