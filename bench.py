@@ -805,7 +805,7 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
         starts, dests, parts = scatter[id(T)]
         tb.check(L.tb_fisher_partial_scatter(T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n, T.n,
                                              c.ctypes.data, W, starts, C.cast(dests[k], C.POINTER(C.c_void_p)),
-                                             sptr))
+                                             (ranks.rank + 1) % W, sptr))
         ev and ev[1].record()
         dist.all_reduce(flag)
         ev and ev[2].record()
@@ -823,10 +823,12 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
         base = scratch.data_ptr()
         local = (C.c_void_p * W)(*[base + 4 * starts[r] for r in range(W)])
         tb.check(L.tb_fisher_partial_scatter(T.g.data_ptr() + 2 * T.n * s0, tb.BF16, s1 - s0, T.n, T.n,
-                                             c.ctypes.data, W, starts, C.cast(local, C.POINTER(C.c_void_p)), sptr))
+                                             c.ctypes.data, W, starts, C.cast(local, C.POINTER(C.c_void_p)),
+                                             ranks.rank, sptr))
         slot = td.push_slot(T.n, m, W)
-        for r in range(W):
-            if r != ranks.rank and starts[r + 1] > starts[r]:
+        for j in range(1, W):  # rank + 1 first: each peer receives from one sender at a time
+            r = (ranks.rank + j) % W
+            if starts[r + 1] > starts[r]:
                 tb.check(L.tb_memcpy_d2d(bufs.ptrs[k][r] + 4 * ranks.rank * slot, base + 4 * starts[r],
                                          4 * (starts[r + 1] - starts[r]), sptr))
         ev and ev[1].record()

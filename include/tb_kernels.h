@@ -315,7 +315,10 @@ int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* thres
  * ranks r = 0..n_ranks-1 own [starts[r], starts[r+1]) (host array of
  * n_ranks + 1 offsets from 0 to N, inner ones multiples of 8) and element
  * starts[r] lands at dest[r][0] (host array of device pointers: a peer's
- * buffer mapped with tb_ipc_open, or this device's own).  The stores to other
+ * buffer mapped with tb_ipc_open, or this device's own).  The pass visits the
+ * elements starting with owner start_owner's range (cyclically): ranks that
+ * start at different owners (e.g. rank + 1) spread their remote stores over
+ * the peers instead of all writing to one peer at a time.  The stores to other
  * GPUs travel over NVLink inside the pass, so the exchange of an all-reduce
  * becomes writes of (P-1)/P of the partial, and each owner then reads the P
  * partials of its range from its own memory (tb_score_mask_pack_peer with
@@ -323,7 +326,7 @@ int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* thres
  * collectives; docs/CLOUD.md:155-169).  S <= 128 per call (TB_ERR_CAPACITY). */
 int tb_fisher_partial_scatter(const void* gradients, int g_dtype, size_t S, size_t g_stride, size_t N,
                               const float* weights, int n_ranks, const uint64_t* starts, float* const* dest,
-                              void* stream);
+                              int start_owner, void* stream);
 
 /* Sample-split pass: the reduction of the ranks' partial Fisher sums fused
  * into the score -> mask -> pack pass (a reduce-scatter over peer memory).

@@ -291,6 +291,7 @@ struct PartialSpec {
     int nranks;
     size_t start[kMaxScatterRanks + 1];    // owner r holds elements [start[r], start[r + 1])
     float* dest[kMaxScatterRanks];         // element start[r] of this partial lands at dest[r][0]
+    size_t rot;                            // vector chunks are visited from chunk `rot` on, cyclically
 };
 
 __device__ __forceinline__ int owner_of(const PartialSpec& q, size_t e) {
@@ -325,7 +326,10 @@ __global__ void __launch_bounds__(kThreads, 3) partial_vec_kernel(const PartialS
     constexpr int U = (GW == 2) ? 4 : 2;
     const size_t nchunks = q.N / kEpt;
     const size_t gstride_b = q.gstride * Dtype<GDT>::kBytes;
-    for (size_t c = blockIdx.x * (size_t)kThreads + threadIdx.x; c < nchunks; c += (size_t)gridDim.x * kThreads) {
+    for (size_t i = blockIdx.x * (size_t)kThreads + threadIdx.x; i < nchunks; i += (size_t)gridDim.x * kThreads) {
+        // Ranks start at different owners' ranges, so that their remote
+        // stores do not all converge on one peer's links at a time.
+        const size_t c = i + q.rot < nchunks ? i + q.rot : i + q.rot - nchunks;
         const size_t e0 = c * kEpt;
         float acc[kEpt];
 #pragma unroll
@@ -691,7 +695,7 @@ extern "C" {
 
 int tb_fisher_partial_scatter(const void* gradients, int g_dtype, size_t S, size_t g_stride, size_t N,
                               const float* weights, int n_ranks, const uint64_t* starts, float* const* dest,
-                              void* stream) {
+                              int start_owner, void* stream) {
     if (N == 0) return TB_OK;
     if (n_ranks < 1 || n_ranks > kMaxScatterRanks)
         return fail(TB_ERR_ARG, "tb_fisher_partial_scatter: %d ranks (1..%d)", n_ranks, kMaxScatterRanks);
@@ -724,11 +728,14 @@ int tb_fisher_partial_scatter(const void* gradients, int g_dtype, size_t S, size
         q.dest[r] = dest[r];
         aligned = aligned && aligned16(dest[r]);
     }
+    if (start_owner < 0 || start_owner >= n_ranks)
+        return fail(TB_ERR_ARG, "tb_fisher_partial_scatter: start_owner %d outside 0..%d", start_owner, n_ranks - 1);
     int rc = require_device(nullptr);
     if (rc) return rc;
     auto st = static_cast<cudaStream_t>(stream);
     const bool vec = S > 0 && aligned && aligned16(gradients) && (stride * dtype_bytes(g_dtype)) % 16 == 0;
     const size_t nvec = vec ? N / kEpt * kEpt : 0;
+    q.rot = nvec ? std::min(starts[start_owner] / kEpt, nvec / kEpt - 1) : 0;
     if (nvec) {
         const unsigned grid = grid_for(nvec / kEpt);
         if (g_dtype == TB_BF16) partial_vec_kernel<TB_BF16><<<grid, kThreads, 0, st>>>(q);

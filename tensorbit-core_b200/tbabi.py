@@ -130,8 +130,8 @@ def lib() -> C.CDLL:
             "tb_obs_hessian_scaled": ([vp, i32, i32, f32, vp, vp], i32),
             "tb_obs_sparsegpt": ([vp, i32, i32, vp, f32, i32, i32, vp, vp, vp], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
-            "tb_fisher_partial_scatter": ([vp, i32, sz, sz, sz, vp, i32, C.POINTER(C.c_uint64), C.POINTER(vp), vp],
-                                          i32),
+            "tb_fisher_partial_scatter": ([vp, i32, sz, sz, sz, vp, i32, C.POINTER(C.c_uint64), C.POINTER(vp), i32,
+                                           vp], i32),
             "tb_prune_one_shot_nm": ([C.POINTER(PruneArgs), f32, C.POINTER(C.c_float), C.POINTER(C.c_uint64),
                                       C.POINTER(C.c_uint64), vp], i32),
             "tb_score_mask_pack_peer": ([C.POINTER(PruneArgs), C.POINTER(vp), i32, vp], i32),

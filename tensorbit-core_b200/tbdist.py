@@ -327,7 +327,7 @@ def prune_sample_split_push(dist, torch, bufs: PeerBuffers, k: int, w_dev, w_dty
     c = ema_weights(S_total, alpha, beta)[s0:s0 + S_local].copy()
     _check(L.tb_fisher_partial_scatter(g_local_dev.data_ptr() if S_local else None, g_dtype, S_local, N, N,
                                        c.ctypes.data if S_local else None, world, starts,
-                                       C.cast(dest, C.POINTER(C.c_void_p)), stream))
+                                       C.cast(dest, C.POINTER(C.c_void_p)), (rank + 1) % world, stream))
     if flag is None:
         flag = torch.zeros(1, dtype=torch.float32, device=w_dev.device)
     dist.all_reduce(flag)
@@ -371,9 +371,11 @@ def prune_sample_split_copy(dist, torch, bufs: PeerBuffers, k: int, scratch, w_d
     c = ema_weights(S_total, alpha, beta)[s0:s0 + S_local].copy()
     _check(L.tb_fisher_partial_scatter(g_local_dev.data_ptr() if S_local else None, g_dtype, S_local, N, N,
                                        c.ctypes.data if S_local else None, world, starts,
-                                       C.cast(local, C.POINTER(C.c_void_p)), stream))
-    for r, (e0, e1) in enumerate(ranges):
-        if r != rank and e1 > e0:
+                                       C.cast(local, C.POINTER(C.c_void_p)), rank, stream))
+    for j in range(1, world):  # rank + 1 first: each peer receives from one sender at a time
+        r = (rank + j) % world
+        e0, e1 = ranges[r]
+        if e1 > e0:
             _check(L.tb_memcpy_d2d(bufs.ptrs[k][r] + 4 * rank * slot, base + 4 * e0, 4 * (e1 - e0), stream))
     if flag is None:
         flag = torch.zeros(1, dtype=torch.float32, device=w_dev.device)

@@ -97,7 +97,7 @@ def test_partial_scatter_equals_weighted_sum(cuda, tblib, gdt, P):
     starts = (C.c_uint64 * (P + 1))(*([a for a, _ in ranges] + [N]))
     dest = (C.c_void_p * P)(*[o.data_ptr() for o in owners])
     tblib.check(tblib.lib().tb_fisher_partial_scatter(gd.data_ptr(), code, S, N, N, c.ctypes.data, P, starts,
-                                                      C.cast(dest, C.POINTER(C.c_void_p)), None))
+                                                      C.cast(dest, C.POINTER(C.c_void_p)), (P - 1) // 2, None))
     torch.cuda.synchronize()
     for (e0, e1), o in zip(ranges, owners):
         assert torch.equal(o[:e1 - e0].view(torch.int32), ref[e0:e1].view(torch.int32))
