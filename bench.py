@@ -1212,7 +1212,7 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1683.6):
     mask = torch.empty(max(1, (r1 - r0) * D // 4), dtype=torch.uint8, device=dev)
     L = tb.lib()
     sptr = torch.cuda.current_stream().cuda_stream
-    ms = []
+    ms, phases = [], []
     for k in range(steps + 1):  # the first pass warms up (workspace, module load)
         W.copy_(W0)
         if world > 1:
@@ -1230,6 +1230,9 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1683.6):
         torch.cuda.synchronize()
         if k:
             ms.append(e0.elapsed_time(e1))
+            ph = (C.c_float * 4)()
+            tb.check(L.tb_obs_sparsegpt_phase_times(ph, 4))
+            phases.append(list(ph))
     pop = sum(((mask >> b) & 1).int() for b in range(4))
     assert r1 == r0 or bool((pop == 2).all()), "OBS mask is not 2:4"
     t = torch.tensor([sum(ms) / len(ms)], dtype=torch.float64, device=dev)
@@ -1242,6 +1245,8 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1683.6):
     return {"workload": f"column-block exact OBS: {R}x{D} down_proj (BF16 -> FP32), X {NT}x{D} BF16 N(0,1) with 1% "
                         "columns x20, damp 0.01 mean(diag), 128-column blocks, 2:4",
             "ms_per_pass": round(t, 2), "passes": steps, "flops_per_pass": f, "tflops": round(tflops, 1),
+            "chain_phase_ms_rank0": {name: round(statistics.median(p[i] for p in phases), 2) for i, name in
+                                     enumerate(["h_prep", "factorisation", "sweep", "total"])},
             "unit": "TFLOP/s", "flop_count": "algorithmic for this route: d(d+1)n + 2d^3/3 + r d^2 (bench.obs_flops)",
             "sparsegpt_flops_per_pass": fs,
             "tflops_sparsegpt_equivalent": round(fs / (t / 1e3) / 1e12, 1),

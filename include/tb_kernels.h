@@ -245,6 +245,12 @@ int tb_obs_hessian_scaled(const void* xt_bf16, int d, int n, float scale, float*
  * TB_ERR_TIMEOUT if an internal bounded wait expired. */
 int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float damp_frac, int n_keep, int m,
                      uint8_t* mask, float* ut_out, void* stream);
+/* Diagnostics, no reference counterpart: phase times (milliseconds, CUDA
+ * events on the internal chain stream) of this host thread's last successful
+ * tb_obs_sparsegpt call: [0] damping and the reversed copy of H, [1] the
+ * factorisation (its chain of dependent steps), [2] the column sweep up to
+ * its last in-block step, [3] all three.  Writes min(n, 4) values. */
+int tb_obs_sparsegpt_phase_times(float* ms_out, int n);
 
 /* ---- fused score -> mask -> pack pass ------------------------------------ */
 /* One pass over a tensor: Fisher EMA over S gradient samples, importance,

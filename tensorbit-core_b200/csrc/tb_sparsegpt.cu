@@ -914,9 +914,12 @@ struct Workspace {
     cudaEvent_t ev = nullptr, join = nullptr, evl = nullptr, join_ahead = nullptr, fork = nullptr, done = nullptr;
     cudaEvent_t wcopy = nullptr;
     cudaEvent_t ev21[kMaxDepth] = {}, ev22[kMaxDepth] = {}, evv[kMaxDepth] = {};
+    cudaEvent_t phase[4] = {};  // timing events on the chain stream: start, H ready, factored, swept
 };
 std::mutex g_ws_mu;
 std::vector<Workspace> g_ws;
+// Chain-stream phase times of this host thread's last successful call.
+thread_local float g_obs_phase_ms[4] = {0, 0, 0, 0};
 
 // Per-device workspace of at least `floats` floats, with the side stream and
 // events of the inverse steps (created once per device).
@@ -942,6 +945,8 @@ int workspace(size_t floats, Workspace* out) {
         cudaEvent_t* evs[] = {&x.ev, &x.join, &x.evl, &x.join_ahead, &x.fork, &x.done, &x.wcopy};
         for (cudaEvent_t* p : evs)
             if (e == cudaSuccess) e = cudaEventCreateWithFlags(p, cudaEventDisableTiming);
+        for (auto& p : x.phase)
+            if (e == cudaSuccess) e = cudaEventCreate(&p);
         for (int k = 0; k < kMaxDepth && e == cudaSuccess; ++k) {
             e = cudaEventCreateWithFlags(&x.ev21[k], cudaEventDisableTiming);
             if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x.ev22[k], cudaEventDisableTiming);
@@ -1024,6 +1029,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     pdl_fence(st);
     pdl_fence(wsp.ahead);
     pdl_fence(wsp.side);  // its first launch follows the previous call's last one
+    cudaEventRecord(wsp.phase[0], st);
     Work w{};
     w.d = d;
     w.side = wsp.side;
@@ -1072,7 +1078,9 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
         if (e == cudaSuccess) e = cudaEventRecord(wsp.wcopy, w.ahead);
         rc = e == cudaSuccess ? check_launch("reverse_columns_kernel") : cuda_fail(e, "reverse_columns launch");
     }
+    if (!rc) cudaEventRecord(wsp.phase[1], st);
     if (!rc) rc = chol(w, 0, d, st, 0, Pending{});
+    if (!rc) cudaEventRecord(wsp.phase[2], st);
     // The sweep starts as soon as the last 128-block is factored: it waits for
     // each node's last inverse step only where it reads that node's V21.
     if (!rc) rc = wait_on(st, wsp.wcopy);
@@ -1082,6 +1090,7 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
                          w.evv,
                          evv_waited},
                    0, d, st, 0, nullptr);
+    if (!rc) cudaEventRecord(wsp.phase[3], st);
     // join: the inverse steps (side) and look-ahead updates (ahead) finish
     // before anything reads V or the next call reuses the workspace (also on errors)
     e = cudaEventRecord(wsp.join, w.side);
@@ -1111,5 +1120,18 @@ extern "C" int tb_obs_sparsegpt(float* W, int r, int d, const float* H, float da
     }
     if (!rc && bad == 2) rc = fail(TB_ERR_TIMEOUT, "a wait inside the 128-block factorisation expired");
     if (!rc && bad == 1) rc = fail(TB_ERR_CONFIG, "H + lambda I is not positive definite in FP32 (a Cholesky pivot <= 0)");
+    if (!rc) {  // the call synchronised: the chain stream's phase events are complete
+        float* t = g_obs_phase_ms;
+        cudaEventElapsedTime(&t[0], wsp.phase[0], wsp.phase[1]);
+        cudaEventElapsedTime(&t[1], wsp.phase[1], wsp.phase[2]);
+        cudaEventElapsedTime(&t[2], wsp.phase[2], wsp.phase[3]);
+        cudaEventElapsedTime(&t[3], wsp.phase[0], wsp.phase[3]);
+    }
     return rc;
+}
+
+extern "C" int tb_obs_sparsegpt_phase_times(float* ms_out, int n) {
+    if (!ms_out || n < 1) return fail(TB_ERR_ARG, "tb_obs_sparsegpt_phase_times: null or empty output");
+    for (int i = 0; i < n && i < 4; ++i) ms_out[i] = g_obs_phase_ms[i];
+    return TB_OK;
 }

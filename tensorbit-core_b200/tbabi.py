@@ -129,6 +129,7 @@ def lib() -> C.CDLL:
             "tb_obs_hessian": ([vp, i32, i32, vp, vp], i32),
             "tb_obs_hessian_scaled": ([vp, i32, i32, f32, vp, vp], i32),
             "tb_obs_sparsegpt": ([vp, i32, i32, vp, f32, i32, i32, vp, vp, vp], i32),
+            "tb_obs_sparsegpt_phase_times": ([C.POINTER(C.c_float), i32], i32),
             "tb_score_mask_pack": ([C.POINTER(PruneArgs), vp], i32),
             "tb_fisher_partial_scatter": ([vp, i32, sz, sz, sz, vp, i32, C.POINTER(C.c_uint64), C.POINTER(vp), i32,
                                            vp], i32),
