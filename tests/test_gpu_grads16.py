@@ -101,3 +101,83 @@ def test_partial_scatter_equals_weighted_sum(cuda, tblib, gdt, P):
     torch.cuda.synchronize()
     for (e0, e1), o in zip(ranges, owners):
         assert torch.equal(o[:e1 - e0].view(torch.int32), ref[e0:e1].view(torch.int32))
+
+
+@pytest.mark.parametrize("P", [1, 3, 8])
+@pytest.mark.parametrize("n,m,strategy", [(2, 4, "optimal"), (2, 8, "iterative"), (1, 4, "topn")])
+def test_peer_pass_sums_partials_in_rank_order(cuda, tblib, P, n, m, strategy):
+    """tb_score_mask_pack_peer with P partials in this device's memory (as a
+    rank sees its own and the received slots): the Fisher state is exactly
+    ((p0 + p1) + ...) + p_{P-1} in FP32, and every output equals
+    tb_score_mask_pack given that sum as its Fisher state."""
+    torch = cuda
+    N = 40 * 4096 + 8 * m  # vector chunks and a tail for the scalar kernel
+    parts = [torch.from_numpy(np.abs(inputs.normal(N, 1e-6, 120 + k))).cuda() for k in range(P)]
+    w = torch.from_numpy(inputs.to_bf16_bits(inputs.normal(N, 0.02, 130)).view(np.int16)).cuda()
+    F = parts[0].clone()
+    for p in parts[1:]:
+        F = F + p
+    outs = []
+    for peer in (True, False):
+        wo = torch.full((N,), float("nan"), device="cuda")
+        mk = torch.full((N // m,), 0x33, dtype=torch.uint8, device="cuda")
+        fo = torch.full((N,), float("nan"), device="cuda")
+        so = torch.full((N,), float("nan"), device="cuda")
+        a = tblib.prune_args(weights=w.data_ptr(), w_dtype=tblib.BF16, grads=None, g_dtype=tblib.BF16, S=0, N=N,
+                             fisher_in=None if peer else F.data_ptr(), fisher_steps_in=64, n=n, m=m,
+                             strategy=strategy, mode="obs", redist="proportional", w_out=wo.data_ptr(),
+                             mask_out=mk.data_ptr(), fisher_out=fo.data_ptr(), scores_out=so.data_ptr())
+        if peer:
+            ptrs = (C.c_void_p * P)(*[p.data_ptr() for p in parts])
+            tblib.check(tblib.lib().tb_score_mask_pack_peer(C.byref(a), C.cast(ptrs, C.POINTER(C.c_void_p)), P,
+                                                             None))
+        else:
+            tblib.check(tblib.score_mask_pack(a, None))
+        torch.cuda.synchronize()
+        outs.append((wo, mk, fo, so))
+    (wp, mp, fp, sp), (ws, ms, fs, ss) = outs
+    assert torch.equal(fp.view(torch.int32), F.view(torch.int32))
+    assert torch.equal(fp.view(torch.int32), fs.view(torch.int32))
+    assert torch.equal(sp.view(torch.int32), ss.view(torch.int32))
+    assert torch.equal(wp.view(torch.int32), ws.view(torch.int32)) and torch.equal(mp, ms)
+
+
+def test_peer_pass_argument_checks(cuda, tblib):
+    torch = cuda
+    N = 4096
+    w = torch.zeros(N, device="cuda")
+    p0 = torch.zeros(N, device="cuda")
+    wo = torch.zeros(N, device="cuda")
+    mk = torch.zeros(N // 4, dtype=torch.uint8, device="cuda")
+    L = tblib.lib()
+
+    def call(P, **kw):
+        base = dict(weights=w.data_ptr(), w_dtype=tblib.F32, grads=None, g_dtype=tblib.F32, S=0, N=N,
+                    fisher_steps_in=8, w_out=wo.data_ptr(), mask_out=mk.data_ptr())
+        base.update(kw)
+        a = tblib.prune_args(**base)
+        ptrs = (C.c_void_p * max(P, 1))(*([p0.data_ptr()] * max(P, 1)))
+        return L.tb_score_mask_pack_peer(C.byref(a), C.cast(ptrs, C.POINTER(C.c_void_p)), P, None)
+
+    assert call(1) == tblib.TB_OK
+    assert call(0) == tblib.TB_ERR_ARG and call(9) == tblib.TB_ERR_ARG           # 1..8 partials
+    assert call(2, fisher_in=p0.data_ptr()) == tblib.TB_ERR_ARG                  # the partials are the state
+    assert call(2, fisher_steps_in=0) == tblib.TB_ERR_ARG                        # must count the samples
+    assert call(2, S=1, grads=p0.data_ptr()) == tblib.TB_ERR_ARG                 # no samples read here
+    # the producer side: ranges must cover [0, N), inner starts on multiples of 8, S <= 128
+    starts = (C.c_uint64 * 3)(0, 100, N)
+    dest = (C.c_void_p * 2)(p0.data_ptr(), p0.data_ptr())
+    cw = np.ones(4, np.float32)
+    g = torch.zeros(4, N, dtype=torch.bfloat16, device="cuda")
+    rc = L.tb_fisher_partial_scatter(g.data_ptr(), tblib.BF16, 4, N, N, cw.ctypes.data, 2, starts,
+                                     C.cast(dest, C.POINTER(C.c_void_p)), 0, None)
+    assert rc == tblib.TB_ERR_ARG
+    starts[1] = 96
+    rc = L.tb_fisher_partial_scatter(g.data_ptr(), tblib.BF16, 4, N, N, cw.ctypes.data, 2, starts,
+                                     C.cast(dest, C.POINTER(C.c_void_p)), 2, None)
+    assert rc == tblib.TB_ERR_ARG                                                 # start_owner outside 0..1
+    big = np.ones(129, np.float32)
+    rc = L.tb_fisher_partial_scatter(g.data_ptr(), tblib.BF16, 129, N, N, big.ctypes.data, 2, starts,
+                                     C.cast(dest, C.POINTER(C.c_void_p)), 0, None)
+    assert rc == tblib.TB_ERR_CAPACITY
+    torch.cuda.synchronize()
