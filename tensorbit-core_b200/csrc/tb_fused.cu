@@ -27,6 +27,19 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kEpt = 16;  // elements per thread in the vector kernel
+// Gradient samples of a 16-bit type whose loads a thread keeps in flight in
+// the vector kernel (two 16-byte loads each), and the CTAs per SM its register
+// budget is set for.  Measured on B200 against 4 and 3 (80 registers): 8 in
+// flight at 2 CTAs (94 registers) and 4 or 2 at 4 CTAs (64 registers, with
+// spills) were 2-11 % slower on the 7B pass and the 70B sweep.
+#ifndef TB_SAMPLES_IN_FLIGHT
+#define TB_SAMPLES_IN_FLIGHT 4
+#endif
+#ifndef TB_VEC_MIN_CTAS
+#define TB_VEC_MIN_CTAS (TB_SAMPLES_IN_FLIGHT > 4 ? 2 : 3)
+#endif
+constexpr int kU16 = TB_SAMPLES_IN_FLIGHT;
+constexpr int kVecMinCtas = TB_VEC_MIN_CTAS;
 constexpr int kMaxParts = 8;  // partial Fisher sums of a sample-split pass (ranks of one node)
 
 // Variants of the pass (template argument of the vector kernel, p.variant in
@@ -181,9 +194,9 @@ __device__ __forceinline__ uint64_t groups16(const FusedParams& p, const float (
 // one-shot keep rule s >= threshold zeroes weights before the importance that
 // CORING ranks is recomputed (tb_prune_one_shot_nm).
 template <int WDT, int GDT, int M, int VAR>
-__global__ void __launch_bounds__(kThreads, 3) fused_vec_kernel(const FusedParams p) {
+__global__ void __launch_bounds__(kThreads, kVecMinCtas) fused_vec_kernel(const FusedParams p) {
     constexpr int GW = Vec16<GDT>::kWords;
-    constexpr int U = (GW == 2) ? 4 : 2;  // samples in flight per thread
+    constexpr int U = (GW == 2) ? kU16 : 2;  // samples in flight per thread
     const uint64_t beta2 = pack2(p.beta, p.beta), c2 = pack2(p.contrib, p.contrib);
     const size_t nchunks = p.N / kEpt;
     const size_t gstride_b = p.gstride * Dtype<GDT>::kBytes;

@@ -16,7 +16,9 @@ import re
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
-LIB_PATH = os.path.join(PKG, "lib", "libtb_b200.so")
+# TB_LIB may name another build of the same library (e.g. one compiled with
+# different tuning constants); the in-tree build is the default.
+LIB_PATH = os.environ.get("TB_LIB") or os.path.join(PKG, "lib", "libtb_b200.so")
 HEADER = os.path.join(ROOT, "include", "tb_kernels.h")
 
 TB_OK, TB_ERR_SHAPE, TB_ERR_ZERO_SIZE, TB_ERR_CONFIG, TB_ERR_CUDA = 0, -1, -2, -3, -4
