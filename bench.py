@@ -840,19 +840,30 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
             tb.check(L.tb_score_mask_pack_peer(C.byref(fused_args(T, e0, e1, count)),
                                                C.cast(parts, C.POINTER(C.c_void_p)), W, sptr))
 
+    pipe_jobs = [(T.w, tb.BF16, T.g[s0:s1], tb.BF16, outs[id(T)], masks[id(T)]) for T in items]
+    pipe_cfg = dict(n=wl.n, damping=0.01, mode=wl.mode, strategy=wl.strategy, redist=wl.redist)
+
     out = {"workload": "the headline 7B pass with each tensor's 64 samples split evenly over the ranks",
            "samples_per_rank": s1 - s0}
-    for variant, fn in (("nccl", tensor_nccl), ("peer", tensor_peer), ("push", tensor_push), ("copy", tensor_copy)):
-        def one_pass(evs=None, count=False):
-            for i, T in enumerate(items):
-                ev = evs[i] if evs else None
-                ev and ev[0].record()
-                fn(T, ev, count)
-                ev and ev[3].record()
+    variants = (("nccl", tensor_nccl), ("peer", tensor_peer), ("push", tensor_push), ("copy", tensor_copy),
+                ("copy_overlap", None))
+    for variant, fn in variants:
+        if fn is None:
+            pipe = td.CopyExchangePipeline(dist, torch, nmax, m)
+
+            def one_pass(evs=None, count=False):
+                pipe.run(pipe_jobs, wl.S, s0, near_ties=ties if count else None, **pipe_cfg)
+        else:
+            def one_pass(evs=None, count=False):
+                for i, T in enumerate(items):
+                    ev = evs[i] if evs else None
+                    ev and ev[0].record()
+                    fn(T, ev, count)
+                    ev and ev[3].record()
 
         one_pass()  # warm-up
         torch.cuda.synchronize()
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in items]
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in items] if fn else None
         ph = [0.0, 0.0, 0.0]
         ranks.barrier()
         torch.cuda.synchronize()
@@ -864,7 +875,7 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
             t1.record()
             torch.cuda.synchronize()
             el += t0.elapsed_time(t1)
-            for ev in evs:
+            for ev in evs or ():
                 for k in range(3):
                     ph[k] += ev[k].elapsed_time(ev[k + 1])
         ranks.barrier()
@@ -881,7 +892,7 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
              "ms_per_step": round(elapsed / steps, 3), "steps": steps,
              "phase_ms_per_step_rank0": {"partial_fisher": round(tot[0][1] / steps, 3),
                                          "exchange": round(tot[0][2] / steps, 3),
-                                         "score_mask_pack": round(tot[0][3] / steps, 3)},
+                                         "score_mask_pack": round(tot[0][3] / steps, 3)} if fn else None,
              "near_tie_groups": int(sum(x[4] for x in tot)),
              "mask_bytes_differing_from_exact_pass": int(sum(x[5] for x in tot)),
              "mask_bytes_compared": sum(T.n // m for ts in sets for T in ts)}
@@ -895,6 +906,12 @@ def run_sample_split(torch, tb, ranks, wl, sets, steps):
                              "score/mask/pack)")
             r["nvlink_read_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
             r["fused_pass_gbs_rank0"] = round(ex_bytes / (tot[0][3] / steps / 1e3) / 1e9, 1)
+        elif variant == "copy_overlap":
+            r["exchange"] = ("as 'copy', pipelined over the tensors (tbdist.CopyExchangePipeline): the copies and "
+                             "the one-element all-reduce of tensor t run on a second stream while the partial of "
+                             "tensor t + 1 runs; three exchange buffers and two partial buffers rotate")
+            r["nvlink_write_bytes_per_step_per_rank"] = ex_bytes * (ranks.world - 1) // ranks.world
+            pipe.close()
         elif variant == "copy":
             r["exchange"] = ("the partial-Fisher kernel writes the rank's partial locally; each other owner's range "
                              "goes to its memory by one device-to-device copy (copy engines over NVLink, in the "

@@ -21,7 +21,8 @@ docs prune shards in separate processes, docs/CLOUD.md:155-170):
   owner's range straight into that owner's memory, and
   `prune_sample_split_copy` moves the owners' ranges of a locally written
   partial with device-to-device copies (the copy engines), so the pass reads
-  all partials locally.  F matches the
+  all partials locally; `CopyExchangePipeline` runs the copies of one tensor
+  on a second stream beside the next tensor's partial.  F matches the
   serial recurrence to FP32 rounding (the association differs), so masks can
   differ only in near-tie groups, which the pass counts.
 
@@ -392,6 +393,117 @@ def prune_sample_split_copy(dist, torch, bufs: PeerBuffers, k: int, scratch, w_d
                           near_ties=near_ties.data_ptr() if near_ties is not None else None, **cfg)
         _check(L.tb_score_mask_pack_peer(C.byref(a), C.cast(parts, C.POINTER(C.c_void_p)), world, stream))
     return {"e0": e0, "e1": e1}
+
+
+class CopyExchangePipeline:
+    """The copy-engine sample split over a sequence of tensors, with the
+    exchange of tensor t overlapped with the partial of tensor t + 1.
+
+    Tensors are numbered u = 0, 1, 2, ... over every run() of the pipeline.
+    Per tensor u: the partial (over this rank's samples) goes to scratch
+    buffer u % 2 on the compute stream; a copy stream waits for it, copies
+    each other owner's range into that owner's exchange buffer u % 3 (rank + 1
+    first) and runs the one-element all-reduce that orders the ranks; the
+    compute stream meanwhile computes the partial of tensor u + 1, then waits
+    for the exchange of u and runs the fused pass that sums the P slots of
+    its range.  Why the buffers suffice: on the compute stream the partial of
+    u + 2 is queued after the pass of u (also across runs, which is why the
+    numbering continues); a scratch buffer is rewritten by the partial of
+    u + 2, after this rank's pass of u, which waited for the copies of u; an
+    exchange buffer is rewritten by a peer's copies of u + 3, which follow
+    that peer's all-reduce of u + 2, which no rank enters before its partial
+    of u + 2, which follows its pass of u.  Same bits as
+    prune_sample_split_copy."""
+
+    def __init__(self, dist, torch, n_max: int, m: int):
+        self.dist, self.torch, self.m = dist, torch, m
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.bufs = PeerBuffers(dist, 4 * max(n_max, self.world * push_slot(n_max, m, self.world)), 3)
+        self.scratch = [torch.empty(n_max, dtype=torch.float32, device=dev) for _ in range(2)]
+        self.copy_stream = torch.cuda.Stream(device=dev)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.ev_part = [torch.cuda.Event() for _ in range(2)]
+        self.ev_done = [torch.cuda.Event() for _ in range(2)]
+        self.count = 0  # tensors queued so far: buffers keep rotating from one run to the next
+
+    def close(self):
+        self.torch.cuda.synchronize()
+        self.bufs.close()
+
+    def run(self, jobs, S_total: int, s0: int, *, n=2, alpha=0.01, beta=0.99, near_ties=None, **cfg):
+        """jobs: [(w_dev, w_dtype, g_local_dev, g_dtype, out_w, out_mask)], each a
+        tensor's N weights, this rank's samples [s0, s0 + S_local) of all N
+        elements ([S_local, N], contiguous), and the outputs of this rank's
+        group range [e0, e1) = group_shard(N, m, world, rank): out_w holds
+        e1 - e0 FP32 weights, out_mask (e1 - e0) / m mask bytes (views
+        out_w_full[e0:e1] and out_mask_full[e0 // m : e1 // m] of full-size
+        outputs do).  Work is queued on the current stream and the pipeline's
+        copy stream; the call returns without a host wait."""
+        torch, L, m, world, rank = self.torch, tb.lib(), self.m, self.world, self.rank
+        compute = torch.cuda.current_stream()
+        cp = self.copy_stream
+        ev_part, ev_done, u0 = self.ev_part, self.ev_done, self.count
+        plans = []
+        for (w, wdt, g, gdt, ow, om) in jobs:
+            N = w.numel()
+            if N > self.scratch[0].numel():
+                raise ValueError(f"tensor of {N} elements exceeds the pipeline's n_max {self.scratch[0].numel()}")
+            ranges = [group_shard(N, m, world, r) for r in range(world)]
+            plans.append((N, ranges, push_slot(N, m, world)))
+
+        def partial(t):
+            (w, wdt, g, gdt, ow, om), (N, ranges, slot) = jobs[t], plans[t]
+            S_local = g.shape[0] if g is not None else 0
+            c = ema_weights(S_total, alpha, beta)[s0:s0 + S_local].copy()
+            base = self.scratch[(u0 + t) % 2].data_ptr()
+            starts = (C.c_uint64 * (world + 1))(*([e0 for e0, _ in ranges] + [N]))
+            local = (C.c_void_p * world)(*[base + 4 * e0 for e0, _ in ranges])
+            _check(L.tb_fisher_partial_scatter(g.data_ptr() if S_local else None, gdt, S_local, N, N,
+                                               c.ctypes.data if S_local else None, world, starts,
+                                               C.cast(local, C.POINTER(C.c_void_p)), rank, compute.cuda_stream))
+            ev_part[(u0 + t) % 2].record(compute)
+
+        def exchange(t):
+            (N, ranges, slot), k = plans[t], (u0 + t) % 3
+            base = self.scratch[(u0 + t) % 2].data_ptr()
+            cp.wait_event(ev_part[(u0 + t) % 2])
+            for j in range(1, world):
+                r = (rank + j) % world
+                e0, e1 = ranges[r]
+                if e1 > e0:
+                    _check(L.tb_memcpy_d2d(self.bufs.ptrs[k][r] + 4 * rank * slot, base + 4 * e0, 4 * (e1 - e0),
+                                           cp.cuda_stream))
+            with torch.cuda.stream(cp):
+                self.dist.all_reduce(self.flag)
+            ev_done[(u0 + t) % 2].record(cp)
+
+        def consume(t):
+            (w, wdt, g, gdt, ow, om), (N, ranges, slot) = jobs[t], plans[t]
+            k = (u0 + t) % 3
+            compute.wait_event(ev_done[(u0 + t) % 2])
+            e0, e1 = ranges[rank]
+            if e1 <= e0:
+                return
+            base = self.scratch[(u0 + t) % 2].data_ptr()
+            parts = (C.c_void_p * world)(*[(base + 4 * e0) if q == rank else (self.bufs.local[k] + 4 * q * slot)
+                                           for q in range(world)])
+            a = tb.prune_args(weights=w.data_ptr() + e0 * w.element_size(), w_dtype=wdt, grads=None, g_dtype=gdt,
+                              S=0, N=e1 - e0, fisher_steps_in=S_total, alpha=alpha, beta=beta, n=n, m=m,
+                              w_out=ow.data_ptr(), mask_out=om.data_ptr(),
+                              near_ties=near_ties.data_ptr() if near_ties is not None else None, **cfg)
+            _check(L.tb_score_mask_pack_peer(C.byref(a), C.cast(parts, C.POINTER(C.c_void_p)), world,
+                                             compute.cuda_stream))
+
+        if not jobs:
+            return
+        partial(0)
+        for t in range(len(jobs)):
+            exchange(t)
+            if t + 1 < len(jobs):
+                partial(t + 1)
+            consume(t)
+        self.count += len(jobs)
 
 
 # ---- column-block exact OBS --------------------------------------------------

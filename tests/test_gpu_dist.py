@@ -101,6 +101,44 @@ def _worker(rank, world, port_no, tmpdir):
     np.save(os.path.join(tmpdir, f"cp_w{rank}.npy"), cw[e0:e1].cpu().numpy())
     np.save(os.path.join(tmpdir, f"cp_m{rank}.npy"), cm[e0 // 4:e1 // 4].cpu().numpy())
     np.save(os.path.join(tmpdir, f"cp_F{rank}.npy"), cF[e0:e1].cpu().numpy())
+    # the copy exchange pipelined over a sequence of tensors: the same bits as
+    # the one-tensor copy pass for each, over two runs of seven tensors (so the
+    # three exchange buffers rotate across the runs' boundary)
+    sizes = (N, (1 << 18) + 4 * 37, 3 << 16)
+    wts = [wd] + [torch.from_numpy(inp.to_bf16_bits(inp.normal(n_, 0.02, 30 + i)).view(np.int16)).cuda()
+                  for i, n_ in enumerate(sizes[1:])]
+    gts = [gd] + [torch.from_numpy(np.ascontiguousarray(
+        inp.to_bf16_bits(inp.normal((S, n_), 1e-3, 40 + i))[s0:s1]).view(np.int16)).cuda()
+        for i, n_ in enumerate(sizes[1:])]
+    want = []
+    for i, n_ in enumerate(sizes):
+        a0, a1 = td.group_shard(n_, 4, world, rank)
+        ow = torch.zeros(n_, dtype=torch.float32, device="cuda")
+        om = torch.zeros(n_ // 4, dtype=torch.uint8, device="cuda")
+        td.prune_sample_split_copy(dist, torch, bufs, i & 1, scratch, wts[i], tb.BF16, gts[i], tb.BF16, S, s0,
+                                   ow, om, strategy="optimal", redist="proportional", mode="obd")
+        torch.cuda.synchronize()
+        want.append((ow[a0:a1].cpu().numpy(), om[a0 // 4:a1 // 4].cpu().numpy()))
+    assert want[0][0].tobytes() == cw[e0:e1].cpu().numpy().tobytes()
+    pipe = td.CopyExchangePipeline(dist, torch, N, 4)
+    order = (0, 1, 2, 0, 1, 2, 1)
+    runs = []
+    for _ in range(2):
+        jobs = []
+        for i in order:
+            a0, a1 = td.group_shard(sizes[i], 4, world, rank)
+            jobs.append((wts[i], tb.BF16, gts[i], tb.BF16,
+                         torch.full((max(1, a1 - a0),), -1.0, dtype=torch.float32, device="cuda"),
+                         torch.full((max(1, (a1 - a0) // 4),), 7, dtype=torch.uint8, device="cuda")))
+        pipe.run(jobs, S, s0, strategy="optimal", redist="proportional", mode="obd")
+        runs.append(jobs)
+    torch.cuda.synchronize()
+    for jobs in runs:
+        for i, job in zip(order, jobs):
+            got_w, got_m = job[4].cpu().numpy(), job[5].cpu().numpy()
+            assert got_w[:want[i][0].size].tobytes() == want[i][0].tobytes(), f"pipeline weights of tensor {i}"
+            assert got_m[:want[i][1].size].tobytes() == want[i][1].tobytes(), f"pipeline mask of tensor {i}"
+    pipe.close()
     bufs.close()
     dist.barrier(device_ids=[rank])
     dist.destroy_process_group()
