@@ -68,6 +68,9 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
 
 __device__ __forceinline__ void stg_stream(float4* p, float4 v) { __stcs(p, v); }
 
+// Hint: bring the line holding p into L2 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // ---------------------------------------------------------------------------
 // Stage 1 arithmetic (include/tensorbit/core/ehap.hpp)
 // ---------------------------------------------------------------------------
