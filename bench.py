@@ -57,8 +57,9 @@ METRIC = "2:4 score+mask+pack Gparams/s at 1/2/4/8 B200; % HBM roofline; OBS TFL
 
 # SHA-256 over the .tb images (header + FP32 weights + mask bytes) of the 14
 # distinct tensors of the headline pass (layer sets A and B, 7 matrices each),
-# as one B200 produced them; every N must reproduce it.
-EXPECTED_7B_DIGEST = None
+# as B200 runs on one, two and eight GPUs produced them (identical); every N
+# must reproduce it.
+EXPECTED_7B_DIGEST = "af8e0831d1d033af326b621e7b01e62279c5b887ad351ad48cc52c33f19ce492"
 
 
 class Workload:
@@ -109,6 +110,11 @@ def parse():
     ap.add_argument("--replicas", action="store_true",
                     help="each rank prunes its own whole model (weak scaling) instead of a share of one")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-even", action="store_true",
+                    help="e2e: split the layer evenly instead of by each rank's measured host-link bandwidth")
+    ap.add_argument("--no-numa-bind", action="store_true",
+                    help="e2e: leave the process's CPU affinity alone (by default each rank runs, and allocates "
+                         "its pinned buffers, on the CPUs of its GPU's NUMA node during the e2e leg)")
     ap.add_argument("--sweep-steps", type=int, default=2, help="timed steps per pattern of the 70B sweep")
     ap.add_argument("--split-steps", type=int, default=3, help="timed steps of each sample-split variant")
     for k in ("e2e", "cpu", "obs", "block-obs", "ties", "layer", "sweep", "split", "digest", "verify", "tbprune"):
@@ -522,13 +528,15 @@ def digest_check(torch, tb, ranks, wl, sets, plan):
     bad_timed = int(ranks.sum([float(bad_timed)])[0])
     bad_unsharded = int(ranks.sum([float(bad_unsharded)])[0])
     dig = h.hexdigest() if ranks.rank == 0 else None
+    # the pinned digest is that of the full 7B workload (both layer sets, all 7 matrices)
+    expected = EXPECTED_7B_DIGEST if (wl is W7B and wl.layer == LAYER_7B and len(sets) == 2) else None
+    match = (dig == expected) if (expected and dig) else None
+    match_all = ranks.sum([0.0 if match is False else 1.0])[0] == ranks.world
     return {"tb_images": 2 * len(sets[0]) if len(sets) > 1 else len(sets[0]),
             "sha256": dig, "assembled_from_ranks": ranks.world,
             "differs_from_one_rank_pass": bad_unsharded, "timed_outputs_differ": bad_timed,
-            "expected_sha256": EXPECTED_7B_DIGEST,
-            "matches_expected": (dig == EXPECTED_7B_DIGEST) if (EXPECTED_7B_DIGEST and dig) else None,
-            "ok": bad_unsharded == 0 and bad_timed == 0 and (EXPECTED_7B_DIGEST is None or dig is None
-                                                             or dig == EXPECTED_7B_DIGEST)}
+            "expected_sha256": expected, "matches_expected": match,
+            "ok": bad_unsharded == 0 and bad_timed == 0 and match_all}
 
 
 # ---------------------------------------------------------------------------
@@ -1096,13 +1104,54 @@ def pcie_peak(torch, ranks, nbytes=1 << 30, reps=5):
     return out
 
 
+def _cpulist(text):
+    cpus = set()
+    for part in text.strip().split(","):
+        if part:
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+    return cpus
+
+
+def gpu_numa_cpus(torch, local):
+    """(NUMA node, CPUs of that node usable by this process) of the PCIe slot of
+    GPU `local`, from sysfs; None where the platform does not say."""
+    try:
+        p = torch.cuda.get_device_properties(local)
+        addr = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        node = int(open(f"/sys/bus/pci/devices/{addr}/numa_node").read())
+        if node < 0:
+            return None
+        cpus = _cpulist(open(f"/sys/devices/system/node/node{node}/cpulist").read()) & os.sched_getaffinity(0)
+        return (node, cpus) if cpus else None
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def run_e2e(torch, tb, ranks, args):
     """Same metric through tb_score_mask_pack_host with pinned host buffers: every
     step copies that step's inputs host->device and the results back inside the
     timed region.  One step = one decoder layer (7 matrices, 218,103,808
-    params), split over the ranks like the headline pass."""
+    params), split over the ranks like the headline pass but in proportion to
+    each rank's measured pinned host-to-device bandwidth (the GPUs' host links
+    differ where several share a PCIe switch or a socket).  Each rank runs the
+    leg on the CPUs of its GPU's NUMA node, so its pinned buffers are allocated
+    in that node's memory; the previous affinity is restored afterwards."""
     import tbdist as td
     wl = W7B
+    old_aff = os.sched_getaffinity(0)
+    numa = None if args.no_numa_bind else gpu_numa_cpus(torch, ranks.local)
+    if numa:
+        os.sched_setaffinity(0, numa[1])
+    try:
+        return _run_e2e(torch, tb, ranks, args, td, wl, numa)
+    finally:
+        os.sched_setaffinity(0, old_aff)
+
+
+def _run_e2e(torch, tb, ranks, args, td, wl, numa):
+    peak = ranks.gather(pcie_peak(torch, ranks))
+    even = args.e2e_even or args.replicas or ranks.world == 1
     S = wl.S
     nmax = max(r * c for _, r, c in wl.layer)
     gen = torch.Generator(device=ranks.dev).manual_seed(99)
@@ -1117,7 +1166,9 @@ def run_e2e(torch, tb, ranks, args):
     sizes = [r * c for _, r, c in wl.layer]
     calls = []
     h2d = d2h = 0
-    for t, e0, e1 in td.model_shard(sizes, 4, 1 if args.replicas else ranks.world, 0 if args.replicas else ranks.rank):
+    weights = None if even else [p[0] for p in peak]
+    for t, e0, e1 in td.model_shard(sizes, 4, 1 if args.replicas else ranks.world, 0 if args.replicas else ranks.rank,
+                                    weights=weights):
         n = e1 - e0  # every matrix reads the leading columns of the shared pinned buffers
         calls.append(tb.prune_args(weights=hw.data_ptr() + 2 * e0, w_dtype=tb.BF16, grads=hg.data_ptr() + 2 * e0,
                                    g_dtype=tb.BF16, S=S, N=n, g_stride=nmax, mode=wl.mode, strategy=wl.strategy,
@@ -1135,9 +1186,8 @@ def run_e2e(torch, tb, ranks, args):
     for _ in range(args.e2e_steps):
         layer()
     el = time.perf_counter() - t0
-    per = ranks.gather([el, h2d, d2h])
+    per = ranks.gather([el, h2d, d2h, numa[0] if numa else -1])
     del hw, hg, hwo, hm
-    peak = ranks.gather(pcie_peak(torch, ranks))
     el = max(r[0] for r in per)
     params = sum(sizes) * (ranks.world if args.replicas else 1)
     return {"value": round(params * args.e2e_steps / el / 1e9, 4), "unit": "Gparams/s",
@@ -1145,6 +1195,10 @@ def run_e2e(torch, tb, ranks, args):
             "steps": args.e2e_steps, "s_per_step": round(el / args.e2e_steps, 4),
             "step": "one decoder layer (7 matrices) via tb_score_mask_pack_host from pinned host memory, split "
                     "over the ranks like the headline pass",
+            "split": ("even" if even else "in proportion to each rank's pinned H2D copy peak (tbdist.model_shard "
+                      "weights)"),
+            "numa_node_per_rank": [int(r[3]) if r[3] >= 0 else None for r in per],
+            "params_per_rank": [int(r[1] // (2 + 2 * wl.S)) for r in per],
             "h2d_gbs_per_rank": [round(r[1] * args.e2e_steps / r[0] / 1e9, 1) for r in per],
             "pinned_copy_peak_gbs_per_rank": {"h2d": [round(p[0], 1) for p in peak],
                                               "d2h": [round(p[1], 1) for p in peak]},

@@ -61,7 +61,8 @@ def group_shard(N: int, m: int, world: int, rank: int) -> tuple[int, int]:
     return e0, e1
 
 
-def model_shard(sizes: list[int], m: int, world: int, rank: int) -> list[tuple[int, int, int]]:
+def model_shard(sizes: list[int], m: int, world: int, rank: int,
+                weights: list[float] | None = None) -> list[tuple[int, int, int]]:
     """This rank's share of a whole model's pass.  The tensors (element counts
     `sizes`, each a multiple of M) are laid end to end as one range of N:M
     groups and cut into `world` contiguous parts of equal size, each cut moved
@@ -70,7 +71,16 @@ def model_shard(sizes: list[int], m: int, world: int, rank: int) -> list[tuple[i
     Returns [(tensor index, e0, e1)]: element ranges inside the tensors, in
     model order.  Ranks differ by at most one alignment unit per cut, however
     unequal the tensors are; whole tensors stay whole unless a cut falls inside
-    one."""
+    one.  With `weights` (one positive number per rank, the same list on every
+    rank) part r is sized in proportion to weights[r] instead, e.g. to each
+    rank's measured host-link bandwidth when the inputs stream from host
+    memory."""
+    if weights is not None:
+        if len(weights) != world or any(not (x > 0) for x in weights):
+            raise ValueError("weights: one positive value per rank")
+        acc = [0.0]
+        for x in weights:
+            acc.append(acc[-1] + float(x))
     for t, n in enumerate(sizes):
         if n % m:
             raise ValueError(f"tensor {t}: numel {n} not divisible by M={m}")
@@ -85,7 +95,7 @@ def model_shard(sizes: list[int], m: int, world: int, rank: int) -> list[tuple[i
             return 0, 0
         if k >= world:
             return len(sizes), 0
-        pos = total * k // world
+        pos = total * k // world if weights is None else min(total, int(total * (acc[k] / acc[-1])))
         t = bisect.bisect_right(starts, pos) - 1
         return t, (pos - starts[t]) // unit * unit
 

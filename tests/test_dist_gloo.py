@@ -63,6 +63,31 @@ def test_model_shards_cover_align_and_balance(sizes, m, world):
     assert all(abs(p - total / world) < unit + 1 for p in per_rank), per_rank
 
 
+@pytest.mark.parametrize("weights", [[22.0, 22.1, 32.5, 32.4], [1.0, 3.0], [5.0, 1.0, 1.0, 1.0, 1.0, 1.0, 1.0, 2.0]])
+def test_weighted_model_shards_cover_and_follow_weights(weights):
+    sizes = LAYER_7B * 3 + [4096 * 16 + 64]
+    world, m = len(weights), 4
+    unit = 16
+    total = sum(sizes)
+    covered = {t: [] for t in range(len(sizes))}
+    for r in range(world):
+        pieces = tbdist.model_shard(sizes, m, world, r, weights=weights)
+        for t, e0, e1 in pieces:
+            assert e0 % unit == 0 and (e1 == sizes[t] or e1 % unit == 0)
+            covered[t].append((e0, e1))
+        share = total * weights[r] / sum(weights)
+        assert abs(sum(e1 - e0 for _, e0, e1 in pieces) - share) < 2 * unit + 2
+    for t, ranges in covered.items():
+        ranges.sort()
+        assert ranges[0][0] == 0 and ranges[-1][1] == sizes[t]
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+    # equal weights give the unweighted cut
+    for r in range(world):
+        assert tbdist.model_shard(sizes, m, world, r, weights=[2.0] * world) == tbdist.model_shard(sizes, m, world, r)
+    with pytest.raises(ValueError):
+        tbdist.model_shard(sizes, m, world, 0, weights=[1.0] * (world + 1))
+
+
 def test_model_shards_keep_whole_tensors_when_layers_divide():
     # 32 equal layers over 1/2/4/8 ranks: every cut lands on a layer boundary
     for world in (1, 2, 4, 8):
