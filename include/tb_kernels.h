@@ -308,11 +308,21 @@ int tb_score_mask_pack(const tb_prune_args* args, void* stream);
  * scores_out (now the importance CORING ranked).  *threshold_out (0 when
  * everything is kept), *ehap_pruned_out (weights the threshold zeroed) and
  * *coring_pruned_out (the analytic (N/M)*(M-N) of coring.hpp:192,222) are
- * host values, any may be NULL; synchronises the stream.  Scratch: about
+ * host values, any may be NULL; synchronises the stream when threshold_out or
+ * ehap_pruned_out is given.  Scratch: about
  * 16 KB, stream-ordered from the library's per-device pool.  Sparsity outside (0, 1) -> TB_ERR_CONFIG before any
  * N:M check, as the reference's EHAP stage fails first. */
 int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* threshold_out,
                          uint64_t* ehap_pruned_out, uint64_t* coring_pruned_out, void* stream);
+
+/* tb_prune_one_shot_nm without the host wait: the threshold and the EHAP count
+ * are copied, in stream order, to threshold_dst / ehap_pruned_dst (device
+ * memory or pinned host memory, either may be NULL) and are valid once the
+ * stream reaches that point, so a caller can queue many tensors and read their
+ * counts after one synchronisation.  *coring_pruned_out is a host value as
+ * above.  Outputs, errors and scratch as tb_prune_one_shot_nm. */
+int tb_prune_one_shot_nm_async(const tb_prune_args* args, float sparsity, float* threshold_dst,
+                               uint64_t* ehap_pruned_dst, uint64_t* coring_pruned_out, void* stream);
 
 /* Sample split, producer side: this rank's partial Fisher
  *   F_part[i] = sum over its S samples of weights[s] * g_s[i]^2

@@ -840,8 +840,11 @@ int tb_score_mask_pack_peer(const tb_prune_args* args, const float* const* parti
     return launch_fused(p, args->nm_m, static_cast<cudaStream_t>(stream));
 }
 
-int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* threshold_out,
-                         uint64_t* ehap_pruned_out, uint64_t* coring_pruned_out, void* stream) {
+// The one-shot sequence; the threshold and EHAP count go to host values
+// (thr_host / pruned_host, with a host wait when either is asked for) and/or
+// are copied, stream-ordered, to device-accessible thr_dst / pruned_dst.
+static int one_shot(const tb_prune_args* args, float sparsity, float* thr_host, uint64_t* pruned_host, float* thr_dst,
+             uint64_t* pruned_dst, uint64_t* coring_pruned_out, void* stream) {
     if (!args) return fail(TB_ERR_ARG, "null args");
     // EHAP's checks come first, as in the reference sequence (the global select
     // runs before CORING sees the tensor).
@@ -889,11 +892,33 @@ int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* thres
         b.thr_pruned = &sel->pruned;
     }
     rc = launch_fused(b, m, st);
-    if (rc == TB_OK) rc = threshold_finish(N, keep, sel, threshold_out, ehap_pruned_out, st);
+    if (rc == TB_OK && (thr_dst || pruned_dst)) {
+        if (!sel) {  // everything kept: threshold 0, nothing pruned
+            if ((rc = scratch_alloc(reinterpret_cast<void**>(&sel), sizeof(SelectState), st))) return rc;
+            rc = threshold_clear(sel, st);
+        }
+        cudaError_t e = cudaSuccess;
+        if (rc == TB_OK && thr_dst)
+            e = cudaMemcpyAsync(thr_dst, &sel->threshold, sizeof(float), cudaMemcpyDefault, st);
+        if (rc == TB_OK && e == cudaSuccess && pruned_dst)
+            e = cudaMemcpyAsync(pruned_dst, &sel->pruned, sizeof(uint64_t), cudaMemcpyDefault, st);
+        if (rc == TB_OK && e != cudaSuccess) rc = cuda_fail(e, "tb_prune_one_shot_nm_async result copy");
+    }
+    if (rc == TB_OK) rc = threshold_finish(N, keep, sel, thr_host, pruned_host, st);
     scratch_free(sel, st);
     if (rc == TB_OK && coring_pruned_out)
         *coring_pruned_out = static_cast<uint64_t>(N / m) * static_cast<uint64_t>(m - args->nm_n);  // coring.hpp:192,222
     return rc;
+}
+
+int tb_prune_one_shot_nm(const tb_prune_args* args, float sparsity, float* threshold_out,
+                         uint64_t* ehap_pruned_out, uint64_t* coring_pruned_out, void* stream) {
+    return one_shot(args, sparsity, threshold_out, ehap_pruned_out, nullptr, nullptr, coring_pruned_out, stream);
+}
+
+int tb_prune_one_shot_nm_async(const tb_prune_args* args, float sparsity, float* threshold_dst,
+                               uint64_t* ehap_pruned_dst, uint64_t* coring_pruned_out, void* stream) {
+    return one_shot(args, sparsity, nullptr, nullptr, threshold_dst, ehap_pruned_dst, coring_pruned_out, stream);
 }
 
 int tb_score_mask_pack_host(const tb_prune_args* a) {

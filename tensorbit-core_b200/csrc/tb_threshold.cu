@@ -6,10 +6,10 @@
 // statistic, so any exact selection returns the same value; ties at it are all
 // kept by the >= comparison.  Here the FP32 scores are mapped to order-
 // preserving 32-bit keys and the key of rank t = N - keep is found digit by
-// digit (11 + 11 + 10 bits): three histogram passes over the scores, each
-// followed by a one-block scan that picks the digit and narrows the rank.
-// A final pass writes the 1-byte-per-element mask (ehap.hpp:320-327) and
-// counts the pruned elements.
+// digit (11 + 11 + 10 bits): three histogram passes over the scores; the last
+// block of each pass to finish (a ticket counter, no waiting) scans the
+// histogram, picks the digit and narrows the rank.  A final pass writes the
+// 1-byte-per-element mask (ehap.hpp:320-327) and counts the pruned elements.
 //
 // Scratch (device memory beyond the inputs and outputs): one 2048-bin u64
 // histogram plus a small state block (struct SelectState, about 16.4 KB).
@@ -31,6 +31,50 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 }
 __device__ __forceinline__ float key_float(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// Run by one whole block of kThreads once a pass's histogram is complete: find
+// the digit whose cumulative count covers the target rank, extend the prefix,
+// narrow the rank, and clear the histogram and the ticket for the next pass
+// (the last pass also sets the threshold).  The histogram is read from L2
+// (it was built by atomics).
+__device__ void scan_digit(SelectState* __restrict__ st, int pass) {
+    __shared__ unsigned long long part[kThreads];
+    const int t = threadIdx.x;
+    const int bins = pass == 2 ? 1024 : 2048;
+    const int per = bins / kThreads;
+    unsigned long long local = 0;
+    for (int j = 0; j < per; ++j) local += __ldcg(&st->hist[t * per + j]);
+    part[t] = local;
+    __syncthreads();
+    // inclusive scan over the kThreads partial sums (Hillis-Steele)
+    for (int off = 1; off < kThreads; off <<= 1) {
+        const unsigned long long v = t >= off ? part[t - off] : 0ull;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    const unsigned long long target = st->target;
+    const unsigned long long before = t ? part[t - 1] : 0ull;
+    if (target >= before && target < part[t]) {
+        unsigned long long c = before;
+        for (int j = 0; j < per; ++j) {
+            const unsigned long long h = __ldcg(&st->hist[t * per + j]);
+            if (target < c + h) {
+                const int digit = t * per + j;
+                const int width = pass == 2 ? 10 : 11;
+                const uint32_t prefix = (st->prefix << width) | static_cast<uint32_t>(digit);
+                st->prefix = prefix;
+                st->target = target - c;
+                if (pass == 2) st->threshold = key_float(prefix);
+                break;
+            }
+            c += h;
+        }
+    }
+    __syncthreads();
+    for (int i = t; i < kBins; i += kThreads) st->hist[i] = 0;
+    if (t == 0) st->done = 0;
 }
 
 // Histogram of digit `(key >> shift) & (bins-1)` over keys whose bits above
@@ -66,45 +110,16 @@ __global__ void __launch_bounds__(kThreads) radix_hist_kernel(const float* __res
     __syncthreads();
     for (int i = threadIdx.x; i < kBins; i += kThreads)
         if (sh[i]) atomicAdd(&st->hist[i], static_cast<unsigned long long>(sh[i]));
-}
-
-// One block: find the digit whose cumulative count covers the target rank,
-// extend the prefix, narrow the rank, and clear the histogram for the next pass.
-__global__ void __launch_bounds__(1024) radix_scan_kernel(SelectState* __restrict__ st, int pass) {
-    __shared__ unsigned long long part[1024];
-    const int t = threadIdx.x;
-    const int bins = pass == 2 ? 1024 : 2048;
-    const int per = bins / 1024;
-    unsigned long long local = 0;
-    for (int j = 0; j < per; ++j) local += st->hist[t * per + j];
-    part[t] = local;
+    // The last block to finish scans the histogram: every block's additions
+    // are made visible (fence) before it takes its ticket.
+    __threadfence();
     __syncthreads();
-    // inclusive scan over 1024 partial sums (Hillis-Steele)
-    for (int off = 1; off < 1024; off <<= 1) {
-        unsigned long long v = t >= off ? part[t - off] : 0ull;
-        __syncthreads();
-        part[t] += v;
-        __syncthreads();
-    }
-    const unsigned long long target = st->target;
-    const unsigned long long before = t ? part[t - 1] : 0ull;
-    if (target >= before && target < part[t]) {
-        unsigned long long c = before;
-        for (int j = 0; j < per; ++j) {
-            const unsigned long long h = st->hist[t * per + j];
-            if (target < c + h) {
-                const int digit = t * per + j;
-                const int width = pass == 2 ? 10 : 11;
-                st->prefix = (st->prefix << width) | static_cast<uint32_t>(digit);
-                st->target = target - c;
-                break;
-            }
-            c += h;
-        }
-    }
+    __shared__ unsigned int ticket;
+    if (threadIdx.x == 0) ticket = atomicAdd(&st->done, 1u);
     __syncthreads();
-    for (int i = t; i < kBins; i += 1024) st->hist[i] = 0;
-    if (pass == 2 && t == 0) st->threshold = key_float(st->prefix);
+    if (ticket != gridDim.x - 1) return;
+    __threadfence();
+    scan_digit(st, pass);
 }
 
 // mask[i] = s[i] >= thr (1 byte per element); counts elements not kept.
@@ -129,6 +144,7 @@ __global__ void init_state_kernel(SelectState* st, unsigned long long target) {
         st->target = target;
         st->pruned = 0;
         st->threshold = 0.0f;
+        st->done = 0;
     }
 }
 
@@ -163,10 +179,7 @@ int threshold_launch(const float* scores, size_t N, size_t keep, uint8_t* mask_o
     }
     init_state_kernel<<<1, 1024, 0, stream>>>(st, static_cast<unsigned long long>(N - keep));
     const unsigned grid = grid_for(N);
-    for (int pass = 0; pass < 3; ++pass) {
-        radix_hist_kernel<<<grid, kThreads, 0, stream>>>(scores, N, st, pass);
-        radix_scan_kernel<<<1, 1024, 0, stream>>>(st, pass);
-    }
+    for (int pass = 0; pass < 3; ++pass) radix_hist_kernel<<<grid, kThreads, 0, stream>>>(scores, N, st, pass);
     threshold_mask_kernel<<<grid, kThreads, 0, stream>>>(scores, N, mask_out, st);
     return check_launch("threshold select");
 }
@@ -174,15 +187,18 @@ int threshold_launch(const float* scores, size_t N, size_t keep, uint8_t* mask_o
 int threshold_digits(const float* scores, size_t N, size_t keep, SelectState* st, cudaStream_t stream) {
     init_state_kernel<<<1, 1024, 0, stream>>>(st, static_cast<unsigned long long>(N - keep));
     const unsigned grid = grid_for(N);
-    for (int pass = 0; pass < 3; ++pass) {
-        radix_hist_kernel<<<grid, kThreads, 0, stream>>>(scores, N, st, pass);
-        radix_scan_kernel<<<1, 1024, 0, stream>>>(st, pass);
-    }
+    for (int pass = 0; pass < 3; ++pass) radix_hist_kernel<<<grid, kThreads, 0, stream>>>(scores, N, st, pass);
     return check_launch("threshold digits");
+}
+
+int threshold_clear(SelectState* st, cudaStream_t stream) {
+    init_state_kernel<<<1, 1024, 0, stream>>>(st, 0ull);
+    return check_launch("threshold clear");
 }
 
 int threshold_finish(size_t N, size_t keep, const SelectState* st, float* thr_out, uint64_t* pruned_out,
                      cudaStream_t stream) {
+    if (!thr_out && !pruned_out) return TB_OK;  // nothing to read back: no host wait
     float thr = 0.0f;
     unsigned long long pruned = 0;
     if (keep < N) {

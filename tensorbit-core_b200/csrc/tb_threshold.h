@@ -14,6 +14,7 @@ struct SelectState {
     unsigned long long pruned;   // elements below the threshold
     uint32_t prefix;             // key digits fixed so far
     float threshold;
+    unsigned int done;           // histogram blocks finished in the current pass (the last one scans)
 };
 
 // keep = (size_t)(sparsity * (float)N), at least 1 (ehap.hpp:301-307);
@@ -26,8 +27,12 @@ int threshold_launch(const float* scores, size_t N, size_t keep, uint8_t* mask_o
 // threshold afterwards and st->pruned is zero, for a later pass that applies
 // the threshold itself and counts what it drops into st->pruned.
 int threshold_digits(const float* scores, size_t N, size_t keep, SelectState* st, cudaStream_t stream);
-// Reads threshold and pruned count back (synchronises `stream`).
+// Reads threshold and pruned count back (synchronises `stream`); with both
+// outputs null it does nothing.
 int threshold_finish(size_t N, size_t keep, const SelectState* st, float* thr_out, uint64_t* pruned_out,
                      cudaStream_t stream);
+// Enqueues zeroing of a state whose threshold and count are to be read
+// without a selection (keep >= N: nothing is pruned).
+int threshold_clear(SelectState* st, cudaStream_t stream);
 
 }  // namespace tb

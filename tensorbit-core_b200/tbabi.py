@@ -137,6 +137,7 @@ def lib() -> C.CDLL:
                                            vp], i32),
             "tb_prune_one_shot_nm": ([C.POINTER(PruneArgs), f32, C.POINTER(C.c_float), C.POINTER(C.c_uint64),
                                       C.POINTER(C.c_uint64), vp], i32),
+            "tb_prune_one_shot_nm_async": ([C.POINTER(PruneArgs), f32, vp, vp, C.POINTER(C.c_uint64), vp], i32),
             "tb_score_mask_pack_peer": ([C.POINTER(PruneArgs), C.POINTER(vp), i32, vp], i32),
             "tb_score_mask_pack_host": ([C.POINTER(PruneArgs)], i32),
             "tb_score_mask_pack_host_noalloc": ([C.POINTER(PruneArgs)], i32),

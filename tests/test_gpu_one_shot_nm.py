@@ -109,3 +109,42 @@ def test_one_shot_nm_checks_sparsity_before_nm(cuda, tblib):
         assert rc == tblib.TB_ERR_CONFIG
     assert one_shot(cuda, tblib, w, None, use_fisher=False, n=4, m=4)[0] == tblib.TB_ERR_CONFIG  # N:M 4:4
     assert one_shot(cuda, tblib, np.zeros(66, np.float32), None, use_fisher=False)[0] == tblib.TB_ERR_SHAPE
+
+
+@pytest.mark.parametrize("N,sparsity", [(200_000, 0.5), (200_000, 0.9), (3 << 20, 0.1)])
+def test_one_shot_nm_async_equals_sync(cuda, tblib, N, sparsity):
+    """The async entry writes the same tensors as the synchronous one and its
+    stream-ordered threshold / EHAP count (one to device memory, one to pinned
+    host memory) equal the synchronous host values."""
+    torch, tb = cuda, tblib
+    w = inputs.normal(N, 0.02, 90)
+    g = inputs.normal((2, N), 1e-3, 91)
+    wd = torch.from_numpy(w).cuda()
+    gd = torch.from_numpy(g).cuda()
+    outs = []
+    for variant in ("sync", "async"):
+        wo = torch.full((N,), float("nan"), device="cuda")
+        mk = torch.full((N // 4,), 0xAA, dtype=torch.uint8, device="cuda")
+        F = torch.full((N,), float("nan"), device="cuda")
+        s = torch.full((N,), float("nan"), device="cuda")
+        a = tb.prune_args(weights=wd.data_ptr(), w_dtype=tb.F32, grads=gd.data_ptr(), g_dtype=tb.F32, S=2, N=N,
+                          mode="obd", strategy="topn", redist="proportional", w_out=wo.data_ptr(),
+                          mask_out=mk.data_ptr(), fisher_out=F.data_ptr(), scores_out=s.data_ptr())
+        cp = C.c_uint64()
+        if variant == "sync":
+            thr, ep = C.c_float(), C.c_uint64()
+            rc = tb.lib().tb_prune_one_shot_nm(C.byref(a), sparsity, C.byref(thr), C.byref(ep), C.byref(cp), None)
+            counts = (thr.value, ep.value)
+        else:
+            dthr = torch.full((1,), float("nan"), device="cuda")
+            hcnt = torch.full((1,), -1, dtype=torch.int64).pin_memory()  # pinned host destination
+            rc = tb.lib().tb_prune_one_shot_nm_async(C.byref(a), sparsity, dthr.data_ptr(), hcnt.data_ptr(),
+                                                     C.byref(cp), None)
+            torch.cuda.synchronize()
+            counts = (float(dthr.item()), int(hcnt.item()))
+        assert rc == 0, tb.lib().tb_last_error()
+        torch.cuda.synchronize()
+        outs.append((wo.cpu().numpy().tobytes(), mk.cpu().numpy().tobytes(), F.cpu().numpy().tobytes(),
+                     s.cpu().numpy().tobytes(), counts, cp.value))
+    assert outs[0] == outs[1]
+    assert outs[0][4][1] > 0
