@@ -1288,7 +1288,7 @@ def sparsegpt_flops(d, r, n):
     return 2 * n * d * d + d ** 3 // 3 + 2 * d ** 3 // 3 + d ** 3 // 3 + r * d * d + r * d * 128
 
 
-def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1683.6):
+def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1669.8):
     """Column-block exact OBS of one down_proj on tensor cores.  With several ranks the tokens are
     split for X^T X (one NCCL all-reduce of H) and the rows of W for the sweep;
     the factorisation of H is replicated on every rank.  Time per pass is the
