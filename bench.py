@@ -1311,16 +1311,17 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1669.8):
     mask = torch.empty(max(1, (r1 - r0) * D // 4), dtype=torch.uint8, device=dev)
     L = tb.lib()
     sptr = torch.cuda.current_stream().cuda_stream
-    ms, phases = [], []
+    ms, phases, ar_ms, h_ms = [], [], [], []
     for k in range(steps + 1):  # the first pass warms up (workspace, module load)
         W.copy_(W0)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ear = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
         e0.record()
         if world > 1:
-            td.obs_hessian_token_split(dist, torch, xt, D, NT, H)
+            td.obs_hessian_token_split(dist, torch, xt, D, NT, H, events=ear)
             td.prune_obs_row_split(dist, torch, W, H, mask)
         else:
             tb.check(L.tb_obs_hessian(xt.data_ptr(), D, NT, H.data_ptr(), sptr))
@@ -1329,6 +1330,9 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1669.8):
         torch.cuda.synchronize()
         if k:
             ms.append(e0.elapsed_time(e1))
+            if world > 1:
+                h_ms.append(e0.elapsed_time(ear[0]))
+                ar_ms.append(ear[0].elapsed_time(ear[1]))
             ph = (C.c_float * 4)()
             tb.check(L.tb_obs_sparsegpt_phase_times(ph, 4))
             phases.append(list(ph))
@@ -1338,6 +1342,13 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1669.8):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t = float(t.item())
+    split = None
+    if world > 1:  # rank 0's share of X^T X and the all-reduce of the d x d FP32 H (822 MB at d = 14336)
+        ar = statistics.median(ar_ms)
+        split = {"xtx_ms_rank0": round(statistics.median(h_ms), 3), "allreduce_ms_rank0": round(ar, 3),
+                 "allreduce_bytes": D * D * 4, "allreduce_algbw_gbs_rank0": round(D * D * 4 / (ar / 1e3) / 1e9, 1),
+                 "note": "the factorisation (chain_phase_ms_rank0) runs replicated on every rank after the "
+                         "all-reduce; only the sweep's rows are split"}
     f = obs_flops(D, R, NT)
     fs = sparsegpt_flops(D, R, NT)
     tflops = f / (t / 1e3) / 1e12
@@ -1353,7 +1364,8 @@ def run_obs(torch, tb, dev, steps, shape=None, dist=None, bf16_peak=1669.8):
                             f"rows split for the sweep" if world > 1 else "1 GPU"),
             "tensor_peak_bf16_tflops": bf16_peak,
             "frac_of_bf16_peak": round(tflops / bf16_peak, 4),
-            "frac_of_3xtf32_ceiling": round(tflops / (bf16_peak / 2 / 3), 4)}
+            "frac_of_3xtf32_ceiling": round(tflops / (bf16_peak / 2 / 3), 4),
+            "token_split": split}
 
 
 # ---------------------------------------------------------------------------

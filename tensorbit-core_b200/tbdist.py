@@ -537,19 +537,25 @@ def token_shard(n: int, world: int, rank: int) -> tuple[int, int]:
     return units * rank // world * OBS_TOKEN_UNIT, units * (rank + 1) // world * OBS_TOKEN_UNIT
 
 
-def obs_hessian_token_split(dist, torch, xt_local_dev, d: int, n_total: int, H) -> None:
+def obs_hessian_token_split(dist, torch, xt_local_dev, d: int, n_total: int, H, events=None) -> None:
     """H = X^T X / n_total over all ranks' tokens.  xt_local_dev is this rank's
     tokens as X^T (BF16 [d][n_local], n_local a multiple of 64, may be None
     for no tokens); H is a d x d FP32 device tensor, overwritten.  The partial
     is formed with scale 1/n_total, so the all-reduced sum needs no rescaling;
-    tiles above the diagonal stay zero on every rank and sum to zero."""
+    tiles above the diagonal stay zero on every rank and sum to zero.
+    `events` (two CUDA events, optional) are recorded on the current stream
+    just before and after the all-reduce, for timing it."""
     stream = torch.cuda.current_stream().cuda_stream
     H.zero_()
     n_local = xt_local_dev.shape[1] if xt_local_dev is not None else 0
     if n_local:
         _check(tb.lib().tb_obs_hessian_scaled(xt_local_dev.data_ptr(), d, n_local, 1.0 / n_total, H.data_ptr(),
                                               stream))
+    if events:
+        events[0].record()
     dist.all_reduce(H)
+    if events:
+        events[1].record()
 
 
 def prune_obs_row_split(dist, torch, W_local, H, mask_local, *, damp_frac=0.01, n_keep=2, m=4) -> None:
